@@ -1,0 +1,177 @@
+/*
+ * smaq_b200 -- C ABI of the B200-native SMAQ compressed-KV hot path.
+ *
+ * Every entry point takes plain device pointers, sizes, strides and a
+ * cudaStream_t (passed as void*), enqueues work on that stream without a host
+ * synchronisation, and returns an int status (SMAQ_OK == 0).  A non-zero
+ * status leaves a message for smaq_last_error() (thread-local).  Nothing here
+ * allocates device memory except where a function says so; scratch space is
+ * caller-provided ("workspace").
+ *
+ * Reference interfaces replaced (gauravsaini/smaq, file:line):
+ *   smaq_quantize_keys_scalar  <- SMAQQuantizer.quantize          smaq/quantizer.py:138-145
+ *                                 (+ _pack_indices                smaq/quantizer.py:34-46)
+ *   smaq_quantize_values       <- quantize_values                 smaq/kv_cache.py:50-91
+ *   smaq_quantize_keys_bvq     <- SMAQBlockVQ.quantize            smaq/block_vq.py:216-244
+ *   smaq_append                <- CompressedKVStore.append_chunk  smaq/store.py:83-95
+ *                                 (keys + values in one pass, written straight into the
+ *                                  store's preallocated / paged rows)
+ *   smaq_decode                <- compute_hybrid_attention        smaq/score.py:23-72
+ *                                 (+ _quantized_scores / _exact_scores / _apply_weights
+ *                                  smaq/score.py:75-124, SMAQQuantizer.attention_score
+ *                                  smaq/quantizer.py:154-184, SMAQBlockVQ.attention_score
+ *                                  smaq/block_vq.py:273-297, dequantize_values
+ *                                  smaq/kv_cache.py:94-103)
+ *   smaq_merge_partials        <- (new) log-sum-exp combine of sequence-split partials;
+ *                                 the reference has no multi-GPU path.
+ *
+ * Store layout ("rows").  All compressed streams of a layer share one row
+ * index.  The store is [n_pages, n_kv_heads, page_size] rows; row r of a
+ * stream lives at base + r * row_bytes.  Token t of a chunk lands in slot
+ *   s = slots ? slots[t] : slot_offset + t,   page = s / page_size,
+ *   row = (page * n_kv_heads + h) * page_size + s % page_size.
+ * A contiguous per-head store [n_kv_heads, capacity] is page_size = capacity
+ * with one page.  Decode reads token t of sequence b from
+ *   page = block_table ? block_table[b * bt_stride + t / page_size] : b.
+ */
+#ifndef SMAQ_B200_H_
+#define SMAQ_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SMAQ_ABI_VERSION 1
+
+/* element types */
+enum { SMAQ_F32 = 0, SMAQ_BF16 = 1, SMAQ_F16 = 2 };
+/* key formats */
+enum { SMAQ_KEYS_NONE = 0, SMAQ_KEYS_SCALAR = 1, SMAQ_KEYS_BVQ = 2 };
+/* status codes */
+enum {
+  SMAQ_OK = 0,
+  SMAQ_ERR_INVALID = 1,      /* bad pointer / shape / stride / alignment */
+  SMAQ_ERR_UNSUPPORTED = 2,  /* valid request outside the compiled configurations */
+  SMAQ_ERR_CUDA = 3,         /* a CUDA runtime call failed */
+  SMAQ_ERR_WORKSPACE = 4,    /* workspace too small */
+  SMAQ_ERR_DEVICE = 5        /* the device reported an error word */
+};
+
+int smaq_abi_version(void);
+const char* smaq_last_error(void);
+
+/* ------------------------------------------------------------------ append */
+
+typedef struct smaq_append_args {
+  /* Input chunk, element (t, h, d) at ptr + t*stride_t + h*stride_h + d
+   * (elements of `dtype`).  k or v may be NULL to skip that half. */
+  const void* k;
+  const void* v;
+  int dtype;
+  int64_t n_tokens;
+  int n_heads;
+  int head_dim;
+  int64_t k_stride_t, k_stride_h;
+  int64_t v_stride_t, v_stride_h;
+  /* destination rows (see the layout note above) */
+  const int64_t* slots; /* nullable, [n_tokens] */
+  int64_t slot_offset;
+  int64_t page_size;
+  /* key format */
+  int key_format;            /* SMAQ_KEYS_SCALAR or SMAQ_KEYS_BVQ */
+  int key_bits;              /* scalar: 2, 3 or 4 */
+  const float* E;            /* scalar: [D, D] row-major fp32, y = k_unit @ E^T */
+  const float* boundaries;   /* scalar: [2^bits - 1] ascending fp32 */
+  const float* E_blocks;     /* bvq: [D/bd, bd, bd] fp32 */
+  const float* centroids;    /* bvq: [D/bd, n_centroids, bd] fp32 (encode space) */
+  int block_dim;             /* bvq: 8 */
+  int n_centroids;           /* bvq: <= 256 */
+  uint8_t* key_codes;        /* scalar: rows of ceil(D / (8/bits)) bytes; bvq: rows of D/bd bytes */
+  void* key_norms;           /* scalar: rows of one `dtype` element */
+  /* value format */
+  int value_bits;            /* 2 or 4 */
+  int group_size;            /* 32, 64 or 128 */
+  uint8_t* v_data;           /* rows of D*bits/8 bytes */
+  void* v_scales;            /* rows of D/group_size `dtype` elements */
+  void* v_zeros;             /* rows of D/group_size `dtype` elements */
+} smaq_append_args;
+
+/* Quantize a chunk of keys and/or values straight into store rows. */
+int smaq_append(const smaq_append_args* args, void* stream);
+
+/* Reference-shaped helpers (dense rows in, dense rows out, n_rows = prod(leading dims)). */
+int smaq_quantize_keys_scalar(const void* k, int dtype, int64_t n_rows, int head_dim,
+                              const float* E, const float* boundaries, int bits,
+                              uint8_t* codes_out, void* norms_out, void* stream);
+int smaq_quantize_values(const void* v, int dtype, int64_t n_rows, int head_dim, int bits,
+                         int group_size, uint8_t* data_out, void* scales_out, void* zeros_out,
+                         void* stream);
+int smaq_quantize_keys_bvq(const void* k, int dtype, int64_t n_rows, int head_dim,
+                           const float* E_blocks, const float* centroids, int block_dim,
+                           int n_centroids, uint8_t* idx_out, void* stream);
+
+/* ------------------------------------------------------------------ decode */
+
+typedef struct smaq_decode_args {
+  /* queries [B, Hq, D]: element (b, h, d) at q + b*q_stride_b + h*q_stride_h + d */
+  const void* q;
+  int q_dtype;
+  int64_t q_stride_b, q_stride_h;
+  int batch, n_q_heads, n_kv_heads, head_dim;
+  float scale;
+  /* compressed history (store rows, see the layout note) */
+  int key_format;            /* SMAQ_KEYS_SCALAR / SMAQ_KEYS_BVQ / SMAQ_KEYS_NONE */
+  int key_bits;
+  const float* E_inv;        /* scalar: [D, D] fp32, q_rot = q @ E_inv^T */
+  const float* centroids;    /* scalar: [2^bits] fp32; bvq: decoded centroids [D/bd, nc, bd] fp32 */
+  int block_dim, n_centroids;
+  const uint8_t* key_codes;
+  const void* key_norms;     /* scalar only, `kv_dtype` */
+  int kv_dtype;              /* dtype of norms / value scales / value zeros */
+  const uint8_t* v_data;
+  const void* v_scales;
+  const void* v_zeros;
+  int value_bits, group_size;
+  const int32_t* block_table; /* nullable: [B, bt_stride] page ids */
+  int64_t bt_stride;
+  int64_t page_size;
+  const int32_t* hist_len;    /* [B] device */
+  const int32_t* hist_total;  /* nullable [B]: history length of the whole sequence (for the
+                                  minimum-history rule when the history is split across GPUs) */
+  int min_history;            /* 16 in the reference */
+  /* exact recent window: element (b, t, h, d) at r + b*r_stride_b + t*r_stride_t + h*r_stride_h + d */
+  const void* recent_k;
+  const void* recent_v;
+  int recent_dtype;
+  int64_t r_stride_b, r_stride_t, r_stride_h;
+  const int32_t* recent_len; /* nullable [B] device */
+  /* outputs: either the final attention output (query dtype) ... */
+  void* out;
+  int64_t o_stride_b, o_stride_h;
+  /* ... and/or fp32 partials [B, Hq, 2*D + 2] (acc_hist[D], acc_recent[D], m, l) for a
+   * cross-GPU merge with smaq_merge_partials.  Either pointer may be NULL, not both. */
+  float* partial_out;
+  /* scratch */
+  void* workspace;
+  size_t workspace_bytes;
+  int num_ctas;              /* 0: one wave over the device's SMs */
+} smaq_decode_args;
+
+/* Bytes of workspace smaq_decode needs for these shapes (host-only computation). */
+size_t smaq_decode_workspace_size(int batch, int n_q_heads, int n_kv_heads, int head_dim,
+                                  int num_ctas);
+int smaq_decode(const smaq_decode_args* args, void* stream);
+
+/* Merge R partial sets [R, B, Hq, 2*D+2] (as written to partial_out) into the
+ * final output [B, Hq, D] (element (b, h, d) at out + b*o_stride_b + h*o_stride_h + d). */
+int smaq_merge_partials(const float* partials, int n_parts, int batch, int n_q_heads, int head_dim,
+                        void* out, int out_dtype, int64_t o_stride_b, int64_t o_stride_h,
+                        void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SMAQ_B200_H_ */

@@ -1,0 +1,93 @@
+"""ctypes binding of ``libsmaq_b200.so`` (declared in ``include/smaq_b200.h``).
+
+The library is loaded from the package directory.  If it is missing the import of any
+compute entry point raises: there is no CPU or pure-torch fallback for the hot path.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libsmaq_b200.so")
+
+SMAQ_F32, SMAQ_BF16, SMAQ_F16 = 0, 1, 2
+SMAQ_KEYS_NONE, SMAQ_KEYS_SCALAR, SMAQ_KEYS_BVQ = 0, 1, 2
+STATUS = {0: "OK", 1: "INVALID", 2: "UNSUPPORTED", 3: "CUDA", 4: "WORKSPACE", 5: "DEVICE"}
+
+# every symbol include/smaq_b200.h declares (checked by the CPU test suite)
+EXPORTS = (
+    "smaq_abi_version", "smaq_last_error", "smaq_append", "smaq_quantize_keys_scalar",
+    "smaq_quantize_values", "smaq_quantize_keys_bvq", "smaq_decode_workspace_size", "smaq_decode",
+    "smaq_merge_partials",
+)
+
+vp = C.c_void_p
+i64 = C.c_int64
+i32 = C.c_int
+
+
+class AppendArgs(C.Structure):
+    _fields_ = [
+        ("k", vp), ("v", vp), ("dtype", i32), ("n_tokens", i64), ("n_heads", i32), ("head_dim", i32),
+        ("k_stride_t", i64), ("k_stride_h", i64), ("v_stride_t", i64), ("v_stride_h", i64),
+        ("slots", vp), ("slot_offset", i64), ("page_size", i64),
+        ("key_format", i32), ("key_bits", i32), ("E", vp), ("boundaries", vp), ("E_blocks", vp),
+        ("centroids", vp), ("block_dim", i32), ("n_centroids", i32), ("key_codes", vp), ("key_norms", vp),
+        ("value_bits", i32), ("group_size", i32), ("v_data", vp), ("v_scales", vp), ("v_zeros", vp),
+    ]
+
+
+class DecodeArgs(C.Structure):
+    _fields_ = [
+        ("q", vp), ("q_dtype", i32), ("q_stride_b", i64), ("q_stride_h", i64),
+        ("batch", i32), ("n_q_heads", i32), ("n_kv_heads", i32), ("head_dim", i32), ("scale", C.c_float),
+        ("key_format", i32), ("key_bits", i32), ("E_inv", vp), ("centroids", vp), ("block_dim", i32),
+        ("n_centroids", i32), ("key_codes", vp), ("key_norms", vp), ("kv_dtype", i32),
+        ("v_data", vp), ("v_scales", vp), ("v_zeros", vp), ("value_bits", i32), ("group_size", i32),
+        ("block_table", vp), ("bt_stride", i64), ("page_size", i64), ("hist_len", vp), ("hist_total", vp),
+        ("min_history", i32), ("recent_k", vp), ("recent_v", vp), ("recent_dtype", i32),
+        ("r_stride_b", i64), ("r_stride_t", i64), ("r_stride_h", i64), ("recent_len", vp),
+        ("out", vp), ("o_stride_b", i64), ("o_stride_h", i64), ("partial_out", vp),
+        ("workspace", vp), ("workspace_bytes", C.c_size_t), ("num_ctas", i32),
+    ]
+
+
+_lib = None
+
+
+def load() -> C.CDLL:
+    """Load the CUDA library; raises if it was not built (no fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(
+            f"smaq_b200 CUDA library not found at {LIB_PATH}; build it with "
+            "`python -m smaq_b200.build` (there is no CPU fallback)")
+    lib = C.CDLL(LIB_PATH)
+    lib.smaq_abi_version.restype = i32
+    lib.smaq_last_error.restype = C.c_char_p
+    lib.smaq_append.argtypes = [C.POINTER(AppendArgs), vp]
+    lib.smaq_append.restype = i32
+    lib.smaq_quantize_keys_scalar.argtypes = [vp, i32, i64, i32, vp, vp, i32, vp, vp, vp]
+    lib.smaq_quantize_keys_scalar.restype = i32
+    lib.smaq_quantize_values.argtypes = [vp, i32, i64, i32, i32, i32, vp, vp, vp, vp]
+    lib.smaq_quantize_values.restype = i32
+    lib.smaq_quantize_keys_bvq.argtypes = [vp, i32, i64, i32, vp, vp, i32, i32, vp, vp]
+    lib.smaq_quantize_keys_bvq.restype = i32
+    lib.smaq_decode_workspace_size.argtypes = [i32, i32, i32, i32, i32]
+    lib.smaq_decode_workspace_size.restype = C.c_size_t
+    lib.smaq_decode.argtypes = [C.POINTER(DecodeArgs), vp]
+    lib.smaq_decode.restype = i32
+    lib.smaq_merge_partials.argtypes = [vp, i32, i32, i32, i32, vp, i32, i64, i64, vp]
+    lib.smaq_merge_partials.restype = i32
+    _lib = lib
+    return lib
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        msg = load().smaq_last_error().decode(errors="replace")
+        raise RuntimeError(f"{what} failed ({STATUS.get(status, status)}): {msg}")

@@ -1,0 +1,146 @@
+"""Block vector quantizer (API of smaq/block_vq.py, encode on sm_100a).
+
+Keys are split into ``head_dim / block_dim`` blocks; block ``b`` is mapped by its own metric
+``E_b`` and assigned the nearest of ``n_centroids`` k-means centroids (distances as torch.cdist
+computes them: ``sqrt(clamp(|x|^2 + |c|^2 - 2 x.c, 0))``, first index on ties).  Encoding runs
+the ``smaq_quantize_keys_bvq`` CUDA kernel; calibration (``fit``: per-block metric and k-means)
+is a one-time torch computation on the caller's device.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import NamedTuple, Optional
+
+import torch
+import torch.nn as nn
+
+from smaq_b200 import ops
+from smaq_b200.ssf import build_smaq_metric
+
+
+class BlockVQQuantized(NamedTuple):
+    """Per-block centroid indices ``(..., n_blocks)`` (int64, as the reference returns them)."""
+
+    indices: torch.Tensor
+    n_blocks: int
+    block_dim: int
+
+
+def _kmeans(data: torch.Tensor, n_centroids: int, n_iters: int = 20, seed: int = 42) -> torch.Tensor:
+    """k-means++ seeding then Lloyd iterations (smaq/block_vq.py:37-79).
+
+    The random draws (one ``randint`` then one ``multinomial`` per further centre, from a
+    generator seeded with ``seed`` on the data's device) follow the reference call for call, so
+    the same data and seed give the reference's codebook on the same device.
+    """
+    n, d = data.shape
+    gen = torch.Generator(device=data.device).manual_seed(seed)
+    if n <= n_centroids:
+        out = torch.zeros((n_centroids, d), device=data.device, dtype=data.dtype)
+        out[:n] = data
+        return out
+    chosen = [int(torch.randint(n, (1,), generator=gen, device=data.device).item())]
+    while len(chosen) < n_centroids:
+        dmin = torch.cdist(data, data[chosen]).min(dim=1).values
+        w = dmin.square()
+        tot = w.sum()
+        if tot > 0:
+            w = w / tot
+        else:
+            w = torch.full((n,), 1.0 / n, device=data.device, dtype=data.dtype)
+        chosen.append(int(torch.multinomial(w, 1, generator=gen).item()))
+    cent = data[chosen].clone()
+    ones = torch.ones(n, device=data.device)
+    for _ in range(n_iters):
+        assign = torch.cdist(data, cent).argmin(dim=1)
+        sums = torch.zeros_like(cent).index_add_(0, assign, data)
+        cnt = torch.zeros(n_centroids, device=data.device).index_add_(0, assign, ones)
+        hit = cnt > 0
+        sums[hit] /= cnt[hit].unsqueeze(1)
+        sums[~hit] = cent[~hit]
+        cent = sums
+    return cent
+
+
+class SMAQBlockVQ(nn.Module):
+    """SMAQ block VQ (constructor and buffers of smaq/block_vq.py:86-149)."""
+
+    def __init__(self, head_dim: int, block_dim: int = 8, n_centroids: int = 256, c: float = 5.0,
+                 device: Optional[torch.device] = None, dtype: torch.dtype = torch.float32):
+        super().__init__()
+        if head_dim % block_dim != 0:
+            raise ValueError(f"head_dim={head_dim} must be divisible by block_dim={block_dim}")
+        self.head_dim = head_dim
+        self.block_dim = block_dim
+        self.n_blocks = head_dim // block_dim
+        self.n_centroids = n_centroids
+        self.c = c
+        self._device = torch.device(device) if device is not None else torch.device("cpu")
+        self._dtype = dtype
+        eye = torch.eye(block_dim, device=self._device, dtype=dtype).expand(self.n_blocks, -1, -1)
+        self.register_buffer("E_blocks", eye.clone())
+        self.register_buffer("E_inv_blocks", eye.clone())
+        z = torch.zeros(self.n_blocks, n_centroids, block_dim, device=self._device, dtype=dtype)
+        self.register_buffer("centroids", z.clone())
+        self.register_buffer("decoded_centroids", z.clone())
+        self._fitted = False
+
+    @property
+    def bits_per_dim(self) -> float:
+        return math.log2(self.n_centroids) / self.block_dim
+
+    def fit(self, calibration_keys: torch.Tensor, calibration_queries: torch.Tensor, kmeans_iters: int = 20,
+            seed: int = 42) -> "SMAQBlockVQ":
+        """Per block: uncentered query covariance -> metric -> k-means in the shaped space ->
+        pre-decoded centroids ``centroid @ E_inv_b^T`` (smaq/block_vq.py:160-210)."""
+        N = calibration_keys.shape[0]
+        Es, Eis, cs, ds = [], [], [], []
+        for b in range(self.n_blocks):
+            sl = slice(b * self.block_dim, (b + 1) * self.block_dim)
+            qb = calibration_queries[:, sl].float()
+            E, E_inv = build_smaq_metric((qb.T @ qb) / N, c=self.c)
+            shaped = calibration_keys[:, sl].float() @ E.T
+            cent = _kmeans(shaped, self.n_centroids, kmeans_iters, seed + b)
+            Es.append(E)
+            Eis.append(E_inv)
+            cs.append(cent)
+            ds.append(cent @ E_inv.T)
+        self.E_blocks = torch.stack(Es).to(self._device, self._dtype)
+        self.E_inv_blocks = torch.stack(Eis).to(self._device, self._dtype)
+        self.centroids = torch.stack(cs).to(self._device, self._dtype)
+        self.decoded_centroids = torch.stack(ds).to(self._device, self._dtype)
+        self._fitted = True
+        return self
+
+    def quantize_u8(self, k: torch.Tensor) -> torch.Tensor:
+        """GPU encode returning the compact uint8 indices the store keeps."""
+        return ops.quantize_keys_bvq(k, self.E_blocks, self.centroids)
+
+    def quantize(self, k: torch.Tensor) -> BlockVQQuantized:
+        idx = self.quantize_u8(k).to(torch.int64)
+        return BlockVQQuantized(indices=idx, n_blocks=self.n_blocks, block_dim=self.block_dim)
+
+    def dequantize(self, q: BlockVQQuantized) -> torch.Tensor:
+        """Gather of the pre-decoded centroids (pure lookup)."""
+        lead = q.indices.shape[:-1]
+        idx = q.indices.reshape(-1, self.n_blocks).long()
+        parts = [self.decoded_centroids[b][idx[:, b]] for b in range(self.n_blocks)]
+        return torch.cat(parts, dim=-1).reshape(*lead, self.head_dim)
+
+    def attention_score(self, query: torch.Tensor, quantized_key: BlockVQQuantized,
+                        scale: Optional[float] = None) -> torch.Tensor:
+        """``q . k_hat [* scale]`` in the query dtype (standalone scoring)."""
+        k_hat = self.dequantize(quantized_key)
+        s = torch.matmul(query.float(), k_hat.float().transpose(-2, -1))
+        if scale is not None:
+            s = s * scale
+        return s.to(query.dtype)
+
+    def logit_mse(self, queries: torch.Tensor, keys: torch.Tensor) -> float:
+        """Held-out logit MSE ``E[(q . (k - k_hat))^2]``."""
+        k_hat = self.dequantize(self.quantize(keys))
+        return (queries.float() * (keys.float() - k_hat.float())).sum(-1).square().mean().item()
+
+    def forward(self, k: torch.Tensor) -> torch.Tensor:
+        return self.dequantize(self.quantize(k))

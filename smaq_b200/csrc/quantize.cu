@@ -1,0 +1,588 @@
+// Append / quantize kernels: value codec, scalar metric-aware key codes, block-VQ key codes.
+//
+// Reference algorithm (gauravsaini/smaq):
+//   values  smaq/kv_cache.py:50-91   group-asymmetric min/max quantization, storage-dtype arithmetic
+//   keys    smaq/quantizer.py:138-145 norm -> k/(norm+1e-10) -> @E^T -> searchsorted -> pack
+//   bvq     smaq/block_vq.py:216-244  per 8-dim block: @E_b^T -> cdist to the codebook -> argmin
+//
+// Bit-exactness: every elementwise step is computed in fp32 and rounded to the storage dtype
+// exactly where torch rounds (one rounding per torch op).  Only the d x d contraction and the
+// cdist dot products have a library-defined summation order; their results agree with the
+// reference except for elements that sit within an fp32 rounding band of a decision boundary.
+#include <math.h>
+
+#include "common.cuh"
+#include "tc_rotate.cuh"
+
+namespace smaq {
+
+// =====================================================================================
+// values: one warp per row, EPL = head_dim / 32 consecutive elements per lane
+// =====================================================================================
+template <class DT, int EPL, int BITS>
+__global__ void __launch_bounds__(256) value_quant_kernel(
+    const typename DT::T* __restrict__ v, int64_t n_tokens, int n_heads, int64_t st, int64_t sh,
+    const int64_t* __restrict__ slots, int64_t slot_offset, int64_t page_size, int group_size,
+    uint8_t* __restrict__ data, typename DT::T* __restrict__ scales, typename DT::T* __restrict__ zeros) {
+  constexpr int D = 32 * EPL;
+  constexpr int NL = (1 << BITS) - 1;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  const int64_t n_rows = n_tokens * n_heads;
+  const int lpg = group_size / EPL;  // lanes per group (power of two)
+  const int ng = D / group_size;
+  const float floor_ = rnd<DT>(1e-10f);
+  for (int64_t r = warp; r < n_rows; r += nwarps) {
+    const int64_t t = r / n_heads;
+    const int h = int(r - t * n_heads);
+    float x[EPL];
+    load_vec<DT, EPL>(v + t * st + h * sh + lane * EPL, x);
+    float mn = x[0], mx = x[0];
+#pragma unroll
+    for (int i = 1; i < EPL; ++i) {
+      mn = fminf(mn, x[i]);
+      mx = fmaxf(mx, x[i]);
+    }
+    for (int o = 1; o < lpg; o <<= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    // scale = ((max - min) / n_levels).clamp(min=1e-10); zero = min   (kv_cache.py:78-83)
+    float scale = rnd<DT>(__fdiv_rn(rnd<DT>(mx - mn), float(NL)));
+    if (scale < floor_) scale = floor_;
+    uint32_t packed = 0;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      // ((v - zero) / scale).round().clamp(0, n_levels)   (kv_cache.py:85)
+      float q = rnd<DT>(__fdiv_rn(rnd<DT>(x[i] - mn), scale));
+      q = fminf(fmaxf(rintf(q), 0.0f), float(NL));  // NaN -> 0 like the reference's uint8 cast
+      packed |= uint32_t(q) << (i * BITS);
+    }
+    const int64_t row = store_row(slots, slot_offset, page_size, n_heads, t, h);
+    constexpr int LANE_BITS = EPL * BITS;
+    uint8_t* dst = data + row * (D * BITS / 8);
+    if constexpr (LANE_BITS >= 8) {
+      constexpr int NB = LANE_BITS / 8;
+      if constexpr (NB == 1) {
+        dst[lane] = uint8_t(packed);
+      } else if constexpr (NB == 2) {
+        reinterpret_cast<uint16_t*>(dst)[lane] = uint16_t(packed);
+      } else {
+        reinterpret_cast<uint32_t*>(dst)[lane] = packed;
+      }
+    } else {  // 4 bits per lane: pair lanes into one byte
+      const uint32_t hi = __shfl_down_sync(0xffffffffu, packed, 1);
+      if ((lane & 1) == 0) dst[lane >> 1] = uint8_t(packed | (hi << 4));
+    }
+    if ((lane % lpg) == 0) {
+      const int g = lane / lpg;
+      scales[row * ng + g] = from_f<DT>(scale);
+      zeros[row * ng + g] = from_f<DT>(mn);
+    }
+  }
+}
+
+// =====================================================================================
+// scalar keys (SIMT path): a warp quantizes R rows at a time; E^T and the k_unit rows are
+// staged in shared memory.  Used for fp32/fp16 keys and for head_dim != 128; bf16 keys at
+// head_dim 128 take the tcgen05 path in tc_rotate.cuh.
+// =====================================================================================
+constexpr int SQ_WARPS = 8;
+constexpr int SQ_ROWS = 8;
+
+template <class DT, int EPL, int BITS>
+__global__ void __launch_bounds__(SQ_WARPS * 32) scalar_key_kernel(
+    const typename DT::T* __restrict__ k, int64_t n_tokens, int n_heads, int64_t st, int64_t sh,
+    const int64_t* __restrict__ slots, int64_t slot_offset, int64_t page_size,
+    const float* __restrict__ E, const float* __restrict__ bnd, uint8_t* __restrict__ codes,
+    typename DT::T* __restrict__ norms) {
+  constexpr int D = 32 * EPL;
+  constexpr int NB = (1 << BITS) - 1;
+  constexpr int VPB = (8 / BITS) > 0 ? 8 / BITS : 1;
+  constexpr int PD = (D + VPB - 1) / VPB;
+  extern __shared__ float smem[];
+  float* ET = smem;                       // [D][D]: ET[i][j] = E[j][i]
+  float* KU = ET + D * D;                 // [warps][R][D]
+  __shared__ float sb[16];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int idx = threadIdx.x; idx < D * D; idx += blockDim.x) {
+    const int j = idx / D, i = idx - j * D;
+    ET[i * D + j] = E[idx];
+  }
+  if (threadIdx.x < NB) sb[threadIdx.x] = bnd[threadIdx.x];
+  __syncthreads();
+  float b[NB];
+#pragma unroll
+  for (int i = 0; i < NB; ++i) b[i] = sb[i];
+  float* ku = KU + wid * SQ_ROWS * D;
+  const int64_t n_rows = n_tokens * n_heads;
+  const int64_t gw = int64_t(blockIdx.x) * SQ_WARPS + wid;
+  const int64_t nw = int64_t(gridDim.x) * SQ_WARPS;
+  for (int64_t r0 = gw * SQ_ROWS; r0 < n_rows; r0 += nw * SQ_ROWS) {
+    float nrm[SQ_ROWS];
+#pragma unroll
+    for (int rr = 0; rr < SQ_ROWS; ++rr) {
+      const int64_t r = r0 + rr;
+      float x[EPL];
+      if (r < n_rows) {
+        const int64_t t = r / n_heads;
+        const int h = int(r - t * n_heads);
+        load_vec<DT, EPL>(k + t * st + h * sh + lane * EPL, x);
+      } else {
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) x[i] = 0.f;
+      }
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) ss = fmaf(x[i], x[i], ss);
+      ss = warp_sum(ss);
+      // norms = k.norm(-1) in the key dtype; k_unit = k / (norms + 1e-10)  (quantizer.py:140-141)
+      const float n = rnd<DT>(sqrtf(ss));
+      nrm[rr] = n;
+      const float den = rnd<DT>(n + 1e-10f);
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) ku[rr * D + lane * EPL + i] = rnd<DT>(__fdiv_rn(x[i], den));
+    }
+    __syncwarp();
+    // y = k_unit.float() @ E.T  (quantizer.py:142)
+    float y[SQ_ROWS][EPL];
+#pragma unroll
+    for (int rr = 0; rr < SQ_ROWS; ++rr)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) y[rr][e] = 0.f;
+#pragma unroll 4
+    for (int i = 0; i < D; ++i) {
+      float et[EPL];
+      if constexpr (EPL == 4) {
+        const float4 w = *reinterpret_cast<const float4*>(ET + i * D + lane * 4);
+        et[0] = w.x; et[1] = w.y; et[2] = w.z; et[3] = w.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) et[e] = ET[i * D + lane * EPL + e];
+      }
+#pragma unroll
+      for (int rr = 0; rr < SQ_ROWS; ++rr) {
+        const float a = ku[rr * D + i];
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) y[rr][e] = fmaf(a, et[e], y[rr][e]);
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int rr = 0; rr < SQ_ROWS; ++rr) {
+      const int64_t r = r0 + rr;
+      if (r >= n_rows) break;
+      const int64_t t = r / n_heads;
+      const int h = int(r - t * n_heads);
+      const int64_t row = store_row(slots, slot_offset, page_size, n_heads, t, h);
+      // searchsorted(decision_boundaries, y), right=False: count of boundaries < y  (:143)
+      uint32_t c[EPL];
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        int cnt = 0;
+#pragma unroll
+        for (int i = 0; i < NB; ++i) cnt += (b[i] < y[rr][e]) ? 1 : 0;
+        c[e] = isnan(y[rr][e]) ? uint32_t(NB) : uint32_t(cnt);
+      }
+      uint8_t* dst = codes + row * PD;
+      // _pack_indices (quantizer.py:34-46): VPB codes per byte, LSB first
+      if constexpr (VPB == 4) {       // 2-bit: EPL codes -> EPL/4 bytes (EPL is 2 or 4)
+        if constexpr (EPL == 4) {
+          dst[lane] = uint8_t(c[0] | (c[1] << 2) | (c[2] << 4) | (c[3] << 6));
+        } else {
+          const uint32_t p = c[0] | (c[1] << 2);
+          const uint32_t hi = __shfl_down_sync(0xffffffffu, p, 1);
+          if ((lane & 1) == 0) dst[lane >> 1] = uint8_t(p | (hi << 4));
+        }
+      } else {                        // 3- and 4-bit: two codes per byte at shifts 0 and BITS
+#pragma unroll
+        for (int e = 0; e < EPL; e += 2) dst[(lane * EPL + e) / 2] = uint8_t(c[e] | (c[e + 1] << BITS));
+      }
+      if (lane == 0) norms[row] = from_f<DT>(nrm[rr]);
+    }
+    __syncwarp();
+  }
+}
+
+// =====================================================================================
+// block VQ keys: a warp encodes BQ_ROWS rows per pass; codebook and its squared norms live
+// in shared memory.  Distances follow torch.cdist's matmul expansion
+//   d2 = |x|^2 + |c|^2 - 2 x.c,  dist = sqrt(clamp(d2, 0)),  argmin (first index on ties).
+// =====================================================================================
+constexpr int BQ_WARPS = 8;
+constexpr int BQ_ROWS = 4;
+
+template <class DT, int EPL>
+__global__ void __launch_bounds__(BQ_WARPS * 32) bvq_key_kernel(
+    const typename DT::T* __restrict__ k, int64_t n_tokens, int n_heads, int64_t st, int64_t sh,
+    const int64_t* __restrict__ slots, int64_t slot_offset, int64_t page_size,
+    const float* __restrict__ Eb, const float* __restrict__ cent, int nc, uint8_t* __restrict__ out) {
+  constexpr int D = 32 * EPL;
+  constexpr int BD = 8;
+  constexpr int NBLK = D / BD;
+  extern __shared__ float smem[];
+  float* C = smem;                        // [NBLK][nc][8]
+  float* CN = C + NBLK * nc * BD;         // [NBLK][nc]
+  float* EB = CN + NBLK * nc;             // [NBLK][8][8]
+  float* KS = EB + NBLK * BD * BD;        // [warps][BQ_ROWS][D]
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < NBLK * nc * BD; i += blockDim.x) C[i] = cent[i];
+  for (int i = threadIdx.x; i < NBLK * BD * BD; i += blockDim.x) EB[i] = Eb[i];
+  __syncthreads();
+  for (int i = threadIdx.x; i < NBLK * nc; i += blockDim.x) {
+    float s = 0.f;  // x2.pow(2).sum(-1)
+#pragma unroll
+    for (int j = 0; j < BD; ++j) s = fmaf(C[i * BD + j], C[i * BD + j], s);
+    CN[i] = s;
+  }
+  __syncthreads();
+  float* ks = KS + wid * BQ_ROWS * D;
+  const int64_t n_rows = n_tokens * n_heads;
+  const int64_t gw = int64_t(blockIdx.x) * BQ_WARPS + wid;
+  const int64_t nw = int64_t(gridDim.x) * BQ_WARPS;
+  for (int64_t r0 = gw * BQ_ROWS; r0 < n_rows; r0 += nw * BQ_ROWS) {
+    // shaped keys: k_b.float() @ E_b^T per block   (block_vq.py:230-235)
+#pragma unroll
+    for (int rr = 0; rr < BQ_ROWS; ++rr) {
+      const int64_t r = r0 + rr;
+      float x[EPL];
+      if (r < n_rows) {
+        const int64_t t = r / n_heads;
+        const int h = int(r - t * n_heads);
+        load_vec<DT, EPL>(k + t * st + h * sh + lane * EPL, x);
+      } else {
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) x[i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) ks[rr * D + lane * EPL + i] = x[i];
+    }
+    __syncwarp();
+    float sh_[BQ_ROWS][EPL];
+#pragma unroll
+    for (int rr = 0; rr < BQ_ROWS; ++rr) {
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        const int j = lane * EPL + e, blk = j / BD, jj = j % BD;
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < BD; ++i) s = fmaf(ks[rr * D + blk * BD + i], EB[(blk * BD + jj) * BD + i], s);
+        sh_[rr][e] = s;
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int rr = 0; rr < BQ_ROWS; ++rr)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) ks[rr * D + lane * EPL + e] = sh_[rr][e];
+    __syncwarp();
+    for (int blk = 0; blk < NBLK; ++blk) {
+      float xs[BQ_ROWS][BD], xn[BQ_ROWS];
+#pragma unroll
+      for (int rr = 0; rr < BQ_ROWS; ++rr) {
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < BD; ++j) {
+          xs[rr][j] = ks[rr * D + blk * BD + j];
+          s = fmaf(xs[rr][j], xs[rr][j], s);
+        }
+        xn[rr] = s;
+      }
+      float best[BQ_ROWS];
+      int bi[BQ_ROWS];
+#pragma unroll
+      for (int rr = 0; rr < BQ_ROWS; ++rr) {
+        best[rr] = INFINITY;
+        bi[rr] = 0;
+      }
+      for (int c = lane; c < nc; c += 32) {
+        const float4 c0 = *reinterpret_cast<const float4*>(C + (blk * nc + c) * BD);
+        const float4 c1 = *reinterpret_cast<const float4*>(C + (blk * nc + c) * BD + 4);
+        const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+        const float cn = CN[blk * nc + c];
+#pragma unroll
+        for (int rr = 0; rr < BQ_ROWS; ++rr) {
+          float dot = 0.f;
+#pragma unroll
+          for (int j = 0; j < BD; ++j) dot = fmaf(-2.0f * xs[rr][j], cv[j], dot);
+          const float d = sqrtf(fmaxf(dot + xn[rr] + cn, 0.0f));
+          if (d < best[rr]) {
+            best[rr] = d;
+            bi[rr] = c;
+          }
+        }
+      }
+#pragma unroll
+      for (int rr = 0; rr < BQ_ROWS; ++rr) {
+        float bv = best[rr];
+        int bx = bi[rr];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int ox = __shfl_xor_sync(0xffffffffu, bx, o);
+          if (ov < bv || (ov == bv && ox < bx)) {
+            bv = ov;
+            bx = ox;
+          }
+        }
+        bi[rr] = bx;
+      }
+      if (lane == 0) {
+#pragma unroll
+        for (int rr = 0; rr < BQ_ROWS; ++rr) {
+          const int64_t r = r0 + rr;
+          if (r < n_rows) {
+            const int64_t t = r / n_heads;
+            const int h = int(r - t * n_heads);
+            const int64_t row = store_row(slots, slot_offset, page_size, n_heads, t, h);
+            out[row * NBLK + blk] = uint8_t(bi[rr]);
+          }
+        }
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// =====================================================================================
+// host side
+// =====================================================================================
+static int grid_for(int64_t warps_needed, int warps_per_block, int blocks_per_sm) {
+  int64_t g = (warps_needed + warps_per_block - 1) / warps_per_block;
+  const int64_t cap = int64_t(num_sms()) * blocks_per_sm;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return int(g);
+}
+
+template <class DT, int EPL>
+static int launch_values_t(const smaq_append_args& a, cudaStream_t s) {
+  const int64_t rows = a.n_tokens * a.n_heads;
+  const int grid = grid_for(rows, 8, 8);
+  using T = typename DT::T;
+  if (a.value_bits == 2)
+    value_quant_kernel<DT, EPL, 2><<<grid, 256, 0, s>>>(
+        static_cast<const T*>(a.v), a.n_tokens, a.n_heads, a.v_stride_t, a.v_stride_h, a.slots,
+        a.slot_offset, a.page_size, a.group_size, a.v_data, static_cast<T*>(a.v_scales),
+        static_cast<T*>(a.v_zeros));
+  else
+    value_quant_kernel<DT, EPL, 4><<<grid, 256, 0, s>>>(
+        static_cast<const T*>(a.v), a.n_tokens, a.n_heads, a.v_stride_t, a.v_stride_h, a.slots,
+        a.slot_offset, a.page_size, a.group_size, a.v_data, static_cast<T*>(a.v_scales),
+        static_cast<T*>(a.v_zeros));
+  return cuda_status(cudaGetLastError(), "value_quant_kernel");
+}
+
+template <class DT>
+static int launch_values_d(const smaq_append_args& a, cudaStream_t s) {
+  switch (a.head_dim) {
+    case 64: return launch_values_t<DT, 2>(a, s);
+    case 128: return launch_values_t<DT, 4>(a, s);
+    case 256: return launch_values_t<DT, 8>(a, s);
+  }
+  return fail(SMAQ_ERR_UNSUPPORTED, "values: head_dim %d not in {64,128,256}", a.head_dim);
+}
+
+template <class DT, int EPL, int BITS>
+static int launch_scalar_t(const smaq_append_args& a, cudaStream_t s) {
+  constexpr int D = 32 * EPL;
+  const size_t sm = sizeof(float) * (D * D + SQ_WARPS * SQ_ROWS * D);
+  auto kern = scalar_key_kernel<DT, EPL, BITS>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+  if (e != cudaSuccess) return cuda_status(e, "scalar_key_kernel attr");
+  const int64_t rows = a.n_tokens * a.n_heads;
+  const int grid = grid_for((rows + SQ_ROWS - 1) / SQ_ROWS, SQ_WARPS, 2);
+  using T = typename DT::T;
+  kern<<<grid, SQ_WARPS * 32, sm, s>>>(static_cast<const T*>(a.k), a.n_tokens, a.n_heads, a.k_stride_t,
+                                       a.k_stride_h, a.slots, a.slot_offset, a.page_size, a.E,
+                                       a.boundaries, a.key_codes, static_cast<T*>(a.key_norms));
+  return cuda_status(cudaGetLastError(), "scalar_key_kernel");
+}
+
+template <class DT, int EPL>
+static int launch_scalar_b(const smaq_append_args& a, cudaStream_t s) {
+  switch (a.key_bits) {
+    case 2: return launch_scalar_t<DT, EPL, 2>(a, s);
+    case 3: return launch_scalar_t<DT, EPL, 3>(a, s);
+    case 4: return launch_scalar_t<DT, EPL, 4>(a, s);
+  }
+  return fail(SMAQ_ERR_UNSUPPORTED, "scalar keys: bits %d not in {2,3,4}", a.key_bits);
+}
+
+template <class DT>
+static int launch_scalar_d(const smaq_append_args& a, cudaStream_t s) {
+  if constexpr (std::is_same<DT, BF16>::value) {
+    if (a.head_dim == 128 && tc_rotate_enabled()) return launch_scalar_keys_tc(a, s);
+  }
+  switch (a.head_dim) {
+    case 64: return launch_scalar_b<DT, 2>(a, s);
+    case 128: return launch_scalar_b<DT, 4>(a, s);
+  }
+  return fail(SMAQ_ERR_UNSUPPORTED, "scalar keys: head_dim %d not in {64,128}", a.head_dim);
+}
+
+template <class DT, int EPL>
+static int launch_bvq_t(const smaq_append_args& a, cudaStream_t s) {
+  constexpr int D = 32 * EPL;
+  constexpr int NBLK = D / 8;
+  const int nc = a.n_centroids;
+  const size_t sm = sizeof(float) * (NBLK * nc * 8 + NBLK * nc + NBLK * 64 + BQ_WARPS * BQ_ROWS * D);
+  auto kern = bvq_key_kernel<DT, EPL>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+  if (e != cudaSuccess) return cuda_status(e, "bvq_key_kernel attr");
+  const int64_t rows = a.n_tokens * a.n_heads;
+  const int grid = grid_for((rows + BQ_ROWS - 1) / BQ_ROWS, BQ_WARPS, 1);
+  using T = typename DT::T;
+  kern<<<grid, BQ_WARPS * 32, sm, s>>>(static_cast<const T*>(a.k), a.n_tokens, a.n_heads, a.k_stride_t,
+                                       a.k_stride_h, a.slots, a.slot_offset, a.page_size, a.E_blocks,
+                                       a.centroids, nc, a.key_codes);
+  return cuda_status(cudaGetLastError(), "bvq_key_kernel");
+}
+
+template <class DT>
+static int launch_bvq_d(const smaq_append_args& a, cudaStream_t s) {
+  switch (a.head_dim) {
+    case 64: return launch_bvq_t<DT, 2>(a, s);
+    case 128: return launch_bvq_t<DT, 4>(a, s);
+  }
+  return fail(SMAQ_ERR_UNSUPPORTED, "bvq keys: head_dim %d not in {64,128}", a.head_dim);
+}
+
+template <template <class> class F>
+static int by_dtype(int dtype, const smaq_append_args& a, cudaStream_t s) {
+  switch (dtype) {
+    case SMAQ_F32: return F<F32>::run(a, s);
+    case SMAQ_BF16: return F<BF16>::run(a, s);
+    case SMAQ_F16: return F<F16>::run(a, s);
+  }
+  return fail(SMAQ_ERR_INVALID, "unknown dtype %d", dtype);
+}
+template <class DT> struct RunValues { static int run(const smaq_append_args& a, cudaStream_t s) { return launch_values_d<DT>(a, s); } };
+template <class DT> struct RunScalar { static int run(const smaq_append_args& a, cudaStream_t s) { return launch_scalar_d<DT>(a, s); } };
+template <class DT> struct RunBvq { static int run(const smaq_append_args& a, cudaStream_t s) { return launch_bvq_d<DT>(a, s); } };
+
+static size_t dsize(int dtype) { return dtype == SMAQ_F32 ? 4 : 2; }
+
+static int validate_append(const smaq_append_args& a) {
+  if (a.n_tokens < 0 || a.n_heads <= 0 || a.head_dim <= 0)
+    return fail(SMAQ_ERR_INVALID, "append: bad sizes n_tokens=%lld n_heads=%d head_dim=%d",
+                (long long)a.n_tokens, a.n_heads, a.head_dim);
+  if (a.page_size <= 0) return fail(SMAQ_ERR_INVALID, "append: page_size must be > 0");
+  if (a.dtype != SMAQ_F32 && a.dtype != SMAQ_BF16 && a.dtype != SMAQ_F16)
+    return fail(SMAQ_ERR_INVALID, "append: unknown dtype %d", a.dtype);
+  const size_t es = dsize(a.dtype);
+  const int epl = a.head_dim / 32;
+  if (a.v) {
+    if (a.value_bits != 2 && a.value_bits != 4)
+      return fail(SMAQ_ERR_INVALID, "values: bits %d not in {2,4}", a.value_bits);
+    if (a.group_size <= 0 || a.head_dim % a.group_size)
+      return fail(SMAQ_ERR_INVALID, "head_dim %d must be divisible by group_size %d", a.head_dim, a.group_size);
+    const int lpg = a.group_size / (epl ? epl : 1);
+    if (a.group_size % (epl ? epl : 1) || (lpg & (lpg - 1)) || lpg < 1 || lpg > 32)
+      return fail(SMAQ_ERR_UNSUPPORTED, "values: group_size %d with head_dim %d", a.group_size, a.head_dim);
+    if (!a.v_data || !a.v_scales || !a.v_zeros) return fail(SMAQ_ERR_INVALID, "values: null output");
+    if ((reinterpret_cast<uintptr_t>(a.v) % (es * epl)) || (a.v_stride_t % epl) || (a.v_stride_h % epl))
+      return fail(SMAQ_ERR_INVALID, "values: input must be aligned to %d elements", epl);
+  }
+  if (a.k) {
+    if ((reinterpret_cast<uintptr_t>(a.k) % (es * epl)) || (a.k_stride_t % epl) || (a.k_stride_h % epl))
+      return fail(SMAQ_ERR_INVALID, "keys: input must be aligned to %d elements", epl);
+    if (a.key_format == SMAQ_KEYS_SCALAR) {
+      if (a.key_bits < 2 || a.key_bits > 4) return fail(SMAQ_ERR_UNSUPPORTED, "scalar keys: bits %d", a.key_bits);
+      if (!a.E || !a.boundaries || !a.key_codes || !a.key_norms)
+        return fail(SMAQ_ERR_INVALID, "scalar keys: null table or output");
+    } else if (a.key_format == SMAQ_KEYS_BVQ) {
+      if (a.block_dim != 8) return fail(SMAQ_ERR_UNSUPPORTED, "bvq: block_dim %d (only 8)", a.block_dim);
+      if (a.n_centroids < 1 || a.n_centroids > 256)
+        return fail(SMAQ_ERR_UNSUPPORTED, "bvq: n_centroids %d not in [1,256]", a.n_centroids);
+      if (!a.E_blocks || !a.centroids || !a.key_codes) return fail(SMAQ_ERR_INVALID, "bvq: null table or output");
+    } else {
+      return fail(SMAQ_ERR_INVALID, "keys given with key_format %d", a.key_format);
+    }
+  }
+  return SMAQ_OK;
+}
+
+}  // namespace smaq
+
+using namespace smaq;
+
+extern "C" int smaq_append(const smaq_append_args* args, void* stream) {
+  if (!args) return fail(SMAQ_ERR_INVALID, "append: null args");
+  const smaq_append_args& a = *args;
+  int st = validate_append(a);
+  if (st) return st;
+  if (a.n_tokens == 0) return SMAQ_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (a.v) {
+    st = by_dtype<RunValues>(a.dtype, a, s);
+    if (st) return st;
+  }
+  if (a.k) {
+    if (a.key_format == SMAQ_KEYS_SCALAR)
+      st = by_dtype<RunScalar>(a.dtype, a, s);
+    else
+      st = by_dtype<RunBvq>(a.dtype, a, s);
+  }
+  return st;
+}
+
+extern "C" int smaq_quantize_keys_scalar(const void* k, int dtype, int64_t n_rows, int head_dim,
+                                         const float* E, const float* boundaries, int bits,
+                                         uint8_t* codes_out, void* norms_out, void* stream) {
+  smaq_append_args a = {};
+  a.k = k;
+  a.dtype = dtype;
+  a.n_tokens = n_rows;
+  a.n_heads = 1;
+  a.head_dim = head_dim;
+  a.k_stride_t = head_dim;
+  a.page_size = n_rows > 0 ? n_rows : 1;
+  a.key_format = SMAQ_KEYS_SCALAR;
+  a.key_bits = bits;
+  a.E = E;
+  a.boundaries = boundaries;
+  a.key_codes = codes_out;
+  a.key_norms = norms_out;
+  return smaq_append(&a, stream);
+}
+
+extern "C" int smaq_quantize_values(const void* v, int dtype, int64_t n_rows, int head_dim, int bits,
+                                    int group_size, uint8_t* data_out, void* scales_out, void* zeros_out,
+                                    void* stream) {
+  smaq_append_args a = {};
+  a.v = v;
+  a.dtype = dtype;
+  a.n_tokens = n_rows;
+  a.n_heads = 1;
+  a.head_dim = head_dim;
+  a.v_stride_t = head_dim;
+  a.page_size = n_rows > 0 ? n_rows : 1;
+  a.value_bits = bits;
+  a.group_size = group_size;
+  a.v_data = data_out;
+  a.v_scales = scales_out;
+  a.v_zeros = zeros_out;
+  return smaq_append(&a, stream);
+}
+
+extern "C" int smaq_quantize_keys_bvq(const void* k, int dtype, int64_t n_rows, int head_dim,
+                                      const float* E_blocks, const float* centroids, int block_dim,
+                                      int n_centroids, uint8_t* idx_out, void* stream) {
+  smaq_append_args a = {};
+  a.k = k;
+  a.dtype = dtype;
+  a.n_tokens = n_rows;
+  a.n_heads = 1;
+  a.head_dim = head_dim;
+  a.k_stride_t = head_dim;
+  a.page_size = n_rows > 0 ? n_rows : 1;
+  a.key_format = SMAQ_KEYS_BVQ;
+  a.E_blocks = E_blocks;
+  a.centroids = centroids;
+  a.block_dim = block_dim;
+  a.n_centroids = n_centroids;
+  a.key_codes = idx_out;
+  return smaq_append(&a, stream);
+}

@@ -1,0 +1,270 @@
+"""Torch-facing wrappers of the C-ABI kernels.
+
+Every function here takes CUDA tensors, enqueues the kernel on
+``torch.cuda.current_stream()`` and returns freshly allocated outputs (or writes
+into caller buffers).  CPU tensors raise ``RuntimeError``: the hot path has no
+CPU implementation.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from smaq_b200 import _lib
+from smaq_b200._lib import SMAQ_BF16, SMAQ_F16, SMAQ_F32, SMAQ_KEYS_BVQ, SMAQ_KEYS_SCALAR
+
+_DT = {torch.float32: SMAQ_F32, torch.bfloat16: SMAQ_BF16, torch.float16: SMAQ_F16}
+
+MIN_HISTORY = 16
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DT[dt]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {dt}; expected float32, bfloat16 or float16") from None
+
+
+def _cuda(*ts: Optional[torch.Tensor]) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(
+                "smaq_b200 kernels need CUDA tensors (there is no CPU fallback); got a tensor on "
+                f"{t.device}")
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def packed_dim(dim: int, bits: int) -> int:
+    vpb = max(1, 8 // bits)
+    return (dim + vpb - 1) // vpb
+
+
+def _rows(x: torch.Tensor) -> torch.Tensor:
+    """Contiguous ``[n_rows, D]`` view of ``(..., D)``."""
+    return x.reshape(-1, x.shape[-1]).contiguous()
+
+
+# --------------------------------------------------------------------- quantize
+def quantize_keys_scalar(k: torch.Tensor, E: torch.Tensor, boundaries: torch.Tensor, bits: int):
+    """``(..., D)`` keys -> (packed codes ``(..., ceil(D / (8//bits)))`` uint8, norms ``(...)``)."""
+    _cuda(k, E, boundaries)
+    lib = _lib.load()
+    D = k.shape[-1]
+    kr = _rows(k)
+    n = kr.shape[0]
+    codes = torch.empty((n, packed_dim(D, bits)), dtype=torch.uint8, device=k.device)
+    norms = torch.empty((n,), dtype=k.dtype, device=k.device)
+    Ef = E.to(torch.float32).contiguous()
+    bf = boundaries.to(torch.float32).contiguous()
+    _lib.check(lib.smaq_quantize_keys_scalar(kr.data_ptr(), dtype_code(k.dtype), n, D, Ef.data_ptr(),
+                                             bf.data_ptr(), bits, codes.data_ptr(), norms.data_ptr(),
+                                             _stream()), "smaq_quantize_keys_scalar")
+    return codes.reshape(*k.shape[:-1], -1), norms.reshape(k.shape[:-1])
+
+
+def quantize_values(v: torch.Tensor, bits: int = 2, group_size: int = 32):
+    """``(..., D)`` values -> (data uint8 ``(..., D*bits/8)``, scales, zeros ``(..., D/group)``)."""
+    _cuda(v)
+    lib = _lib.load()
+    D = v.shape[-1]
+    vr = _rows(v)
+    n = vr.shape[0]
+    data = torch.empty((n, D * bits // 8), dtype=torch.uint8, device=v.device)
+    scales = torch.empty((n, D // group_size), dtype=v.dtype, device=v.device)
+    zeros = torch.empty_like(scales)
+    _lib.check(lib.smaq_quantize_values(vr.data_ptr(), dtype_code(v.dtype), n, D, bits, group_size,
+                                        data.data_ptr(), scales.data_ptr(), zeros.data_ptr(), _stream()),
+               "smaq_quantize_values")
+    lead = v.shape[:-1]
+    return data.reshape(*lead, -1), scales.reshape(*lead, -1), zeros.reshape(*lead, -1)
+
+
+def quantize_keys_bvq(k: torch.Tensor, E_blocks: torch.Tensor, centroids: torch.Tensor) -> torch.Tensor:
+    """``(..., D)`` keys -> uint8 block indices ``(..., D / block_dim)``."""
+    _cuda(k, E_blocks, centroids)
+    lib = _lib.load()
+    D = k.shape[-1]
+    nb, nc, bd = centroids.shape
+    kr = _rows(k)
+    n = kr.shape[0]
+    idx = torch.empty((n, nb), dtype=torch.uint8, device=k.device)
+    Eb = E_blocks.to(torch.float32).contiguous()
+    cf = centroids.to(torch.float32).contiguous()
+    _lib.check(lib.smaq_quantize_keys_bvq(kr.data_ptr(), dtype_code(k.dtype), n, D, Eb.data_ptr(),
+                                          cf.data_ptr(), bd, nc, idx.data_ptr(), _stream()),
+               "smaq_quantize_keys_bvq")
+    return idx.reshape(*k.shape[:-1], nb)
+
+
+def append(key: Optional[torch.Tensor], value: Optional[torch.Tensor], *, n_heads: int, slot_offset: int = 0,
+           slots: Optional[torch.Tensor] = None, page_size: int, key_format: int = SMAQ_KEYS_SCALAR,
+           key_bits: int = 3, E: Optional[torch.Tensor] = None, boundaries: Optional[torch.Tensor] = None,
+           E_blocks: Optional[torch.Tensor] = None, centroids: Optional[torch.Tensor] = None,
+           key_codes: Optional[torch.Tensor] = None, key_norms: Optional[torch.Tensor] = None,
+           value_bits: int = 2, group_size: int = 32, v_data: Optional[torch.Tensor] = None,
+           v_scales: Optional[torch.Tensor] = None, v_zeros: Optional[torch.Tensor] = None) -> None:
+    """Quantize a ``[T, H, D]`` chunk of keys and/or values into store rows (see include/smaq_b200.h)."""
+    _cuda(key, value, slots, E, boundaries, E_blocks, centroids, key_codes, key_norms, v_data)
+    lib = _lib.load()
+    ref = key if key is not None else value
+    if ref is None:
+        return
+    a = _lib.AppendArgs()
+    a.dtype = dtype_code(ref.dtype)
+    a.n_tokens = ref.shape[0]
+    a.n_heads = n_heads
+    a.head_dim = ref.shape[-1]
+    keep = []
+    if key is not None:
+        if key.stride(-1) != 1:
+            key = key.contiguous()
+        keep.append(key)
+        a.k = key.data_ptr()
+        a.k_stride_t, a.k_stride_h = key.stride(0), key.stride(1)
+        a.key_format = key_format
+        a.key_bits = key_bits
+        a.key_codes = _ptr(key_codes)
+        if key_format == SMAQ_KEYS_SCALAR:
+            Ef = E.to(torch.float32).contiguous()
+            bf = boundaries.to(torch.float32).contiguous()
+            keep += [Ef, bf]
+            a.E, a.boundaries = Ef.data_ptr(), bf.data_ptr()
+            a.key_norms = _ptr(key_norms)
+        else:
+            Eb = E_blocks.to(torch.float32).contiguous()
+            cf = centroids.to(torch.float32).contiguous()
+            keep += [Eb, cf]
+            a.E_blocks, a.centroids = Eb.data_ptr(), cf.data_ptr()
+            a.block_dim = centroids.shape[2]
+            a.n_centroids = centroids.shape[1]
+    if value is not None:
+        if value.stride(-1) != 1:
+            value = value.contiguous()
+        keep.append(value)
+        a.v = value.data_ptr()
+        a.v_stride_t, a.v_stride_h = value.stride(0), value.stride(1)
+        a.value_bits = value_bits
+        a.group_size = group_size
+        a.v_data, a.v_scales, a.v_zeros = _ptr(v_data), _ptr(v_scales), _ptr(v_zeros)
+    if slots is not None:
+        slots = slots.to(torch.int64).contiguous()
+        keep.append(slots)
+        a.slots = slots.data_ptr()
+    a.slot_offset = slot_offset
+    a.page_size = page_size
+    _lib.check(lib.smaq_append(a, _stream()), "smaq_append")
+
+
+# --------------------------------------------------------------------- decode
+def decode_workspace_bytes(batch: int, n_q_heads: int, n_kv_heads: int, head_dim: int, num_ctas: int = 0) -> int:
+    return int(_lib.load().smaq_decode_workspace_size(batch, n_q_heads, n_kv_heads, head_dim, num_ctas))
+
+
+def decode(q: torch.Tensor, *, n_kv_heads: int, key_format: int, key_codes: torch.Tensor,
+           v_data: torch.Tensor, v_scales: torch.Tensor, v_zeros: torch.Tensor, hist_len: torch.Tensor,
+           page_size: int, key_bits: int = 4, E_inv: Optional[torch.Tensor] = None,
+           centroids: Optional[torch.Tensor] = None, key_norms: Optional[torch.Tensor] = None,
+           value_bits: int = 2, group_size: int = 32, block_table: Optional[torch.Tensor] = None,
+           hist_total: Optional[torch.Tensor] = None, recent_k: Optional[torch.Tensor] = None,
+           recent_v: Optional[torch.Tensor] = None, recent_len: Optional[torch.Tensor] = None,
+           scale: Optional[float] = None, min_history: int = MIN_HISTORY, out: Optional[torch.Tensor] = None,
+           partial_out: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
+           num_ctas: int = 0, want_out: bool = True) -> Optional[torch.Tensor]:
+    """Batched hybrid decode attention.
+
+    ``q``: ``[B, Hq, D]``.  History streams are store rows ``[pages, Hkv, page_size, ...]``;
+    ``recent_k/v``: ``[B, W, Hkv, D]`` (stride 0 on B allowed).  Returns ``out [B, Hq, D]`` in
+    the query dtype (reference rounding), and/or fills ``partial_out [B, Hq, 2D+2]``.
+    """
+    _cuda(q, key_codes, v_data, hist_len, recent_k, block_table)
+    lib = _lib.load()
+    B, Hq, D = q.shape
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None and want_out:
+        out = torch.empty((B, Hq, D), dtype=q.dtype, device=q.device)
+    keep = [q]
+    a = _lib.DecodeArgs()
+    a.q, a.q_dtype, a.q_stride_b, a.q_stride_h = q.data_ptr(), dtype_code(q.dtype), q.stride(0), q.stride(1)
+    a.batch, a.n_q_heads, a.n_kv_heads, a.head_dim = B, Hq, n_kv_heads, D
+    a.scale = float(scale)
+    a.key_format = key_format
+    a.key_bits = key_bits
+    if key_format == SMAQ_KEYS_SCALAR:
+        Ei = E_inv.to(torch.float32).contiguous()
+        cf = centroids.to(torch.float32).contiguous()
+        keep += [Ei, cf]
+        a.E_inv, a.centroids = Ei.data_ptr(), cf.data_ptr()
+        a.key_norms = key_norms.data_ptr()
+        a.kv_dtype = dtype_code(key_norms.dtype)
+    else:
+        cf = centroids.to(torch.float32).contiguous()
+        keep.append(cf)
+        a.centroids = cf.data_ptr()
+        a.block_dim = centroids.shape[2]
+        a.n_centroids = centroids.shape[1]
+        a.kv_dtype = dtype_code(v_scales.dtype)
+    a.key_codes = key_codes.data_ptr()
+    a.v_data, a.v_scales, a.v_zeros = v_data.data_ptr(), v_scales.data_ptr(), v_zeros.data_ptr()
+    a.value_bits, a.group_size = value_bits, group_size
+    if block_table is not None:
+        bt = block_table.to(torch.int32)
+        if bt.stride(-1) != 1:
+            bt = bt.contiguous()
+        keep.append(bt)
+        a.block_table, a.bt_stride = bt.data_ptr(), bt.stride(0)
+    a.page_size = page_size
+    hl = hist_len.to(torch.int32).contiguous()
+    keep.append(hl)
+    a.hist_len = hl.data_ptr()
+    if hist_total is not None:
+        ht = hist_total.to(torch.int32).contiguous()
+        keep.append(ht)
+        a.hist_total = ht.data_ptr()
+    a.min_history = min_history
+    if recent_k is not None and recent_len is not None:
+        if recent_k.stride(-1) != 1 or recent_v.stride(-1) != 1 or recent_k.stride() != recent_v.stride():
+            recent_k, recent_v = recent_k.contiguous(), recent_v.contiguous()
+        rl = recent_len.to(torch.int32).contiguous()
+        keep += [recent_k, recent_v, rl]
+        a.recent_k, a.recent_v = recent_k.data_ptr(), recent_v.data_ptr()
+        a.recent_dtype = dtype_code(recent_k.dtype)
+        a.r_stride_b, a.r_stride_t, a.r_stride_h = recent_k.stride(0), recent_k.stride(1), recent_k.stride(2)
+        a.recent_len = rl.data_ptr()
+    if out is not None:
+        a.out, a.o_stride_b, a.o_stride_h = out.data_ptr(), out.stride(0), out.stride(1)
+    if partial_out is not None:
+        a.partial_out = partial_out.data_ptr()
+    need = decode_workspace_bytes(B, Hq, n_kv_heads, D, num_ctas)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty((max(need, 256),), dtype=torch.uint8, device=q.device)
+    keep.append(workspace)
+    a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel()
+    a.num_ctas = num_ctas
+    _lib.check(lib.smaq_decode(a, _stream()), "smaq_decode")
+    return out
+
+
+def merge_partials(partials: torch.Tensor, out_dtype: torch.dtype) -> torch.Tensor:
+    """``[R, B, Hq, 2D+2]`` fp32 partials -> ``[B, Hq, D]`` output."""
+    _cuda(partials)
+    lib = _lib.load()
+    R, B, Hq, W = partials.shape
+    D = (W - 2) // 2
+    p = partials.contiguous()
+    out = torch.empty((B, Hq, D), dtype=out_dtype, device=partials.device)
+    _lib.check(lib.smaq_merge_partials(p.data_ptr(), R, B, Hq, D, out.data_ptr(), dtype_code(out_dtype),
+                                       out.stride(0), out.stride(1), _stream()), "smaq_merge_partials")
+    return out

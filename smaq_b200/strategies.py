@@ -1,0 +1,168 @@
+"""Key quantization strategies on the hot path (same classes as smaq/strategies.py).
+
+Only the two strategies the decode kernels serve are provided:
+``SMAQFullMetricScalarStrategy`` (scalar codes, the reference's default key strategy) and
+``SMAQBlockVQStrategy``.  The RotationAdapter-based strategies of the reference (identity /
+diagonal metric, exact shadow) are outside this package's scope.
+"""
+
+from __future__ import annotations
+
+from typing import Any
+
+import torch
+
+from smaq_b200.block_vq import BlockVQQuantized, SMAQBlockVQ
+from smaq_b200.core import MetricStrategy, QuantizationStrategy
+from smaq_b200.quantizer import SMAQQuantized, SMAQQuantizer
+from smaq_b200.ssf import build_smaq_metric
+
+
+def _dev(device):
+    return torch.device(device) if device is not None else torch.device("cuda" if torch.cuda.is_available() else "cpu")
+
+
+class IdentityMetricStrategy(MetricStrategy):
+    name = "identity"
+
+    def __init__(self, dim: int, device: torch.device | None = None):
+        self.dim = dim
+        self.device = _dev(device)
+        self.sigma_q = torch.eye(dim, dtype=torch.float32, device=self.device)
+
+    def fit(self, calibration_queries: Any, calibration_keys: Any | None = None) -> "IdentityMetricStrategy":
+        return self
+
+    def export_state(self) -> dict[str, Any]:
+        return {"Sigma_q": self.sigma_q}
+
+
+def _centered_cov(q: torch.Tensor) -> torch.Tensor:
+    q = q.float()
+    qc = q - q.mean(dim=0, keepdim=True)
+    return qc.T @ qc / max(1, qc.shape[0])
+
+
+class SMAQFullMetricStrategy(MetricStrategy):
+    name = "smaq_full_metric"
+
+    def __init__(self, dim: int, Sigma_q: torch.Tensor | None = None, device: torch.device | None = None):
+        self.dim = dim
+        self.device = _dev(device)
+        self.sigma_q = Sigma_q if Sigma_q is not None else torch.eye(dim, dtype=torch.float32, device=self.device)
+        self.E, self.E_inv = build_smaq_metric(self.sigma_q.to(torch.float32), c=5.0)
+
+    def fit(self, calibration_queries: Any, calibration_keys: Any | None = None) -> "SMAQFullMetricStrategy":
+        self.sigma_q = _centered_cov(calibration_queries)
+        self.E, self.E_inv = build_smaq_metric(self.sigma_q, c=5.0)
+        return self
+
+    def export_state(self) -> dict[str, Any]:
+        return {"Sigma_q": self.sigma_q, "E": self.E, "E_inv": self.E_inv}
+
+
+class SMAQDiagonalMetricState(MetricStrategy):
+    name = "smaq_diagonal_metric"
+
+    def __init__(self, dim: int, Sigma_q: torch.Tensor | None = None, device: torch.device | None = None):
+        self.dim = dim
+        self.device = _dev(device)
+        self.sigma_q = Sigma_q if Sigma_q is not None else torch.eye(dim, dtype=torch.float32, device=self.device)
+
+    def fit(self, calibration_queries: Any, calibration_keys: Any | None = None) -> "SMAQDiagonalMetricState":
+        self.sigma_q = _centered_cov(calibration_queries)
+        return self
+
+    def export_state(self) -> dict[str, Any]:
+        return {"Sigma_q": self.sigma_q}
+
+
+class SMAQFullMetricScalarStrategy(QuantizationStrategy):
+    """Scalar metric-aware key codes (smaq/strategies.py:100-168)."""
+
+    name = "smaq_full_metric_scalar"
+    metric_name = "smaq_full_metric"
+    quantization_name = "scalar"
+
+    def __init__(self, dim: int, bits: int = 3, Sigma_q: torch.Tensor | None = None,
+                 device: torch.device | None = None, dtype: torch.dtype = torch.float32):
+        self.quantizer = SMAQQuantizer(dim=dim, bits=bits, Sigma_q=Sigma_q, device=device, dtype=dtype)
+        self.bits = bits
+
+    @property
+    def supports_kernel(self) -> bool:
+        return True
+
+    def fit(self, calibration_queries: Any, calibration_keys: Any | None = None) -> "SMAQFullMetricScalarStrategy":
+        self.quantizer.fit(calibration_queries)
+        return self
+
+    def quantize(self, keys: Any) -> Any:
+        return self.quantizer.quantize(keys)
+
+    def dequantize(self, quantized: Any) -> Any:
+        return self.quantizer.dequantize(quantized)
+
+    def attention_score(self, query: Any, quantized: Any, scale: float | None = None, **kwargs: Any) -> Any:
+        return self.quantizer.attention_score(query, quantized, scale=scale,
+                                              use_kernel=kwargs.get("use_kernel", False))
+
+    def flatten_quantized(self, quantized: SMAQQuantized) -> SMAQQuantized:
+        ix, nm = quantized.indices, quantized.norms
+        return SMAQQuantized(indices=ix.reshape(-1, ix.shape[-2], ix.shape[-1]).contiguous(),
+                             norms=nm.reshape(-1, nm.shape[-1]).contiguous(), bits=quantized.bits)
+
+    def concat_quantized(self, chunks: list[SMAQQuantized]) -> SMAQQuantized:
+        return SMAQQuantized(indices=torch.cat([c.indices for c in chunks], dim=-2),
+                             norms=torch.cat([c.norms for c in chunks], dim=-1), bits=chunks[0].bits)
+
+    def select_head(self, quantized: SMAQQuantized, head_idx: int) -> SMAQQuantized:
+        return SMAQQuantized(indices=quantized.indices[head_idx], norms=quantized.norms[head_idx],
+                             bits=quantized.bits)
+
+    def memory_bytes(self, quantized: SMAQQuantized) -> int:
+        # the reference's accounting: one byte per packed code byte, two per norm
+        return quantized.indices.nelement() + quantized.norms.nelement() * 2
+
+
+class SMAQBlockVQStrategy(QuantizationStrategy):
+    """Block-VQ key codes (smaq/strategies.py:195-255)."""
+
+    name = "smaq_block_vq"
+    metric_name = "smaq_full_metric"
+    quantization_name = "block_vq"
+
+    def __init__(self, head_dim: int, block_dim: int = 8, n_centroids: int = 256, c: float = 5.0,
+                 device: torch.device | None = None, dtype: torch.dtype = torch.float32):
+        self.quantizer = SMAQBlockVQ(head_dim=head_dim, block_dim=block_dim, n_centroids=n_centroids, c=c,
+                                     device=device, dtype=dtype)
+
+    def fit(self, calibration_queries: Any, calibration_keys: Any | None = None) -> "SMAQBlockVQStrategy":
+        keys = calibration_keys if calibration_keys is not None else calibration_queries
+        self.quantizer.fit(keys, calibration_queries)
+        return self
+
+    def quantize(self, keys: Any) -> Any:
+        return self.quantizer.quantize(keys)
+
+    def dequantize(self, quantized: Any) -> Any:
+        return self.quantizer.dequantize(quantized)
+
+    def attention_score(self, query: Any, quantized: Any, scale: float | None = None, **kwargs: Any) -> Any:
+        return self.quantizer.attention_score(query, quantized, scale=scale)
+
+    def flatten_quantized(self, quantized: BlockVQQuantized) -> BlockVQQuantized:
+        ix = quantized.indices
+        return BlockVQQuantized(indices=ix.reshape(-1, ix.shape[-2], ix.shape[-1]).contiguous(),
+                                n_blocks=quantized.n_blocks, block_dim=quantized.block_dim)
+
+    def concat_quantized(self, chunks: list[BlockVQQuantized]) -> BlockVQQuantized:
+        return BlockVQQuantized(indices=torch.cat([c.indices for c in chunks], dim=-2),
+                                n_blocks=chunks[0].n_blocks, block_dim=chunks[0].block_dim)
+
+    def select_head(self, quantized: BlockVQQuantized, head_idx: int) -> BlockVQQuantized:
+        return BlockVQQuantized(indices=quantized.indices[head_idx], n_blocks=quantized.n_blocks,
+                                block_dim=quantized.block_dim)
+
+    def memory_bytes(self, quantized: BlockVQQuantized) -> int:
+        return quantized.indices.nelement() * quantized.indices.element_size()

@@ -1,0 +1,49 @@
+"""The C-ABI library loads and exports every symbol include/smaq_b200.h declares (no GPU calls)."""
+
+import os
+import re
+
+from conftest import REPO
+
+
+def declared_symbols():
+    src = open(os.path.join(REPO, "include", "smaq_b200.h")).read()
+    return sorted(set(re.findall(r"\b(smaq_[a-z_]+)\s*\(", src)))
+
+
+def test_library_exports_header_symbols():
+    from smaq_b200 import _lib, build
+    build.build()
+    lib = _lib.load()
+    decl = declared_symbols()
+    assert decl, "no declarations found"
+    missing = [s for s in decl if not hasattr(lib, s)]
+    assert not missing, missing
+    assert set(decl) == set(_lib.EXPORTS)
+    assert lib.smaq_abi_version() == 1
+
+
+def test_invalid_arguments_are_reported_without_a_gpu():
+    """Argument validation runs on the host and fails with a message, before any CUDA call."""
+    import ctypes
+    from smaq_b200 import _lib
+    lib = _lib.load()
+    a = _lib.AppendArgs()
+    a.n_tokens, a.n_heads, a.head_dim, a.page_size = 4, 1, 128, 4
+    a.dtype = 7
+    st = lib.smaq_append(ctypes.byref(a), None)
+    assert st == 1
+    assert b"dtype" in lib.smaq_last_error()
+    d = _lib.DecodeArgs()
+    d.batch, d.n_q_heads, d.n_kv_heads, d.head_dim = 1, 6, 4, 128
+    assert lib.smaq_decode(ctypes.byref(d), None) == 1
+    assert b"head counts" in lib.smaq_last_error()
+    assert lib.smaq_decode_workspace_size(2, 32, 8, 128, 100) > 0
+
+
+def test_cpu_tensors_raise():
+    import pytest
+    import torch
+    from smaq_b200 import ops
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        ops.quantize_values(torch.zeros(4, 128))

@@ -1,0 +1,153 @@
+"""Batched / paged decode and append through slot mappings, checked against the oracle."""
+
+import numpy as np
+import pytest
+
+from oracle import smaq_oracle as O
+from smaq_b200 import synthetic as syn
+
+pytestmark = pytest.mark.gpu
+D = 128
+
+
+def tn(t):
+    import torch
+    if t.dtype in (torch.bfloat16, torch.float16):
+        t = t.float()
+    return t.cpu().numpy()
+
+
+def scalar_tables(bits, dev):
+    import torch
+    from smaq_b200.quantizer import SMAQQuantizer
+    qz = SMAQQuantizer(D, bits=bits, device=dev)
+    qz.fit(torch.from_numpy(syn.calibration_queries(512, D)).to(dev))
+    return qz
+
+
+def random_codebook(dev, seed=7):
+    import torch
+    rng = np.random.default_rng(seed)
+    Eb = (np.eye(8)[None] + 0.1 * rng.standard_normal((16, 8, 8))).astype(np.float32)
+    C = rng.standard_normal((16, 256, 8)).astype(np.float32)
+    dec = rng.standard_normal((16, 256, 8)).astype(np.float32) * 0.5
+    return [torch.from_numpy(x).to(dev) for x in (Eb, C, dec)]
+
+
+def build_paged(dev, kind, bits, B, Hkv, hist, page_size, dtype, seed):
+    """Quantize per-sequence histories into a shuffled paged store via slot mappings."""
+    import torch
+    from smaq_b200 import ops
+    from smaq_b200._lib import SMAQ_KEYS_BVQ, SMAQ_KEYS_SCALAR
+    rng = np.random.default_rng(seed)
+    pages_per = [(int(n) + page_size - 1) // page_size for n in hist]
+    n_pages = max(1, sum(pages_per))
+    perm = rng.permutation(n_pages)
+    maxp = max(1, max(pages_per))
+    bt = np.zeros((B, maxp), np.int32)
+    o = 0
+    for b in range(B):
+        bt[b, :pages_per[b]] = perm[o:o + pages_per[b]]
+        o += pages_per[b]
+    P = ops.packed_dim(D, bits) if kind == "scalar" else 16
+    tdt = getattr(torch, dtype)
+    st = {
+        "codes": torch.zeros((n_pages, Hkv, page_size, P), dtype=torch.uint8, device=dev),
+        "norms": torch.zeros((n_pages, Hkv, page_size), dtype=tdt, device=dev),
+        "vdata": torch.zeros((n_pages, Hkv, page_size, D // 4), dtype=torch.uint8, device=dev),
+        "vs": torch.zeros((n_pages, Hkv, page_size, D // 32), dtype=tdt, device=dev),
+        "vz": torch.zeros((n_pages, Hkv, page_size, D // 32), dtype=tdt, device=dev),
+        "bt": torch.from_numpy(bt).to(dev),
+    }
+    raw = []
+    for b in range(B):
+        n = int(hist[b])
+        k = torch.from_numpy(syn.keys((n, Hkv), D, seed=seed * 100 + b)).to(dev).to(tdt)
+        v = torch.from_numpy(syn.values((n, Hkv), D, seed=seed * 100 + 50 + b)).to(dev).to(tdt)
+        t = np.arange(n)
+        slots = torch.from_numpy(bt[b, t // page_size].astype(np.int64) * page_size + t % page_size).to(dev)
+        raw.append((k, v, slots))
+    return st, raw
+
+
+def run_case(cuda, kind, bits, B, Hkv, G, hist, recent, page_size, dtype, seed, num_ctas=0):
+    import torch
+    from smaq_b200 import ops
+    from smaq_b200._lib import SMAQ_KEYS_BVQ, SMAQ_KEYS_SCALAR
+    tdt = getattr(torch, dtype)
+    qd = {"float32": "fp32", "bfloat16": "bf16", "float16": "fp16"}[dtype]
+    st, raw = build_paged(cuda, kind, bits, B, Hkv, hist, page_size, dtype, seed)
+    if kind == "scalar":
+        qz = scalar_tables(bits, cuda)
+        E, E_inv, cent, bnd = qz.E, qz.E_inv, qz.centroids, qz.decision_boundaries
+    else:
+        Eb, C, dec = random_codebook(cuda)
+    for b, (k, v, slots) in enumerate(raw):
+        if kind == "scalar":
+            ops.append(k, v, n_heads=Hkv, slots=slots, page_size=page_size, key_format=SMAQ_KEYS_SCALAR,
+                       key_bits=bits, E=E, boundaries=bnd, key_codes=st["codes"], key_norms=st["norms"],
+                       v_data=st["vdata"], v_scales=st["vs"], v_zeros=st["vz"])
+        else:
+            ops.append(k, v, n_heads=Hkv, slots=slots, page_size=page_size, key_format=SMAQ_KEYS_BVQ,
+                       E_blocks=Eb, centroids=C, key_codes=st["codes"], v_data=st["vdata"],
+                       v_scales=st["vs"], v_zeros=st["vz"])
+    W = max(1, int(max(recent)))
+    rk = torch.from_numpy(syn.keys((B, W, Hkv), D, seed=seed + 7)).to(cuda).to(tdt)
+    rv = torch.from_numpy(syn.values((B, W, Hkv), D, seed=seed + 8)).to(cuda).to(tdt)
+    q = torch.from_numpy(syn.queries((B, Hkv * G), D, seed=seed + 9)).to(cuda).to(tdt)
+    hl = torch.tensor(hist, dtype=torch.int32, device=cuda)
+    rl = torch.tensor(recent, dtype=torch.int32, device=cuda)
+    kw = dict(key_format=SMAQ_KEYS_SCALAR, key_bits=bits, E_inv=E_inv, centroids=cent,
+              key_norms=st["norms"]) if kind == "scalar" else dict(key_format=SMAQ_KEYS_BVQ, centroids=dec)
+    out = ops.decode(q, n_kv_heads=Hkv, key_codes=st["codes"], v_data=st["vdata"], v_scales=st["vs"],
+                     v_zeros=st["vz"], hist_len=hl, page_size=page_size, block_table=st["bt"],
+                     recent_k=rk, recent_v=rv, recent_len=rl, num_ctas=num_ctas, **kw)
+    got = tn(out)
+    # oracle per sequence, from the GPU-written rows (isolates decode from quantize parity)
+    codes, norms = tn(st["codes"]), tn(st["norms"])
+    vdata, vs, vz = tn(st["vdata"]), tn(st["vs"]), tn(st["vz"])
+    bt = tn(st["bt"])
+    worst = 0.0
+    for b in range(B):
+        n = int(hist[b])
+        t = np.arange(n)
+        pg = bt[b, t // page_size]
+        off = t % page_size
+        c_b = codes[pg, :, off].transpose(1, 0, 2)          # [Hkv, n, P]
+        if kind == "scalar":
+            K = O.scalar_score_keys(c_b, norms[pg, :, off].T, bits, tn(E_inv), tn(cent), D) if n else None
+        else:
+            K = O.bvq_dequantize(c_b.astype(np.int64), tn(dec)) if n else None
+        V = O.dequantize_values(vdata[pg, :, off].transpose(1, 0, 2), vs[pg, :, off].transpose(1, 0, 2),
+                                vz[pg, :, off].transpose(1, 0, 2), 2, 32) if n else None
+        r = int(recent[b])
+        ref, _, _ = O.hybrid_attention(tn(q[b:b + 1]), qd, K, V, tn(rk[b, :r]) if r else None,
+                                       tn(rv[b, :r]) if r else None, Hkv * G, Hkv)
+        e = O.rel_l2(got[b:b + 1], ref)
+        worst = max(worst, e)
+    assert worst <= (1e-5 if qd == "fp32" else 2e-3), worst
+    return got
+
+
+@pytest.mark.parametrize("kind,bits", [("scalar", 4), ("scalar", 3), ("scalar", 2), ("bvq", 0)])
+def test_paged_decode_bf16(cuda, kind, bits):
+    hist = [700, 15, 16, 0, 333, 1]
+    recent = [64, 3, 0, 17, 1, 0]
+    run_case(cuda, kind, bits, B=6, Hkv=4, G=7, hist=hist, recent=recent, page_size=16, dtype="bfloat16",
+             seed=11)
+
+
+@pytest.mark.parametrize("kind,bits", [("scalar", 4), ("bvq", 0)])
+def test_paged_decode_fp32_gqa8(cuda, kind, bits):
+    run_case(cuda, kind, bits, B=3, Hkv=2, G=8, hist=[513, 40, 1000], recent=[5, 128, 0], page_size=16,
+             dtype="float32", seed=12)
+
+
+@pytest.mark.parametrize("num_ctas", [1, 3, 29, 2000])
+def test_stream_k_partition_invariance(cuda, num_ctas):
+    """Any number of CTAs (one slice, many splits, more CTAs than tokens) gives the same answer."""
+    a = run_case(cuda, "bvq", 0, B=4, Hkv=2, G=4, hist=[900, 300, 17, 64], recent=[128, 0, 9, 1],
+                 page_size=16, dtype="bfloat16", seed=13, num_ctas=num_ctas)
+    b = run_case(cuda, "bvq", 0, B=4, Hkv=2, G=4, hist=[900, 300, 17, 64], recent=[128, 0, 9, 1],
+                 page_size=16, dtype="bfloat16", seed=13, num_ctas=0)
+    assert O.rel_l2(a, b) < 1e-3
