@@ -23,7 +23,8 @@ namespace smaq {
 
 constexpr int DEC_WARPS = 8;
 constexpr int DEC_THREADS = DEC_WARPS * 32;
-constexpr int RECENT_COST = 8;  // exact bf16 K+V token = 512 B vs 48-114 B for a compressed token
+constexpr int RECENT_COST = 8;
+constexpr int DEC_MAX_CTAS_PER_SM = 8;  // grid cap when the caller lets the library choose  // exact bf16 K+V token = 512 B vs 48-114 B for a compressed token
 
 struct DecodeParams {
   const void* q;
@@ -483,6 +484,7 @@ static int launch_decode_t(DecodeParams& p, int grid_req, cudaStream_t s, int* g
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, DEC_THREADS, sm);
     if (e != cudaSuccess) return cuda_status(e, "decode occupancy");
     if (occ < 1) occ = 1;
+    if (occ > DEC_MAX_CTAS_PER_SM) occ = DEC_MAX_CTAS_PER_SM;
     grid = num_sms() * occ;
   }
   *grid_out = grid;
@@ -534,7 +536,7 @@ extern "C" size_t smaq_decode_workspace_size(int batch, int n_q_heads, int n_kv_
   if (batch <= 0 || n_kv_heads <= 0 || n_q_heads % n_kv_heads) return 0;
   const int n_seg = 2 * batch * n_kv_heads;
   const int G = n_q_heads / n_kv_heads;
-  const int grid = num_ctas > 0 ? num_ctas : num_sms() * 2;
+  const int grid = num_ctas > 0 ? num_ctas : num_sms() * DEC_MAX_CTAS_PER_SM;
   return plan_bytes(n_seg) + sizeof(float) * size_t(grid + n_seg) * G * (head_dim + 2);
 }
 
