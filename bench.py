@@ -1,0 +1,369 @@
+"""Benchmark: compressed-KV decode attention (SMAQ hot path) on B200.
+
+Default workload: Llama-3-8B KV shape -- 32 layers, 32 query / 8 KV
+heads, head_dim 128, bf16 -- batch 16 sequences x 32768 compressed history tokens (block-VQ
+keys: 8-dim blocks, 256-entry fp16-valued codebook k-means-fit on 16K calibration keys; 2-bit
+values in groups of 32) plus a 128-token exact bf16 window, one decode token per sequence.
+A step = the attention of all 32 layers for one decode token of every sequence.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+N > 1 (torchrun, one rank per GPU): every rank serves its own 16 sequences (sequences are
+independent units; no collective on the data path) -> ``scaling: weak``.
+
+Inputs: seeded synthetic data with the spectral key distribution (no dataset).  The KV cache
+of one step (8.9 GB) is far larger than L2 (126 MB), so no explicit L2 flush is needed.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "compressed-KV decode attn tokens/s & HBM GB/s (% of roofline) at 32K/128K ctx"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="smaq_b200", choices=["smaq_b200", "reference"])
+    ap.add_argument("--batch", type=int, default=16)
+    ap.add_argument("--ctx", type=int, default=32768)
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--window", type=int, default=128)
+    ap.add_argument("--hq", type=int, default=32)
+    ap.add_argument("--hkv", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def config_of(a):
+    return {"workload": "cfg1_llama3_8b_bvq_decode", "layers": a.layers, "batch_per_gpu": a.batch,
+            "n_q_heads": a.hq, "n_kv_heads": a.hkv, "head_dim": 128, "history_tokens": a.ctx,
+            "window_tokens": a.window, "keys": "block-VQ 8x256 (fp16 codebook)", "values": "2-bit g32",
+            "l2": "inputs larger than L2 (no flush)"}
+
+
+def bytes_per_layer(a) -> int:
+    """Algorithmic HBM bytes of one layer's decode (roofline)."""
+    D = 128
+    hist = a.ctx * (D // 8 + D // 4 + 2 * 2 * (D // 32))      # 16 B idx + 32 B codes + 8 B scales + 8 B zeros
+    recent = a.window * 2 * D * 2                              # exact bf16 K and V
+    qo = a.hq * D * 2 * 2                                      # query in, output out (bf16)
+    return a.batch * (a.hkv * (hist + recent) + qo)
+
+
+# ----------------------------------------------------------------------------- clocks
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power)}
+
+
+# ----------------------------------------------------------------------------- workload
+def make_codebook(dev):
+    """256-entry block-VQ codebook fit by seeded k-means on 16K calibration keys, fp16 values."""
+    import torch
+    from smaq_b200 import synthetic as syn
+    from smaq_b200.block_vq import SMAQBlockVQ
+    vq = SMAQBlockVQ(128, device=dev)
+    ck = torch.from_numpy(syn.keys((16384,), 128, seed=21)).to(dev)
+    cq = torch.from_numpy(syn.calibration_queries(16384, 128, seed=syn.SEED_CAL_Q)).to(dev)
+    vq.fit(ck, cq, seed=syn.SEED_KMEANS)
+    for name in ("E_blocks", "E_inv_blocks", "centroids", "decoded_centroids"):
+        getattr(vq, name).copy_(getattr(vq, name).half().float())
+    return vq
+
+
+def spectral_keys_gpu(n, gen, U, lam_sqrt, outl, dtype):
+    import torch
+    z = torch.randn((n, 128), generator=gen, device=U.device, dtype=torch.float32) * lam_sqrt
+    x = z @ U.T
+    x[:, outl] *= 8.0
+    return x.to(dtype)
+
+
+def build_layers(a, dev, vq, seed0: int):
+    """Per layer: batched store rows [B, Hkv, ctx, ...], recent window, queries."""
+    import torch
+    from smaq_b200 import ops, synthetic as syn
+    from smaq_b200._lib import SMAQ_KEYS_BVQ, SMAQ_LAYOUT_DECODE
+    U_np, outl = syn.basis(128)
+    U = torch.from_numpy(U_np.astype(np.float32)).to(dev)
+    lam = torch.from_numpy(np.sqrt(syn.spectrum(128)).astype(np.float32)).to(dev)
+    outl = torch.from_numpy(outl).to(dev)
+    B, H, T, D, W = a.batch, a.hkv, a.ctx, 128, a.window
+    bf = torch.bfloat16
+    layers = []
+    for li in range(a.layers):
+        gen = torch.Generator(device=dev).manual_seed(seed0 * 1000 + li)
+        L = {
+            "codes": torch.empty((B, H, T, 16), dtype=torch.uint8, device=dev),
+            "vdata": torch.empty((B, H, T, 32), dtype=torch.uint8, device=dev),
+            "vs": torch.empty((B, H, T, 4), dtype=bf, device=dev),
+            "vz": torch.empty((B, H, T, 4), dtype=bf, device=dev),
+        }
+        for b in range(B):
+            k = spectral_keys_gpu(T * H, gen, U, lam, outl, bf).reshape(T, H, D)
+            v = torch.randn((T, H, D), generator=gen, device=dev, dtype=torch.float32).to(bf)
+            ops.append(k, v, n_heads=H, slot_offset=b * T, page_size=T, key_format=SMAQ_KEYS_BVQ,
+                       E_blocks=vq.E_blocks, centroids=vq.centroids, key_codes=L["codes"], v_data=L["vdata"],
+                       v_scales=L["vs"], v_zeros=L["vz"], layout=SMAQ_LAYOUT_DECODE)
+        L["rk"] = spectral_keys_gpu(B * W * H, gen, U, lam, outl, bf).reshape(B, W, H, D)
+        L["rv"] = torch.randn((B, W, H, D), generator=gen, device=dev, dtype=torch.float32).to(bf)
+        L["q"] = (torch.randn((B, a.hq, D), generator=gen, device=dev, dtype=torch.float32)).to(bf)
+        L["out"] = torch.empty((B, a.hq, D), dtype=bf, device=dev)
+        layers.append(L)
+    torch.cuda.synchronize()
+    return layers
+
+
+def decode_layer(a, L, vq, hl, rl, ws, q=None, out=None):
+    from smaq_b200 import ops
+    from smaq_b200._lib import SMAQ_KEYS_BVQ, SMAQ_LAYOUT_DECODE
+    return ops.decode(L["q"] if q is None else q, n_kv_heads=a.hkv, key_format=SMAQ_KEYS_BVQ,
+                      centroids=vq.decoded_centroids, key_codes=L["codes"], v_data=L["vdata"], v_scales=L["vs"],
+                      v_zeros=L["vz"], hist_len=hl, page_size=a.ctx, recent_k=L["rk"], recent_v=L["rv"],
+                      recent_len=rl, out=L["out"] if out is None else out, workspace=ws, layout=SMAQ_LAYOUT_DECODE)
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def cpu_sample(a, seconds_cap: float = 20.0):
+    """Time the CPU port of the reference path (oracle, fp32 like the reference's torch ops) on
+    one layer x one sequence, and scale to the metric's unit."""
+    from oracle import smaq_oracle as O
+    from smaq_b200 import synthetic as syn
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max([i.get("num_threads", 1) for i in threadpool_info()] + [1])
+    except Exception:
+        cores = os.cpu_count() or 1
+    rng = np.random.default_rng(5)
+    H, T, D, W = a.hkv, a.ctx, 128, a.window
+    idx = rng.integers(0, 256, size=(H, T, 16))
+    dec = rng.standard_normal((16, 256, 8)).astype(np.float32)
+    vdata = rng.integers(0, 256, size=(H, T, 32), dtype=np.uint8)
+    vs = np.abs(rng.standard_normal((H, T, 4))).astype(np.float32)
+    vz = rng.standard_normal((H, T, 4)).astype(np.float32)
+    q = syn.queries((1, a.hq), D, seed=9)
+    rk = syn.keys((W, H), D, seed=10)
+    rv = syn.values((W, H), D, seed=11)
+    runs = []
+    t_end = time.perf_counter() + seconds_cap
+    while True:
+        t0 = time.perf_counter()
+        K = O.bvq_dequantize(idx, dec, work=np.float32)           # the reference materialises k_hat
+        V = O.dequantize_values(vdata, vs, vz, 2, 32)
+        O.hybrid_attention(q, "bf16", K, V, rk, rv, a.hq, H, work=np.float32)
+        runs.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end or len(runs) >= 5:
+            break
+    t = statistics.median(runs)
+    step_s = t * a.layers * a.batch                                 # one layer x one sequence -> full step
+    return {"value": a.batch / step_s, "unit": "tokens/s", "cores": int(cores), "kind": "port",
+            "sample": f"1 layer x 1 sequence ({T} history + {W} window tokens, {H} kv heads), "
+                      f"median of {len(runs)} runs = {t*1e3:.1f} ms, scaled x{a.layers * a.batch}"}
+
+
+def run_reference(a, rank: int, world: int):
+    if rank != 0:
+        return
+    for _ in range(max(0, a.warmup)):
+        pass
+    vals = []
+    info = None
+    for _ in range(max(1, a.steps)):
+        info = cpu_sample(a, seconds_cap=max(2.0, 60.0 / max(1, a.steps)))
+        vals.append(info["value"])
+    v = statistics.median(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * a.batch / v, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config_of(a),
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": info["cores"], "kind": "port",
+                             "sample": info["sample"]},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    a = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        run_reference(a, rank, world)
+        return
+    import torch
+    import torch.distributed as dist
+    from smaq_b200 import build
+    build.build()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    vq = make_codebook(dev)
+    layers = build_layers(a, dev, vq, seed0=rank + 1)
+    hl = torch.full((a.batch,), a.ctx, dtype=torch.int32, device=dev)
+    rl = torch.full((a.batch,), a.window, dtype=torch.int32, device=dev)
+    from smaq_b200 import ops
+    ws = torch.empty(ops.decode_workspace_bytes(a.batch, a.hq, a.hkv, 128), dtype=torch.uint8, device=dev)
+
+    def step():
+        for L in layers:
+            decode_layer(a, L, vq, hl, rl, ws)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(max(3, a.warmup)):
+        step()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1) / a.steps
+    ck = clocks.stop()
+    # per-layer decode call time (plan + decode + merge kernels) for the roofline
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in layers]
+    for _ in range(2):
+        for L, (s0, s1) in zip(layers, evs):
+            s0.record()
+            decode_layer(a, L, vq, hl, rl, ws)
+            s1.record()
+        torch.cuda.synchronize()
+    layer_ms = statistics.mean(s0.elapsed_time(s1) for s0, s1 in evs)
+    # end to end through the public API with host buffers: H2D queries, decode, D2H outputs
+    hq = [torch.empty_like(L["q"], device="cpu").pin_memory() for L in layers]
+    for h, L in zip(hq, layers):
+        h.copy_(L["q"].cpu())
+    ho = [torch.empty_like(L["out"], device="cpu").pin_memory() for L in layers]
+    dq = [torch.empty_like(L["q"]) for L in layers]
+
+    def e2e_step():
+        for i, L in enumerate(layers):
+            dq[i].copy_(hq[i], non_blocking=True)
+            decode_layer(a, L, vq, hl, rl, ws, q=dq[i])
+            ho[i].copy_(L["out"], non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0.record()
+    for _ in range(a.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / a.steps
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms, layer_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms, layer_ms = t.tolist()
+    bpl = bytes_per_layer(a)
+    peak_gbs = None
+    peak_src = "fallback 6650 GB/s"
+    try:
+        peak_gbs = float(json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))["hbm_gbs"])
+        peak_src = "measured"
+    except Exception:
+        peak_gbs = 6650.0
+    achieved = bpl / (layer_ms * 1e-3) / 1e9
+    h2d = sum(t.numel() * t.element_size() for t in hq)
+    d2h = sum(t.numel() * t.element_size() for t in ho)
+    if rank == 0:
+        tokens = a.batch * world
+        line = {
+            "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "steps": a.steps, "warmup": max(3, a.warmup), "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32-accum/bf16-io", "data": "synthetic",
+            "config": config_of(a),
+            "hbm_gbs": bpl * a.layers / (ms * 1e-3) / 1e9,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s",
+                         "frac": achieved / peak_gbs, "traffic": None, "peak_source": peak_src,
+                         "kernel": "smaq_decode (plan+decode+merge) per layer",
+                         "algorithmic_bytes_per_launch": bpl},
+            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": 3 * a.layers * a.steps,
+            "clocks": ck,
+        }
+        if world == 1 and not a.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_sample(a)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

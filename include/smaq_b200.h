@@ -31,8 +31,17 @@
  *   s = slots ? slots[t] : slot_offset + t,   page = s / page_size,
  *   row = (page * n_kv_heads + h) * page_size + s % page_size.
  * A contiguous per-head store [n_kv_heads, capacity] is page_size = capacity
- * with one page.  Decode reads token t of sequence b from
- *   page = block_table ? block_table[b * bt_stride + t / page_size] : b.
+ * with one page (SMAQ_LAYOUT_DECODE stores need page_size % 16 == 0).  Decode reads token t of
+ * sequence b from page = block_table ? block_table[b * bt_stride + t / page_size] : b.
+ *
+ * SMAQ_LAYOUT_DECODE permutes bytes inside rows (same bits, same row sizes):
+ *   block-VQ indices: each aligned group of 8 rows (128 bytes) stores, at byte
+ *     (b % 8) * 16 + ((row ^ b) % 8) * 2 + b / 8, the index of block b of that row, so one
+ *     16-byte load yields the index pair (b, b + 8) of eight consecutive tokens (in an
+ *     order XOR-swizzled by b % 8);
+ *   2-bit values (head_dim 128): byte 4 * g + j of a row holds reference byte 8 * j + g
+ *     (g < 8, j < 4), so each 32-bit word carries one byte of every value group.
+ * Reference-layout bytes are recovered by the inverse permutation.
  */
 #ifndef SMAQ_B200_H_
 #define SMAQ_B200_H_
@@ -50,6 +59,11 @@ extern "C" {
 enum { SMAQ_F32 = 0, SMAQ_BF16 = 1, SMAQ_F16 = 2 };
 /* key formats */
 enum { SMAQ_KEYS_NONE = 0, SMAQ_KEYS_SCALAR = 1, SMAQ_KEYS_BVQ = 2 };
+/* store row layouts */
+enum {
+  SMAQ_LAYOUT_REFERENCE = 0, /* bytes exactly as the reference packs them */
+  SMAQ_LAYOUT_DECODE = 1     /* decode-friendly byte order inside each row group (see below) */
+};
 /* status codes */
 enum {
   SMAQ_OK = 0,
@@ -97,6 +111,7 @@ typedef struct smaq_append_args {
   uint8_t* v_data;           /* rows of D*bits/8 bytes */
   void* v_scales;            /* rows of D/group_size `dtype` elements */
   void* v_zeros;             /* rows of D/group_size `dtype` elements */
+  int layout;                /* SMAQ_LAYOUT_REFERENCE or SMAQ_LAYOUT_DECODE */
 } smaq_append_args;
 
 /* Quantize a chunk of keys and/or values straight into store rows. */
@@ -158,6 +173,7 @@ typedef struct smaq_decode_args {
   void* workspace;
   size_t workspace_bytes;
   int num_ctas;              /* 0: one wave over the device's SMs */
+  int layout;                /* row layout of the history streams */
 } smaq_decode_args;
 
 /* Bytes of workspace smaq_decode needs for these shapes (host-only computation). */

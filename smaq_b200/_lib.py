@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(_HERE, "libsmaq_b200.so")
 
 SMAQ_F32, SMAQ_BF16, SMAQ_F16 = 0, 1, 2
 SMAQ_KEYS_NONE, SMAQ_KEYS_SCALAR, SMAQ_KEYS_BVQ = 0, 1, 2
+SMAQ_LAYOUT_REFERENCE, SMAQ_LAYOUT_DECODE = 0, 1
 STATUS = {0: "OK", 1: "INVALID", 2: "UNSUPPORTED", 3: "CUDA", 4: "WORKSPACE", 5: "DEVICE"}
 
 # every symbol include/smaq_b200.h declares (checked by the CPU test suite)
@@ -36,6 +37,7 @@ class AppendArgs(C.Structure):
         ("key_format", i32), ("key_bits", i32), ("E", vp), ("boundaries", vp), ("E_blocks", vp),
         ("centroids", vp), ("block_dim", i32), ("n_centroids", i32), ("key_codes", vp), ("key_norms", vp),
         ("value_bits", i32), ("group_size", i32), ("v_data", vp), ("v_scales", vp), ("v_zeros", vp),
+        ("layout", i32),
     ]
 
 
@@ -50,7 +52,7 @@ class DecodeArgs(C.Structure):
         ("min_history", i32), ("recent_k", vp), ("recent_v", vp), ("recent_dtype", i32),
         ("r_stride_b", i64), ("r_stride_t", i64), ("r_stride_h", i64), ("recent_len", vp),
         ("out", vp), ("o_stride_b", i64), ("o_stride_h", i64), ("partial_out", vp),
-        ("workspace", vp), ("workspace_bytes", C.c_size_t), ("num_ctas", i32),
+        ("workspace", vp), ("workspace_bytes", C.c_size_t), ("num_ctas", i32), ("layout", i32),
     ]
 
 

@@ -18,56 +18,9 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "decode_common.cuh"
 
 namespace smaq {
-
-constexpr int DEC_WARPS = 8;
-constexpr int DEC_THREADS = DEC_WARPS * 32;
-constexpr int RECENT_COST = 8;
-constexpr int DEC_MAX_CTAS_PER_SM = 8;  // grid cap when the caller lets the library choose  // exact bf16 K+V token = 512 B vs 48-114 B for a compressed token
-
-struct DecodeParams {
-  const void* q;
-  int q_dtype;
-  int64_t q_sb, q_sh;
-  int B, Hq, Hkv, G, D;
-  float scale;
-  const float* E_inv;
-  const float* cent;
-  int nc;
-  const uint8_t* kcodes;
-  const void* knorms;
-  int kv_dtype;
-  const uint8_t* vdata;
-  const void* vscales;
-  const void* vzeros;
-  int gs;
-  const int32_t* bt;
-  int64_t bt_stride;
-  int64_t page_size;
-  const int32_t* hist_len;
-  const int32_t* hist_total;
-  int min_hist;
-  const void* rk;
-  const void* rv;
-  int r_dtype;
-  int64_t r_sb, r_st, r_sh;
-  const int32_t* recent_len;
-  int n_seg;
-  int64_t* plan;    // [n_seg + 1] prefix costs, then [per] at index n_seg + 1
-  float* slots;     // [(grid + n_seg)][G][D + 2]
-  int grid;
-};
-
-__device__ __forceinline__ int seg_tokens(const DecodeParams& p, int s) {
-  const int pair = s >> 1, b = pair / p.Hkv;
-  if ((s & 1) == 0) {
-    const int tot = p.hist_total ? p.hist_total[b] : p.hist_len[b];
-    return tot >= p.min_hist ? p.hist_len[b] : 0;
-  }
-  return p.recent_len ? p.recent_len[b] : 0;
-}
-__device__ __forceinline__ int seg_cost(int s) { return (s & 1) ? RECENT_COST : 1; }
 
 // One CTA: prefix sums of segment costs and the per-CTA slice length.
 __global__ void decode_plan_kernel(DecodeParams p) {
@@ -78,7 +31,7 @@ __global__ void decode_plan_kernel(DecodeParams p) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int base = 0; base < p.n_seg; base += blockDim.x) {
     const int s = base + threadIdx.x;
-    int64_t c = (s < p.n_seg) ? int64_t(seg_tokens(p, s)) * seg_cost(s) : 0;
+    int64_t c = (s < p.n_seg) ? seg_span(p, s) : 0;
     int64_t x = c;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -107,86 +60,11 @@ __global__ void decode_plan_kernel(DecodeParams p) {
     const int64_t total = carry;
     p.plan[p.n_seg] = total;
     int64_t per = (total + p.grid - 1) / p.grid;
-    if (per < RECENT_COST) per = RECENT_COST;
+    per = (per + 15) & ~int64_t(15);
+    if (per < 16) per = 16;
     p.plan[p.n_seg + 1] = per;
+    p.plan[p.n_seg + 2] = 0;  // error word (set by a kernel whose bounded wait ran out)
   }
-}
-
-__device__ __forceinline__ int64_t hist_row(const DecodeParams& p, int b, int h, int64_t t) {
-  const int64_t ps = p.page_size;
-  const int64_t pg = t / ps;
-  const int64_t page = p.bt ? int64_t(p.bt[b * p.bt_stride + pg]) : int64_t(b);
-  return (page * p.Hkv + h) * ps + (t - pg * ps);
-}
-
-// Online-softmax state of one warp for G query heads; lane owns dims [4*lane, 4*lane+4).
-template <int GM>
-struct WarpState {
-  float m[GM], l[GM], acc[GM][4];
-  __device__ __forceinline__ void init() {
-#pragma unroll
-    for (int g = 0; g < GM; ++g) {
-      m[g] = -INFINITY;
-      l[g] = 0.f;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[g][e] = 0.f;
-    }
-  }
-  // fold one chunk of scores (lane = token, -inf for absent lanes); returns p per head in s
-  __device__ __forceinline__ void softmax_chunk(float (&s)[GM], int G) {
-#pragma unroll
-    for (int g = 0; g < GM; ++g) {
-      if (g >= G) break;
-      const float cm = warp_max(s[g]);
-      const float mn = fmaxf(m[g], cm);
-      const float alpha = expf(m[g] - mn);
-      const float pv = expf(s[g] - mn);
-      l[g] = l[g] * alpha + warp_sum(pv);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[g][e] *= alpha;
-      m[g] = mn;
-      s[g] = pv;
-    }
-  }
-};
-
-// merge the DEC_WARPS warp states in shared memory and write one partial slot
-template <int GM>
-__device__ void cta_flush(const DecodeParams& p, WarpState<GM>& st, float* red, int slot) {
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int G = p.G, D = p.D;
-  const int stride = GM * (D + 2);
-  float* mine = red + wid * stride;
-#pragma unroll
-  for (int g = 0; g < GM; ++g) {
-    if (g >= G) break;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) mine[g * D + lane * 4 + e] = st.acc[g][e];
-    if (lane == 0) {
-      mine[GM * D + g * 2] = st.m[g];
-      mine[GM * D + g * 2 + 1] = st.l[g];
-    }
-  }
-  __syncthreads();
-  float* out = p.slots + int64_t(slot) * G * (D + 2);
-  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
-    const int g = i / D, d = i - g * D;
-    float M = -INFINITY;
-    for (int w = 0; w < DEC_WARPS; ++w) M = fmaxf(M, red[w * stride + GM * D + g * 2]);
-    float a = 0.f, L = 0.f;
-    for (int w = 0; w < DEC_WARPS; ++w) {
-      const float mw = red[w * stride + GM * D + g * 2];
-      const float f = (mw == -INFINITY) ? 0.f : expf(mw - M);
-      a += red[w * stride + g * D + d] * f;
-      L += red[w * stride + GM * D + g * 2 + 1] * f;
-    }
-    out[g * D + d] = a;
-    if (d == 0) {
-      out[G * D + g * 2] = M;
-      out[G * D + g * 2 + 1] = L;
-    }
-  }
-  __syncthreads();
 }
 
 template <int GM, int KB, int VB>
@@ -282,8 +160,16 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_kernel(DecodeParams p) {
         if (valid) {
           const int64_t row = hist_row(p, b, h, t);
           if constexpr (KB == 0) {
-            const uint4 iv = __ldg(reinterpret_cast<const uint4*>(p.kcodes + row * NBLK));
-            const uint8_t* ib = reinterpret_cast<const uint8_t*>(&iv);
+            uint4 iv;
+            uint8_t* ibw = reinterpret_cast<uint8_t*>(&iv);
+            if (p.layout == SMAQ_LAYOUT_DECODE) {
+              const uint8_t* g8 = p.kcodes + (row & ~int64_t(7)) * NBLK;
+#pragma unroll
+              for (int blk = 0; blk < NBLK; ++blk) ibw[blk] = g8[(blk & 7) * 16 + ((row ^ blk) & 7) * 2 + (blk >> 3)];
+            } else {
+              iv = __ldg(reinterpret_cast<const uint4*>(p.kcodes + row * NBLK));
+            }
+            const uint8_t* ib = ibw;
 #pragma unroll
             for (int g = 0; g < GM; ++g) {
               if (g >= G) break;
@@ -353,7 +239,8 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_kernel(DecodeParams p) {
           const float sc_ = load_elem(p.vscales, p.kv_dtype, row * ng + grp);
           const float zr = load_elem(p.vzeros, p.kv_dtype, row * ng + grp);
           if constexpr (VB == 2) {
-            const uint32_t by = p.vdata[row * (D / 4) + lane];
+            const int pos = p.layout == SMAQ_LAYOUT_DECODE ? 4 * (lane & 7) + (lane >> 3) : lane;
+            const uint32_t by = p.vdata[row * (D / 4) + pos];
 #pragma unroll
             for (int e = 0; e < 4; ++e) v[e] = fmaf(float((by >> (2 * e)) & 3u), sc_, zr);
           } else {
@@ -464,7 +351,8 @@ __global__ void merge_partials_kernel(const float* __restrict__ parts, int R, in
 // ---------------------------------------------------------------- host
 static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-static size_t plan_bytes(int n_seg) { return align_up(sizeof(int64_t) * (n_seg + 2), 256); }
+// [n_seg] prefix costs, total, per-CTA slice, device error word
+static size_t plan_bytes(int n_seg) { return align_up(sizeof(int64_t) * (n_seg + 4), 256); }
 
 static size_t dec_smem(int GM, int KB, int nc) {
   const int D = 128;
@@ -489,10 +377,6 @@ static int launch_decode_t(DecodeParams& p, int grid_req, cudaStream_t s, int* g
   }
   *grid_out = grid;
   if (query_only) return SMAQ_OK;
-  p.grid = grid;
-  decode_plan_kernel<<<1, 1024, 0, s>>>(p);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_status(e, "decode_plan_kernel");
   kern<<<grid, DEC_THREADS, sm, s>>>(p);
   return cuda_status(cudaGetLastError(), "decode_kernel");
 }
@@ -520,6 +404,8 @@ static int launch_decode_g(DecodeParams& p, int kb, int vb, int grid_req, cudaSt
 
 static int dispatch_decode(DecodeParams& p, int kb, int vb, int grid_req, cudaStream_t s, int* grid_out,
                            bool query_only) {
+  if (kb == 0 && decode_v2_eligible(p, SMAQ_KEYS_BVQ, vb, p.q_dtype))
+    return launch_decode_v2(p, grid_req, s, grid_out, query_only);
   if (p.G <= 1) return launch_decode_g<1>(p, kb, vb, grid_req, s, grid_out, query_only);
   if (p.G <= 2) return launch_decode_g<2>(p, kb, vb, grid_req, s, grid_out, query_only);
   if (p.G <= 4) return launch_decode_g<4>(p, kb, vb, grid_req, s, grid_out, query_only);
@@ -606,6 +492,7 @@ extern "C" int smaq_decode(const smaq_decode_args* args, void* stream) {
   p.r_sh = a.r_stride_h;
   p.recent_len = a.recent_len;
   p.n_seg = 2 * a.batch * a.n_kv_heads;
+  p.layout = a.layout;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int grid = 0;
   int st = dispatch_decode(p, kb, a.value_bits, a.num_ctas, s, &grid, true);
@@ -615,6 +502,10 @@ extern "C" int smaq_decode(const smaq_decode_args* args, void* stream) {
     return fail(SMAQ_ERR_WORKSPACE, "decode: workspace %zu bytes < %zu needed", a.workspace_bytes, need);
   p.plan = static_cast<int64_t*>(a.workspace);
   p.slots = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + plan_bytes(p.n_seg));
+  p.grid = grid;
+  decode_plan_kernel<<<1, 1024, 0, s>>>(p);
+  st = cuda_status(cudaGetLastError(), "decode_plan_kernel");
+  if (st) return st;
   st = dispatch_decode(p, kb, a.value_bits, grid, s, &grid, false);
   if (st) return st;
   decode_merge_kernel<<<a.batch * a.n_kv_heads, 256, 0, s>>>(p, a.out, a.o_stride_b, a.o_stride_h, a.partial_out);

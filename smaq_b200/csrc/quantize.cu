@@ -23,7 +23,8 @@ template <class DT, int EPL, int BITS>
 __global__ void __launch_bounds__(256) value_quant_kernel(
     const typename DT::T* __restrict__ v, int64_t n_tokens, int n_heads, int64_t st, int64_t sh,
     const int64_t* __restrict__ slots, int64_t slot_offset, int64_t page_size, int group_size,
-    uint8_t* __restrict__ data, typename DT::T* __restrict__ scales, typename DT::T* __restrict__ zeros) {
+    uint8_t* __restrict__ data, typename DT::T* __restrict__ scales, typename DT::T* __restrict__ zeros,
+    int layout) {
   constexpr int D = 32 * EPL;
   constexpr int NL = (1 << BITS) - 1;
   const int lane = threadIdx.x & 31;
@@ -65,7 +66,9 @@ __global__ void __launch_bounds__(256) value_quant_kernel(
     if constexpr (LANE_BITS >= 8) {
       constexpr int NB = LANE_BITS / 8;
       if constexpr (NB == 1) {
-        dst[lane] = uint8_t(packed);
+        // decode layout (2-bit, D = 128): reference byte 8j + g goes to byte 4g + j
+        const int pos = layout == SMAQ_LAYOUT_DECODE ? 4 * (lane & 7) + (lane >> 3) : lane;
+        dst[pos] = uint8_t(packed);
       } else if constexpr (NB == 2) {
         reinterpret_cast<uint16_t*>(dst)[lane] = uint16_t(packed);
       } else {
@@ -217,7 +220,8 @@ template <class DT, int EPL>
 __global__ void __launch_bounds__(BQ_WARPS * 32) bvq_key_kernel(
     const typename DT::T* __restrict__ k, int64_t n_tokens, int n_heads, int64_t st, int64_t sh,
     const int64_t* __restrict__ slots, int64_t slot_offset, int64_t page_size,
-    const float* __restrict__ Eb, const float* __restrict__ cent, int nc, uint8_t* __restrict__ out) {
+    const float* __restrict__ Eb, const float* __restrict__ cent, int nc, uint8_t* __restrict__ out,
+    int layout) {
   constexpr int D = 32 * EPL;
   constexpr int BD = 8;
   constexpr int NBLK = D / BD;
@@ -336,7 +340,10 @@ __global__ void __launch_bounds__(BQ_WARPS * 32) bvq_key_kernel(
             const int64_t t = r / n_heads;
             const int h = int(r - t * n_heads);
             const int64_t row = store_row(slots, slot_offset, page_size, n_heads, t, h);
-            out[row * NBLK + blk] = uint8_t(bi[rr]);
+            int64_t off = row * NBLK + blk;
+            if (layout == SMAQ_LAYOUT_DECODE)  // 8-row groups, see include/smaq_b200.h
+              off = (row & ~int64_t(7)) * NBLK + (blk & 7) * 16 + ((row ^ blk) & 7) * 2 + (blk >> 3);
+            out[off] = uint8_t(bi[rr]);
           }
         }
       }
@@ -365,12 +372,12 @@ static int launch_values_t(const smaq_append_args& a, cudaStream_t s) {
     value_quant_kernel<DT, EPL, 2><<<grid, 256, 0, s>>>(
         static_cast<const T*>(a.v), a.n_tokens, a.n_heads, a.v_stride_t, a.v_stride_h, a.slots,
         a.slot_offset, a.page_size, a.group_size, a.v_data, static_cast<T*>(a.v_scales),
-        static_cast<T*>(a.v_zeros));
+        static_cast<T*>(a.v_zeros), a.layout);
   else
     value_quant_kernel<DT, EPL, 4><<<grid, 256, 0, s>>>(
         static_cast<const T*>(a.v), a.n_tokens, a.n_heads, a.v_stride_t, a.v_stride_h, a.slots,
         a.slot_offset, a.page_size, a.group_size, a.v_data, static_cast<T*>(a.v_scales),
-        static_cast<T*>(a.v_zeros));
+        static_cast<T*>(a.v_zeros), SMAQ_LAYOUT_REFERENCE);
   return cuda_status(cudaGetLastError(), "value_quant_kernel");
 }
 
@@ -436,7 +443,7 @@ static int launch_bvq_t(const smaq_append_args& a, cudaStream_t s) {
   using T = typename DT::T;
   kern<<<grid, BQ_WARPS * 32, sm, s>>>(static_cast<const T*>(a.k), a.n_tokens, a.n_heads, a.k_stride_t,
                                        a.k_stride_h, a.slots, a.slot_offset, a.page_size, a.E_blocks,
-                                       a.centroids, nc, a.key_codes);
+                                       a.centroids, nc, a.key_codes, a.layout);
   return cuda_status(cudaGetLastError(), "bvq_key_kernel");
 }
 
@@ -473,6 +480,13 @@ static int validate_append(const smaq_append_args& a) {
     return fail(SMAQ_ERR_INVALID, "append: unknown dtype %d", a.dtype);
   const size_t es = dsize(a.dtype);
   const int epl = a.head_dim / 32;
+  if (a.layout != SMAQ_LAYOUT_REFERENCE && a.layout != SMAQ_LAYOUT_DECODE)
+    return fail(SMAQ_ERR_INVALID, "append: unknown layout %d", a.layout);
+  if (a.layout == SMAQ_LAYOUT_DECODE) {
+    if (a.head_dim != 128 || (a.v && a.value_bits != 2) || (a.k && a.key_format == SMAQ_KEYS_BVQ && a.block_dim != 8))
+      return fail(SMAQ_ERR_UNSUPPORTED, "decode layout needs head_dim 128, 2-bit values, 8-dim VQ blocks");
+    if (a.page_size % 16) return fail(SMAQ_ERR_INVALID, "decode layout needs page_size %% 16 == 0");
+  }
   if (a.v) {
     if (a.value_bits != 2 && a.value_bits != 4)
       return fail(SMAQ_ERR_INVALID, "values: bits %d not in {2,4}", a.value_bits);

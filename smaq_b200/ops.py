@@ -14,7 +14,8 @@ from typing import Optional
 import torch
 
 from smaq_b200 import _lib
-from smaq_b200._lib import SMAQ_BF16, SMAQ_F16, SMAQ_F32, SMAQ_KEYS_BVQ, SMAQ_KEYS_SCALAR
+from smaq_b200._lib import (SMAQ_BF16, SMAQ_F16, SMAQ_F32, SMAQ_KEYS_BVQ, SMAQ_KEYS_SCALAR,
+                           SMAQ_LAYOUT_DECODE, SMAQ_LAYOUT_REFERENCE)
 
 _DT = {torch.float32: SMAQ_F32, torch.bfloat16: SMAQ_BF16, torch.float16: SMAQ_F16}
 
@@ -112,7 +113,8 @@ def append(key: Optional[torch.Tensor], value: Optional[torch.Tensor], *, n_head
            E_blocks: Optional[torch.Tensor] = None, centroids: Optional[torch.Tensor] = None,
            key_codes: Optional[torch.Tensor] = None, key_norms: Optional[torch.Tensor] = None,
            value_bits: int = 2, group_size: int = 32, v_data: Optional[torch.Tensor] = None,
-           v_scales: Optional[torch.Tensor] = None, v_zeros: Optional[torch.Tensor] = None) -> None:
+           v_scales: Optional[torch.Tensor] = None, v_zeros: Optional[torch.Tensor] = None,
+           layout: int = SMAQ_LAYOUT_REFERENCE) -> None:
     """Quantize a ``[T, H, D]`` chunk of keys and/or values into store rows (see include/smaq_b200.h)."""
     _cuda(key, value, slots, E, boundaries, E_blocks, centroids, key_codes, key_norms, v_data)
     lib = _lib.load()
@@ -162,6 +164,7 @@ def append(key: Optional[torch.Tensor], value: Optional[torch.Tensor], *, n_head
         a.slots = slots.data_ptr()
     a.slot_offset = slot_offset
     a.page_size = page_size
+    a.layout = layout
     _lib.check(lib.smaq_append(a, _stream()), "smaq_append")
 
 
@@ -179,7 +182,7 @@ def decode(q: torch.Tensor, *, n_kv_heads: int, key_format: int, key_codes: torc
            recent_v: Optional[torch.Tensor] = None, recent_len: Optional[torch.Tensor] = None,
            scale: Optional[float] = None, min_history: int = MIN_HISTORY, out: Optional[torch.Tensor] = None,
            partial_out: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
-           num_ctas: int = 0, want_out: bool = True) -> Optional[torch.Tensor]:
+           num_ctas: int = 0, want_out: bool = True, layout: int = SMAQ_LAYOUT_REFERENCE) -> Optional[torch.Tensor]:
     """Batched hybrid decode attention.
 
     ``q``: ``[B, Hq, D]``.  History streams are store rows ``[pages, Hkv, page_size, ...]``;
@@ -253,6 +256,7 @@ def decode(q: torch.Tensor, *, n_kv_heads: int, key_format: int, key_codes: torc
     keep.append(workspace)
     a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel()
     a.num_ctas = num_ctas
+    a.layout = layout
     _lib.check(lib.smaq_decode(a, _stream()), "smaq_decode")
     return out
 
@@ -268,3 +272,23 @@ def merge_partials(partials: torch.Tensor, out_dtype: torch.dtype) -> torch.Tens
     _lib.check(lib.smaq_merge_partials(p.data_ptr(), R, B, Hq, D, out.data_ptr(), dtype_code(out_dtype),
                                        out.stride(0), out.stride(1), _stream()), "smaq_merge_partials")
     return out
+
+
+# --------------------------------------------------------------------- decode-layout byte order
+# (SMAQ_LAYOUT_DECODE, include/smaq_b200.h): same bits as the reference, permuted inside rows.
+_VPERM = [4 * (k % 8) + k // 8 for k in range(32)]          # reference byte k lives at _VPERM[k]
+
+
+def values_to_reference(data: torch.Tensor) -> torch.Tensor:
+    """Decode-layout 2-bit value rows ``(..., 32)`` -> reference byte order."""
+    return data[..., _VPERM]
+
+
+def bvq_to_reference(idx: torch.Tensor) -> torch.Tensor:
+    """Decode-layout block-VQ rows ``(..., N, 16)`` (N a multiple of 8) -> reference order."""
+    lead, n = idx.shape[:-2], idx.shape[-2]
+    g = idx.reshape(*lead, n // 8, 128)
+    b = torch.arange(16, device=idx.device)
+    t8 = torch.arange(8, device=idx.device)
+    pos = (b[None, :] % 8) * 16 + ((t8[:, None] ^ b[None, :]) % 8) * 2 + b[None, :] // 8  # [8 tok, 16 blk]
+    return g[..., pos.reshape(-1)].reshape(*lead, n, 16)

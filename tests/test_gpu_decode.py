@@ -70,7 +70,7 @@ def build_paged(dev, kind, bits, B, Hkv, hist, page_size, dtype, seed):
     return st, raw
 
 
-def run_case(cuda, kind, bits, B, Hkv, G, hist, recent, page_size, dtype, seed, num_ctas=0):
+def run_case(cuda, kind, bits, B, Hkv, G, hist, recent, page_size, dtype, seed, num_ctas=0, layout=0):
     import torch
     from smaq_b200 import ops
     from smaq_b200._lib import SMAQ_KEYS_BVQ, SMAQ_KEYS_SCALAR
@@ -86,11 +86,11 @@ def run_case(cuda, kind, bits, B, Hkv, G, hist, recent, page_size, dtype, seed, 
         if kind == "scalar":
             ops.append(k, v, n_heads=Hkv, slots=slots, page_size=page_size, key_format=SMAQ_KEYS_SCALAR,
                        key_bits=bits, E=E, boundaries=bnd, key_codes=st["codes"], key_norms=st["norms"],
-                       v_data=st["vdata"], v_scales=st["vs"], v_zeros=st["vz"])
+                       v_data=st["vdata"], v_scales=st["vs"], v_zeros=st["vz"], layout=layout)
         else:
             ops.append(k, v, n_heads=Hkv, slots=slots, page_size=page_size, key_format=SMAQ_KEYS_BVQ,
                        E_blocks=Eb, centroids=C, key_codes=st["codes"], v_data=st["vdata"],
-                       v_scales=st["vs"], v_zeros=st["vz"])
+                       v_scales=st["vs"], v_zeros=st["vz"], layout=layout)
     W = max(1, int(max(recent)))
     rk = torch.from_numpy(syn.keys((B, W, Hkv), D, seed=seed + 7)).to(cuda).to(tdt)
     rv = torch.from_numpy(syn.values((B, W, Hkv), D, seed=seed + 8)).to(cuda).to(tdt)
@@ -101,11 +101,16 @@ def run_case(cuda, kind, bits, B, Hkv, G, hist, recent, page_size, dtype, seed, 
               key_norms=st["norms"]) if kind == "scalar" else dict(key_format=SMAQ_KEYS_BVQ, centroids=dec)
     out = ops.decode(q, n_kv_heads=Hkv, key_codes=st["codes"], v_data=st["vdata"], v_scales=st["vs"],
                      v_zeros=st["vz"], hist_len=hl, page_size=page_size, block_table=st["bt"],
-                     recent_k=rk, recent_v=rv, recent_len=rl, num_ctas=num_ctas, **kw)
+                     recent_k=rk, recent_v=rv, recent_len=rl, num_ctas=num_ctas, layout=layout, **kw)
     got = tn(out)
     # oracle per sequence, from the GPU-written rows (isolates decode from quantize parity)
-    codes, norms = tn(st["codes"]), tn(st["norms"])
-    vdata, vs, vz = tn(st["vdata"]), tn(st["vs"]), tn(st["vz"])
+    codes_t, vdata_t = st["codes"], st["vdata"]
+    if layout == 1:
+        vdata_t = ops.values_to_reference(vdata_t)
+        if kind == "bvq":
+            codes_t = ops.bvq_to_reference(codes_t)
+    codes, norms = tn(codes_t), tn(st["norms"])
+    vdata, vs, vz = tn(vdata_t), tn(st["vs"]), tn(st["vz"])
     bt = tn(st["bt"])
     worst = 0.0
     for b in range(B):
@@ -151,3 +156,45 @@ def test_stream_k_partition_invariance(cuda, num_ctas):
     b = run_case(cuda, "bvq", 0, B=4, Hkv=2, G=4, hist=[900, 300, 17, 64], recent=[128, 0, 9, 1],
                  page_size=16, dtype="bfloat16", seed=13, num_ctas=0)
     assert O.rel_l2(a, b) < 1e-3
+
+
+@pytest.mark.parametrize("G", [1, 4, 7, 8])
+def test_fast_bvq_decode_paged(cuda, G):
+    """Block-VQ fast path (decode layout, TMA staging, tensor-core P.V) against the oracle."""
+    run_case(cuda, "bvq", 0, B=5, Hkv=2, G=G, hist=[1000, 15, 16, 333, 2048], recent=[64, 3, 0, 128, 1],
+             page_size=16, dtype="bfloat16", seed=21, layout=1)
+
+
+def test_fast_bvq_decode_long_pages(cuda):
+    run_case(cuda, "bvq", 0, B=2, Hkv=4, G=4, hist=[5000, 4097], recent=[128, 128], page_size=1024,
+             dtype="bfloat16", seed=22, layout=1)
+
+
+@pytest.mark.parametrize("num_ctas", [1, 7, 300])
+def test_fast_bvq_partition_invariance(cuda, num_ctas):
+    run_case(cuda, "bvq", 0, B=3, Hkv=2, G=4, hist=[3000, 100, 17], recent=[128, 0, 9], page_size=16,
+             dtype="bfloat16", seed=23, num_ctas=num_ctas, layout=1)
+
+
+def test_decode_layout_bytes_are_permuted_reference_bytes(cuda):
+    """Decode-layout rows hold exactly the reference bytes, permuted (bit-exact)."""
+    import torch
+    from smaq_b200 import ops
+    from smaq_b200._lib import SMAQ_KEYS_BVQ
+    Eb, C, _ = random_codebook(cuda)
+    k = torch.from_numpy(syn.keys((64, 2), D, seed=31)).to(cuda).to(torch.bfloat16)
+    v = torch.from_numpy(syn.values((64, 2), D, seed=32)).to(cuda).to(torch.bfloat16)
+    out = {}
+    for lay in (0, 1):
+        codes = torch.zeros((2, 64, 16), dtype=torch.uint8, device=cuda)
+        vd = torch.zeros((2, 64, 32), dtype=torch.uint8, device=cuda)
+        vs = torch.zeros((2, 64, 4), dtype=torch.bfloat16, device=cuda)
+        vz = torch.zeros_like(vs)
+        ops.append(k, v, n_heads=2, page_size=64, key_format=SMAQ_KEYS_BVQ, E_blocks=Eb, centroids=C,
+                   key_codes=codes, v_data=vd, v_scales=vs, v_zeros=vz, layout=lay)
+        out[lay] = (codes, vd, vs, vz)
+    assert torch.equal(ops.bvq_to_reference(out[1][0]), out[0][0])
+    assert torch.equal(ops.values_to_reference(out[1][1]), out[0][1])
+    assert torch.equal(out[1][2], out[0][2]) and torch.equal(out[1][3], out[0][3])
+    ref_idx = ops.quantize_keys_bvq(k, Eb, C).reshape(64, 2, 16).transpose(0, 1)
+    assert torch.equal(out[0][0], ref_idx)
