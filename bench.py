@@ -130,6 +130,9 @@ def make_codebook(dev):
     vq.fit(ck, cq, seed=syn.SEED_KMEANS)
     for name in ("E_blocks", "E_inv_blocks", "centroids", "decoded_centroids"):
         getattr(vq, name).copy_(getattr(vq, name).half().float())
+    from smaq_b200 import ops
+    vq.cb16 = ops.fp16_codebook(vq.decoded_centroids)
+    assert vq.cb16 is not None
     return vq
 
 
@@ -182,7 +185,8 @@ def decode_layer(a, L, vq, hl, rl, ws, q=None, out=None):
     return ops.decode(L["q"] if q is None else q, n_kv_heads=a.hkv, key_format=SMAQ_KEYS_BVQ,
                       centroids=vq.decoded_centroids, key_codes=L["codes"], v_data=L["vdata"], v_scales=L["vs"],
                       v_zeros=L["vz"], hist_len=hl, page_size=a.ctx, recent_k=L["rk"], recent_v=L["rv"],
-                      recent_len=rl, out=L["out"] if out is None else out, workspace=ws, layout=SMAQ_LAYOUT_DECODE)
+                      recent_len=rl, out=L["out"] if out is None else out, workspace=ws, layout=SMAQ_LAYOUT_DECODE,
+                      centroids_f16=vq.cb16)
 
 
 # ----------------------------------------------------------------------------- CPU baseline

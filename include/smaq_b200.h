@@ -35,10 +35,9 @@
  * sequence b from page = block_table ? block_table[b * bt_stride + t / page_size] : b.
  *
  * SMAQ_LAYOUT_DECODE permutes bytes inside rows (same bits, same row sizes):
- *   block-VQ indices: each aligned group of 8 rows (128 bytes) stores, at byte
- *     (b % 8) * 16 + ((row ^ b) % 8) * 2 + b / 8, the index of block b of that row, so one
- *     16-byte load yields the index pair (b, b + 8) of eight consecutive tokens (in an
- *     order XOR-swizzled by b % 8);
+ *   block-VQ indices (16 blocks): byte 2 * (4 * (b / 8) + b % 4) + (b / 4) % 2 of a row holds
+ *     the index of block b, so the pair of blocks (b, b + 4) a tensor-core lane gathers for
+ *     one token sits in one 16-bit half of one 32-bit word;
  *   2-bit values (head_dim 128): byte 4 * g + j of a row holds reference byte 8 * j + g
  *     (g < 8, j < 4), so each 32-bit word carries one byte of every value group.
  * Reference-layout bytes are recovered by the inverse permutation.
@@ -174,6 +173,10 @@ typedef struct smaq_decode_args {
   size_t workspace_bytes;
   int num_ctas;              /* 0: one wave over the device's SMs */
   int layout;                /* row layout of the history streams */
+  /* bvq only, nullable: the decoded centroids as fp16 [D/bd, nc, bd].  The caller promises
+   * they equal `centroids` exactly (an fp16-valued codebook); with SMAQ_LAYOUT_DECODE rows,
+   * bf16/fp16 queries, 2-bit values and group 32 this selects the tensor-core kernel. */
+  const void* centroids_f16;
 } smaq_decode_args;
 
 /* Bytes of workspace smaq_decode needs for these shapes (host-only computation). */

@@ -53,6 +53,7 @@ class DecodeArgs(C.Structure):
         ("r_stride_b", i64), ("r_stride_t", i64), ("r_stride_h", i64), ("recent_len", vp),
         ("out", vp), ("o_stride_b", i64), ("o_stride_h", i64), ("partial_out", vp),
         ("workspace", vp), ("workspace_bytes", C.c_size_t), ("num_ctas", i32), ("layout", i32),
+        ("centroids_f16", vp),
     ]
 
 

@@ -163,9 +163,9 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_kernel(DecodeParams p) {
             uint4 iv;
             uint8_t* ibw = reinterpret_cast<uint8_t*>(&iv);
             if (p.layout == SMAQ_LAYOUT_DECODE) {
-              const uint8_t* g8 = p.kcodes + (row & ~int64_t(7)) * NBLK;
+              const uint8_t* rb = p.kcodes + row * NBLK;
 #pragma unroll
-              for (int blk = 0; blk < NBLK; ++blk) ibw[blk] = g8[(blk & 7) * 16 + ((row ^ blk) & 7) * 2 + (blk >> 3)];
+              for (int blk = 0; blk < NBLK; ++blk) ibw[blk] = rb[2 * (4 * (blk >> 3) + (blk & 3)) + ((blk >> 2) & 1)];
             } else {
               iv = __ldg(reinterpret_cast<const uint4*>(p.kcodes + row * NBLK));
             }
@@ -493,6 +493,7 @@ extern "C" int smaq_decode(const smaq_decode_args* args, void* stream) {
   p.recent_len = a.recent_len;
   p.n_seg = 2 * a.batch * a.n_kv_heads;
   p.layout = a.layout;
+  p.cent16 = a.key_format == SMAQ_KEYS_BVQ ? static_cast<const uint16_t*>(a.centroids_f16) : nullptr;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int grid = 0;
   int st = dispatch_decode(p, kb, a.value_bits, a.num_ctas, s, &grid, true);

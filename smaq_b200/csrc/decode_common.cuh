@@ -41,6 +41,7 @@ struct DecodeParams {
   float* slots;     // [(grid + n_seg)][G][D + 2]
   int grid;
   int layout;
+  const uint16_t* cent16;  // bvq: fp16 copy of the decoded centroids (exact), or null
 };
 
 __device__ __forceinline__ int seg_tokens(const DecodeParams& p, int s) {

@@ -341,8 +341,8 @@ __global__ void __launch_bounds__(BQ_WARPS * 32) bvq_key_kernel(
             const int h = int(r - t * n_heads);
             const int64_t row = store_row(slots, slot_offset, page_size, n_heads, t, h);
             int64_t off = row * NBLK + blk;
-            if (layout == SMAQ_LAYOUT_DECODE)  // 8-row groups, see include/smaq_b200.h
-              off = (row & ~int64_t(7)) * NBLK + (blk & 7) * 16 + ((row ^ blk) & 7) * 2 + (blk >> 3);
+            if (layout == SMAQ_LAYOUT_DECODE)  // see include/smaq_b200.h
+              off = row * NBLK + 2 * (4 * (blk >> 3) + (blk & 3)) + ((blk >> 2) & 1);
             out[off] = uint8_t(bi[rr]);
           }
         }

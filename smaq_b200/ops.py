@@ -182,7 +182,8 @@ def decode(q: torch.Tensor, *, n_kv_heads: int, key_format: int, key_codes: torc
            recent_v: Optional[torch.Tensor] = None, recent_len: Optional[torch.Tensor] = None,
            scale: Optional[float] = None, min_history: int = MIN_HISTORY, out: Optional[torch.Tensor] = None,
            partial_out: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
-           num_ctas: int = 0, want_out: bool = True, layout: int = SMAQ_LAYOUT_REFERENCE) -> Optional[torch.Tensor]:
+           num_ctas: int = 0, want_out: bool = True, layout: int = SMAQ_LAYOUT_REFERENCE,
+           centroids_f16: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
     """Batched hybrid decode attention.
 
     ``q``: ``[B, Hq, D]``.  History streams are store rows ``[pages, Hkv, page_size, ...]``;
@@ -257,6 +258,10 @@ def decode(q: torch.Tensor, *, n_kv_heads: int, key_format: int, key_codes: torc
     a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel()
     a.num_ctas = num_ctas
     a.layout = layout
+    if centroids_f16 is not None:
+        c16 = centroids_f16.to(torch.float16).contiguous()
+        keep.append(c16)
+        a.centroids_f16 = c16.data_ptr()
     _lib.check(lib.smaq_decode(a, _stream()), "smaq_decode")
     return out
 
@@ -285,10 +290,14 @@ def values_to_reference(data: torch.Tensor) -> torch.Tensor:
 
 
 def bvq_to_reference(idx: torch.Tensor) -> torch.Tensor:
-    """Decode-layout block-VQ rows ``(..., N, 16)`` (N a multiple of 8) -> reference order."""
-    lead, n = idx.shape[:-2], idx.shape[-2]
-    g = idx.reshape(*lead, n // 8, 128)
+    """Decode-layout block-VQ rows ``(..., 16)`` -> reference block order."""
     b = torch.arange(16, device=idx.device)
-    t8 = torch.arange(8, device=idx.device)
-    pos = (b[None, :] % 8) * 16 + ((t8[:, None] ^ b[None, :]) % 8) * 2 + b[None, :] // 8  # [8 tok, 16 blk]
-    return g[..., pos.reshape(-1)].reshape(*lead, n, 16)
+    pos = 2 * (4 * (b // 8) + b % 4) + (b // 4) % 2
+    return idx[..., pos]
+
+
+def fp16_codebook(decoded_centroids: torch.Tensor) -> Optional[torch.Tensor]:
+    """fp16 copy of a decoded codebook if it is exactly fp16-valued (enables the tensor-core
+    decode kernel), else None."""
+    c16 = decoded_centroids.to(torch.float16)
+    return c16 if torch.equal(c16.to(decoded_centroids.dtype), decoded_centroids) else None

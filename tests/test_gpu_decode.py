@@ -30,7 +30,8 @@ def random_codebook(dev, seed=7):
     rng = np.random.default_rng(seed)
     Eb = (np.eye(8)[None] + 0.1 * rng.standard_normal((16, 8, 8))).astype(np.float32)
     C = rng.standard_normal((16, 256, 8)).astype(np.float32)
-    dec = rng.standard_normal((16, 256, 8)).astype(np.float32) * 0.5
+    # fp16-valued decoded codebook (like BASELINE config 1's), so the tensor-core path applies
+    dec = (rng.standard_normal((16, 256, 8)) * 0.5).astype(np.float16).astype(np.float32)
     return [torch.from_numpy(x).to(dev) for x in (Eb, C, dec)]
 
 
@@ -99,6 +100,9 @@ def run_case(cuda, kind, bits, B, Hkv, G, hist, recent, page_size, dtype, seed, 
     rl = torch.tensor(recent, dtype=torch.int32, device=cuda)
     kw = dict(key_format=SMAQ_KEYS_SCALAR, key_bits=bits, E_inv=E_inv, centroids=cent,
               key_norms=st["norms"]) if kind == "scalar" else dict(key_format=SMAQ_KEYS_BVQ, centroids=dec)
+    if kind == "bvq" and layout == 1:
+        kw["centroids_f16"] = ops.fp16_codebook(dec)
+        assert kw["centroids_f16"] is not None
     out = ops.decode(q, n_kv_heads=Hkv, key_codes=st["codes"], v_data=st["vdata"], v_scales=st["vs"],
                      v_zeros=st["vz"], hist_len=hl, page_size=page_size, block_table=st["bt"],
                      recent_k=rk, recent_v=rv, recent_len=rl, num_ctas=num_ctas, layout=layout, **kw)
