@@ -70,43 +70,34 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
 // block b of the codebook lives at 16-byte slot sigma(b) of its 256-byte row (see the bank note)
 __host__ __device__ constexpr int cb_sigma(int b) { return b < 8 ? b : 8 + ((b - 8 + 4) & 7); }
 
-// Issue the bulk copies of chunk `kc` of a history segment into `stage`.
-__device__ __forceinline__ void v3_issue(const DecodeParams& p, int b, int h, int64_t t0, int64_t t1, int kc,
-                                         uint8_t* stage, uint64_t* bar) {
-  const int64_t tc = t0 + int64_t(kc) * CH;
-  int64_t nv = t1 - tc;
-  if (nv > CH) nv = CH;
-  const uint32_t ncopy = uint32_t((nv + 15) & ~int64_t(15));
-  mbar_arrive_expect_tx(bar, ncopy * 64);
-  const int64_t ps = p.page_size;
-  int64_t row0;
-  uint32_t len0 = ncopy;
-  if (p.bt) {
-    const int64_t pg = tc / ps, off = tc - pg * ps;
-    row0 = (int64_t(p.bt[b * p.bt_stride + pg]) * p.Hkv + h) * ps + off;
-    if (int64_t(len0) > ps - off) len0 = uint32_t(ps - off);
-  } else {
-    row0 = (int64_t(b) * p.Hkv + h) * ps + tc;
+// Per-segment source description of one stream for the bulk copies.
+struct V3Src {
+  const uint8_t* base;  // contiguous store: this stream at token t0 of the segment; paged: stream base
+  uint32_t row_bytes;   // 16 (indices), 32 (value codes), 8 (scales), 8 (zeros)
+  uint32_t dst_off;     // offset of the stream inside a stage
+};
+
+// Lanes 0..3 each copy one stream of chunk `kc` (tokens t0 + 32kc ..) into `stage`; the
+// mbarrier was initialised with 4 arrivals.  Paged stores split the copy at page boundaries.
+__device__ __forceinline__ void v3_issue(const DecodeParams& p, const V3Src& src, int b, int h, int64_t t0,
+                                         int nv, int kc, uint8_t* stage, uint64_t* bar) {
+  const uint32_t ncopy = (uint32_t(nv) + 15u) & ~15u;
+  mbar_arrive_expect_tx(bar, ncopy * src.row_bytes);
+  if (!p.bt) {
+    bulk_g2s(stage + src.dst_off, src.base + size_t(kc) * CH * src.row_bytes, ncopy * src.row_bytes, bar);
+    return;
   }
-  bulk_g2s(stage + ST_IDX, p.kcodes + row0 * 16, len0 * 16, bar);
-  bulk_g2s(stage + ST_V, p.vdata + row0 * 32, len0 * 32, bar);
-  bulk_g2s(stage + ST_S, static_cast<const uint8_t*>(p.vscales) + row0 * 8, len0 * 8, bar);
-  bulk_g2s(stage + ST_Z, static_cast<const uint8_t*>(p.vzeros) + row0 * 8, len0 * 8, bar);
-  if (len0 < ncopy) {  // chunk crosses into the next page (page_size 16 or 32)
-    int64_t t = tc + len0;
-    uint32_t done = len0;
-    while (done < ncopy) {
-      const int64_t pg = t / ps, off = t - pg * ps;
-      uint32_t len = ncopy - done;
-      if (int64_t(len) > ps - off) len = uint32_t(ps - off);
-      const int64_t r = (int64_t(p.bt[b * p.bt_stride + pg]) * p.Hkv + h) * ps + off;
-      bulk_g2s(stage + ST_IDX + done * 16, p.kcodes + r * 16, len * 16, bar);
-      bulk_g2s(stage + ST_V + done * 32, p.vdata + r * 32, len * 32, bar);
-      bulk_g2s(stage + ST_S + done * 8, static_cast<const uint8_t*>(p.vscales) + r * 8, len * 8, bar);
-      bulk_g2s(stage + ST_Z + done * 8, static_cast<const uint8_t*>(p.vzeros) + r * 8, len * 8, bar);
-      done += len;
-      t += len;
-    }
+  const int64_t ps = p.page_size;
+  int64_t t = t0 + int64_t(kc) * CH;
+  uint32_t done = 0;
+  while (done < ncopy) {
+    const int64_t pg = t / ps, off = t - pg * ps;
+    uint32_t len = ncopy - done;
+    if (int64_t(len) > ps - off) len = uint32_t(ps - off);
+    const int64_t r = (int64_t(p.bt[b * p.bt_stride + pg]) * p.Hkv + h) * ps + off;
+    bulk_g2s(stage + src.dst_off + done * src.row_bytes, src.base + r * src.row_bytes, len * src.row_bytes, bar);
+    done += len;
+    t += len;
   }
 }
 
@@ -202,20 +193,20 @@ __device__ __forceinline__ void v3_chunk(uint32_t st, uint32_t cb_s, uint32_t sz
     mma_f16_16816(d, qa[2], e1.x, e1.y);
     mma_f16_16816(d, qa[3], e1.z, e1.w);
     const float sc = (d[0] + d[3]) * lscale;
-    s[i] = ((FULL || 4 * i + tig < nv) && gid < G) ? sc : -INFINITY;
+    s[i] = (FULL || 4 * i + tig < nv) ? sc : -INFINITY;  // heads >= G score 0: harmless
   }
   // ---- online softmax for head gid over the 8 tokens of this thread and its 3 tig peers
   float mx = fmaxf(fmaxf(fmaxf(s[0], s[1]), fmaxf(s[2], s[3])), fmaxf(fmaxf(s[4], s[5]), fmaxf(s[6], s[7])));
   mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
   mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
   const float mn = fmaxf(mrun, mx);
-  const float alpha = mn == -INFINITY ? 1.f : fast_exp2(mrun - mn);
+  const float alpha = fast_exp2(mrun - mn);  // first chunk: exp2(-inf) = 0
   const bool grew = mn != mrun;
   mrun = mn;
   float ls = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    s[i] = mn == -INFINITY ? 0.f : fast_exp2(s[i] - mn);  // p; 0 for masked tokens / padded heads
+    s[i] = fast_exp2(s[i] - mn);  // p; 0 for masked tokens
     ls += s[i];
   }
   lrun = lrun * alpha + ls;
@@ -292,7 +283,7 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
   float* rec = reinterpret_cast<float*>(wreg);                       // merge record (after the loop)
   uint64_t* wbar = bars + wid * ST;
   if (lane == 0) {
-    for (int s = 0; s < ST; ++s) mbar_init(&wbar[s], 1);
+    for (int s = 0; s < ST; ++s) mbar_init(&wbar[s], 4);
     fence_mbar_init();
   }
   uint32_t phase = 0;
@@ -443,11 +434,25 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
     }
 
     // ---------------- compressed history
-    const int64_t nchunks = (t1 - t0 + CH - 1) / CH;
-    const int mine = (wid < nchunks) ? int((nchunks - 1 - wid) / WARPS + 1) : 0;
-    if (lane == 0) {
-      for (int i = 0; i < ST && i < mine; ++i)
-        v3_issue(p, b, h, t0, t1, wid + WARPS * i, wreg + i * STAGE_BYTES, &wbar[i]);
+    const int ntok = int(t1 - t0);
+    const int nchunks = (ntok + CH - 1) / CH;
+    const int mine = (wid < nchunks) ? (nchunks - 1 - wid) / WARPS + 1 : 0;
+    V3Src src;
+    {
+      const int k = lane & 3;
+      const uint8_t* base = k == 0 ? p.kcodes
+                            : k == 1 ? p.vdata
+                            : k == 2 ? static_cast<const uint8_t*>(p.vscales)
+                                     : static_cast<const uint8_t*>(p.vzeros);
+      src.row_bytes = k == 0 ? 16u : k == 1 ? 32u : 8u;
+      src.dst_off = k == 0 ? uint32_t(ST_IDX) : k == 1 ? uint32_t(ST_V) : k == 2 ? uint32_t(ST_S) : uint32_t(ST_Z);
+      src.base = p.bt ? base : base + ((int64_t(b) * p.Hkv + h) * p.page_size + t0) * src.row_bytes;
+    }
+    if (lane < 4) {
+      for (int i = 0; i < ST && i < mine; ++i) {
+        const int kc = wid + WARPS * i;
+        v3_issue(p, src, b, h, t0, min(CH, ntok - kc * CH), kc, wreg + i * STAGE_BYTES, &wbar[i]);
+      }
     }
     __syncthreads();  // qs complete
     // A fragments of the score MMA: rows (head gid, half 0) and (head gid, half 1); k-step ks
@@ -476,13 +481,15 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
       uint8_t* stage = wreg + stg * STAGE_BYTES;
       if (!failed && !mbar_wait(&wbar[stg], (phase >> stg) & 1u)) failed = true;
       phase ^= 1u << stg;
-      const int64_t tc = t0 + int64_t(wid + WARPS * i) * CH;
-      const int nv = int((t1 - tc) < CH ? (t1 - tc) : CH);
+      const int nv = min(CH, ntok - (wid + WARPS * i) * CH);
       if (nv == CH)
         v3_chunk<true>(ring_s + stg * STAGE_BYTES, cb_s, szs, L, qa, G, lscale, nv, acc, zacc, mrun, lrun);
       else
         v3_chunk<false>(ring_s + stg * STAGE_BYTES, cb_s, szs, L, qa, G, lscale, nv, acc, zacc, mrun, lrun);
-      if (lane == 0 && i + ST < mine) v3_issue(p, b, h, t0, t1, wid + WARPS * (i + ST), stage, &wbar[stg]);
+      if (lane < 4 && i + ST < mine) {
+        const int kc = wid + WARPS * (i + ST);
+        v3_issue(p, src, b, h, t0, min(CH, ntok - kc * CH), kc, stage, &wbar[stg]);
+      }
     }
 
     // ---- warp epilogue: per head (m, l, zero term) -> misc, then the value sums -> record
