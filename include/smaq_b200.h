@@ -184,6 +184,19 @@ size_t smaq_decode_workspace_size(int batch, int n_q_heads, int n_kv_heads, int 
                                   int num_ctas);
 int smaq_decode(const smaq_decode_args* args, void* stream);
 
+/* No counterpart in the reference.  smaq_decode without a caller workspace, for callers that
+ * cannot allocate device memory (all device memory owned by another allocator or pool, or a
+ * host that reaches the GPU only through this ABI).  Scratch comes from a fixed 8 MiB array in
+ * the library's device image (held on every GPU that loads the library until exit; its size is
+ * smaq_decode_noalloc_max_workspace()).  Shapes whose smaq_decode_workspace_size exceeds it are
+ * rejected with SMAQ_ERR_WORKSPACE.  args->workspace / workspace_bytes are ignored.  The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress) with that device
+ * current, so make that first call before any stream capture.  Every call shares the one array
+ * and fully rewrites what it reads, so nothing carries over between calls; calls that can
+ * overlap on the GPU (different streams, or several threads) race on it -- serialise them. */
+int smaq_decode_noalloc(const smaq_decode_args* args, void* stream);
+size_t smaq_decode_noalloc_max_workspace(void);
+
 /* Merge R partial sets [R, B, Hq, 2*D+2] (as written to partial_out) into the
  * final output [B, Hq, D] (element (b, h, d) at out + b*o_stride_b + h*o_stride_h + d). */
 int smaq_merge_partials(const float* partials, int n_parts, int batch, int n_q_heads, int head_dim,

@@ -21,7 +21,7 @@ STATUS = {0: "OK", 1: "INVALID", 2: "UNSUPPORTED", 3: "CUDA", 4: "WORKSPACE", 5:
 EXPORTS = (
     "smaq_abi_version", "smaq_last_error", "smaq_append", "smaq_quantize_keys_scalar",
     "smaq_quantize_values", "smaq_quantize_keys_bvq", "smaq_decode_workspace_size", "smaq_decode",
-    "smaq_merge_partials",
+    "smaq_merge_partials", "smaq_decode_noalloc", "smaq_decode_noalloc_max_workspace",
 )
 
 vp = C.c_void_p
@@ -86,6 +86,9 @@ def load() -> C.CDLL:
     lib.smaq_decode.restype = i32
     lib.smaq_merge_partials.argtypes = [vp, i32, i32, i32, i32, vp, i32, i64, i64, vp]
     lib.smaq_merge_partials.restype = i32
+    lib.smaq_decode_noalloc.argtypes = [C.POINTER(DecodeArgs), vp]
+    lib.smaq_decode_noalloc.restype = i32
+    lib.smaq_decode_noalloc_max_workspace.restype = C.c_size_t
     _lib = lib
     return lib
 

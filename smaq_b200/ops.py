@@ -183,7 +183,7 @@ def decode(q: torch.Tensor, *, n_kv_heads: int, key_format: int, key_codes: torc
            scale: Optional[float] = None, min_history: int = MIN_HISTORY, out: Optional[torch.Tensor] = None,
            partial_out: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
            num_ctas: int = 0, want_out: bool = True, layout: int = SMAQ_LAYOUT_REFERENCE,
-           centroids_f16: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+           centroids_f16: Optional[torch.Tensor] = None, entry: str = "smaq_decode") -> Optional[torch.Tensor]:
     """Batched hybrid decode attention.
 
     ``q``: ``[B, Hq, D]``.  History streams are store rows ``[pages, Hkv, page_size, ...]``;
@@ -251,17 +251,23 @@ def decode(q: torch.Tensor, *, n_kv_heads: int, key_format: int, key_codes: torc
         a.out, a.o_stride_b, a.o_stride_h = out.data_ptr(), out.stride(0), out.stride(1)
     if partial_out is not None:
         a.partial_out = partial_out.data_ptr()
-    need = decode_workspace_bytes(B, Hq, n_kv_heads, D, num_ctas)
-    if workspace is None or workspace.numel() < need:
-        workspace = torch.empty((max(need, 256),), dtype=torch.uint8, device=q.device)
-    keep.append(workspace)
-    a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel()
+    if entry != "smaq_decode_noalloc":
+        need = decode_workspace_bytes(B, Hq, n_kv_heads, D, num_ctas)
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.empty((max(need, 256),), dtype=torch.uint8, device=q.device)
+        keep.append(workspace)
+        a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel()
     a.num_ctas = num_ctas
     a.layout = layout
     if centroids_f16 is not None:
         c16 = centroids_f16.to(torch.float16).contiguous()
         keep.append(c16)
         a.centroids_f16 = c16.data_ptr()
+    if entry == "smaq_decode_noalloc":
+        # fixed scratch inside the library: no workspace is passed (see include/smaq_b200.h)
+        a.workspace, a.workspace_bytes = None, 0
+        _lib.check(lib.smaq_decode_noalloc(a, _stream()), "smaq_decode_noalloc")
+        return out
     _lib.check(lib.smaq_decode(a, _stream()), "smaq_decode")
     return out
 
