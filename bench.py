@@ -343,6 +343,9 @@ def main():
     except Exception:
         peak_gbs = 6650.0
     achieved = bpl / (layer_ms * 1e-3) / 1e9
+    # DRAM bytes per launch from one ncu capture of this workload (profiles/decode_bvq_cfg1_kernel.md)
+    default_shape = (a.batch, a.ctx, a.window, a.hq, a.hkv) == (16, 32768, 128, 32, 8)
+    traffic = 284.2e6 if default_shape else None
     h2d = sum(t.numel() * t.element_size() for t in hq)
     d2h = sum(t.numel() * t.element_size() for t in ho)
     if rank == 0:
@@ -354,7 +357,7 @@ def main():
             "config": config_of(a),
             "hbm_gbs": bpl * a.layers / (ms * 1e-3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s",
-                         "frac": achieved / peak_gbs, "traffic": None, "peak_source": peak_src,
+                         "frac": achieved / peak_gbs, "traffic": traffic, "peak_source": peak_src,
                          "kernel": "smaq_decode (plan+decode+merge) per layer",
                          "algorithmic_bytes_per_launch": bpl},
             "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
