@@ -63,7 +63,7 @@ def up_to_date() -> bool:
 
 def _compile(src: str, verbose_ptxas: bool) -> str:
     obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
-    cmd = [nvcc(), *ARCH, *FLAGS, "-c", src, "-o", obj]
+    cmd = [nvcc(), *ARCH, *FLAGS, *os.environ.get("SMAQ_NVCC_EXTRA", "").split(), "-c", src, "-o", obj]
     if verbose_ptxas:
         cmd += ["-Xptxas", "-v"]
     r = subprocess.run(cmd, capture_output=True, text=True)

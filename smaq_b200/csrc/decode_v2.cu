@@ -32,6 +32,9 @@
 
 namespace smaq {
 
+#ifndef SMAQ_ABL
+#define SMAQ_ABL 0  // profiling builds only: bit 1 skips P.V, 2 skips score MMAs, 4 skips staging
+#endif
 constexpr int CH = 32;  // tokens per chunk
 constexpr int ST_IDX = 0, ST_V = CH * 16, ST_S = CH * 48, ST_Z = CH * 56, STAGE_BYTES = CH * 64;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -39,9 +42,13 @@ constexpr float kLn2 = 0.6931471805599453f;
 
 template <int GM>
 struct V3Cfg {
-  static constexpr int WARPS = 16;
+#ifndef SMAQ_V3_WARPS
+#define SMAQ_V3_WARPS 16
+#define SMAQ_V3_STAGES 3
+#endif
+  static constexpr int WARPS = SMAQ_V3_WARPS;
   static constexpr int THREADS = WARPS * 32;
-  static constexpr int STAGES = 3;
+  static constexpr int STAGES = SMAQ_V3_STAGES;
   static constexpr int CB_BYTES = 256 * 16 * 16;                 // fp16 codebook [c][block'][8]
   static constexpr int Q_BYTES = 8 * 128 * 4;
   static constexpr int SZ_BYTES = 2 * 4 * CH * 2;                // fp16 scales | zeros [j][ks][slot]
@@ -61,11 +68,10 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-__device__ __forceinline__ uint4 lds128(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
-  return v;
-}
+// Shared-memory accesses by 32-bit offset from the start of the dynamic shared window.  Plain C++
+// accesses (not volatile asm) so the compiler may hoist independent loads ahead of the mma chains.
+extern __shared__ __align__(128) uint8_t sm[];
+__device__ __forceinline__ uint4 lds128(uint32_t off) { return *reinterpret_cast<const uint4*>(sm + off); }
 
 // block b of the codebook lives at 16-byte slot sigma(b) of its 256-byte row (see the bank note)
 __host__ __device__ constexpr int cb_sigma(int b) { return b < 8 ? b : 8 + ((b - 8 + 4) & 7); }
@@ -138,19 +144,9 @@ struct V3Lane {
 
 // One 32-token chunk for one warp.  Thread (gid, tig): score/MMA-B role = head gid and the
 // tokens t = 4i + tig; P.V A role = value word gid of those tokens.  FULL: all 32 tokens valid.
-__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-  return v;
-}
-__device__ __forceinline__ uint2 lds64(uint32_t addr) {
-  uint2 v;
-  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
-  return v;
-}
-__device__ __forceinline__ void sts16(uint32_t addr, uint16_t v) {
-  asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v));
-}
+__device__ __forceinline__ uint32_t lds32(uint32_t off) { return *reinterpret_cast<const uint32_t*>(sm + off); }
+__device__ __forceinline__ uint2 lds64(uint32_t off) { return *reinterpret_cast<const uint2*>(sm + off); }
+__device__ __forceinline__ void sts16(uint32_t off, uint16_t v) { *reinterpret_cast<uint16_t*>(sm + off) = v; }
 __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
   uint32_t r;
   asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
@@ -168,7 +164,7 @@ __device__ __forceinline__ void v3_chunk(uint32_t st, uint32_t cb_s, uint32_t sz
   const int gid = lane >> 2, tig = lane & 3;
 
   // ---- the chunk's value scales and zeros as fp16, in MMA k-slot order (one token per lane)
-  {
+  if (!(SMAQ_ABL & 4)) {
     uint2 s2 = lds64(st + ST_S + lane * 8);
     uint2 z2 = lds64(st + ST_Z + lane * 8);
     if (!FULL && lane >= nv) s2 = z2 = make_uint2(0u, 0u);  // rows past the end may hold anything
@@ -185,17 +181,21 @@ __device__ __forceinline__ void v3_chunk(uint32_t st, uint32_t cb_s, uint32_t sz
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const uint32_t w = lds32(st + ST_IDX + L.idx_off + i * 64);
-    const uint4 e0 = lds128(cb_s + __byte_perm(w, L.base[0], L.sel[0]));
-    const uint4 e1 = lds128(cb_s + __byte_perm(w, L.base[1], L.sel[1]));
+    uint4 e0, e1;
+    if (SMAQ_ABL & 16) { e0 = make_uint4(w, w, w, w); e1 = e0; } else {
+    e0 = lds128(cb_s + __byte_perm(w, L.base[0], L.sel[0]));
+    e1 = lds128(cb_s + __byte_perm(w, L.base[1], L.sel[1])); }
     float d[4] = {0.f, 0.f, 0.f, 0.f};
+    if (SMAQ_ABL & 2) { d[0] = __uint_as_float(e0.x ^ e1.w); } else {
     mma_f16_16816(d, qa[0], e0.x, e0.y);
     mma_f16_16816(d, qa[1], e0.z, e0.w);
     mma_f16_16816(d, qa[2], e1.x, e1.y);
-    mma_f16_16816(d, qa[3], e1.z, e1.w);
+    mma_f16_16816(d, qa[3], e1.z, e1.w); }
     const float sc = (d[0] + d[3]) * lscale;
     s[i] = (FULL || 4 * i + tig < nv) ? sc : -INFINITY;  // heads >= G score 0: harmless
   }
   // ---- online softmax for head gid over the 8 tokens of this thread and its 3 tig peers
+  if (!(SMAQ_ABL & 8)) {
   float mx = fmaxf(fmaxf(fmaxf(s[0], s[1]), fmaxf(s[2], s[3])), fmaxf(fmaxf(s[4], s[5]), fmaxf(s[6], s[7])));
   mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
   mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
@@ -220,10 +220,11 @@ __device__ __forceinline__ void v3_chunk(uint32_t st, uint32_t cb_s, uint32_t sz
     }
     zacc[0] *= aa; zacc[1] *= ab; zacc[2] *= aa; zacc[3] *= ab;
   }
+  } else { lrun += s[0] + s[1] + s[2] + s[3] + s[4] + s[5] + s[6] + s[7]; }
   __syncwarp();  // fp16 scales / zeros visible to the warp
   // ---- P.V: k-step ks covers tokens 16ks + tig + 4u (u = 0..3) = this thread's s[4ks + u]
 #pragma unroll
-  for (int ks = 0; ks < 2; ++ks) {
+  for (int ks = 0; ks < ((SMAQ_ABL & 1) ? 0 : 2); ++ks) {
     const uint32_t p01 = pack_f16x2(s[4 * ks + 0], s[4 * ks + 1]);   // k-slots 2tig, 2tig+1
     const uint32_t p23 = pack_f16x2(s[4 * ks + 2], s[4 * ks + 3]);   // k-slots 2tig+8, 2tig+9
     const uint32_t sb = szs + ks * 32 + tig * 4;
@@ -268,7 +269,6 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
   constexpr int D = 128;
   constexpr int ST = C::STAGES;
   constexpr int WARPS = C::WARPS;
-  extern __shared__ __align__(128) uint8_t sm[];
   uint8_t* cb = sm;
   float* qs = reinterpret_cast<float*>(sm + C::CB_BYTES);
   uint8_t* wreg0 = sm + C::CB_BYTES + C::Q_BYTES;
@@ -278,7 +278,7 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
   const int gid = lane >> 2, tig = lane & 3;
   const int G = p.G;
   uint8_t* wreg = wreg0 + wid * C::WARP_BYTES;                       // ring | s,z | misc
-  const uint32_t szs = smem_u32(wreg + ST * STAGE_BYTES);
+  const uint32_t szs = uint32_t(wreg + ST * STAGE_BYTES - sm);
   float* misc = reinterpret_cast<float*>(wreg + ST * STAGE_BYTES + C::SZ_BYTES);
   float* rec = reinterpret_cast<float*>(wreg);                       // merge record (after the loop)
   uint64_t* wbar = bars + wid * ST;
@@ -295,13 +295,6 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
   const int64_t lo = int64_t(c) * per, hi = min(lo + per, total);
   if (lo >= hi) return;
 
-  // codebook -> shared, entry (block b, code cc) at cc * 256 + sigma(b) * 16
-  for (int u = threadIdx.x; u < 16 * 256; u += blockDim.x) {
-    const int blk = u >> 8, cc = u & 255;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (cc < p.nc) v = __ldg(reinterpret_cast<const uint4*>(cb16) + blk * p.nc + cc);
-    *reinterpret_cast<uint4*>(cb + cc * 256 + cb_sigma(blk) * 16) = v;
-  }
   // per-lane constants of the score gather (B column = (token gid>>1, half gid&1), block quad tig)
   V3Lane L;
   {
@@ -317,8 +310,9 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
       L.sel[kp] = 0x6504u | (uint32_t((tig & 1) * 2 + kp) << 4);
     }
   }
-  const uint32_t cb_s = smem_u32(cb);
-  const uint32_t ring_s = smem_u32(wreg);
+  bool cb_ready = false;
+  const uint32_t cb_s = uint32_t(cb - sm);
+  const uint32_t ring_s = uint32_t(wreg - sm);
   __syncthreads();
 
   int sa = 0, sb_ = p.n_seg - 1;
@@ -342,96 +336,7 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
       const int g = i / D, d = i - g * D;
       qs[i] = g < G ? load_elem(p.q, p.q_dtype, b * p.q_sb + int64_t(h * G + g) * p.q_sh + d) : 0.f;
     }
-    if (s & 1) {
-      // ---------------- exact recent window (SIMT; a few percent of the bytes)
-      __syncthreads();
-      WarpState<GM> st;
-      st.init();
-      const int64_t nch = (t1 - t0 + 31) / 32;
-      for (int64_t ch = wid; ch < nch; ch += WARPS) {
-        const int64_t tb = t0 + ch * 32;
-        const int nvalid = int((t1 - tb) < 32 ? (t1 - tb) : 32);
-        float sc[GM];
-#pragma unroll
-        for (int g = 0; g < GM; ++g) sc[g] = -INFINITY;
-        if (lane < nvalid) {
-          const int64_t rb = b * p.r_sb + (tb + lane) * p.r_st + h * p.r_sh;
-          float a[GM];
-#pragma unroll
-          for (int g = 0; g < GM; ++g) a[g] = 0.f;
-          if (p.r_dtype == SMAQ_BF16) {
-            const uint4* kr = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.rk) + rb);
-#pragma unroll 4
-            for (int i = 0; i < 16; ++i) {
-              const uint4 kv = __ldg(kr + i);
-              const uint32_t w[4] = {kv.x, kv.y, kv.z, kv.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float k0 = bf16lo(w[e]), k1 = bf16hi(w[e]);
-#pragma unroll
-                for (int g = 0; g < GM; ++g) {
-                  const float2 qq = *reinterpret_cast<const float2*>(qs + g * D + i * 8 + e * 2);
-                  a[g] = fmaf(qq.x, k0, a[g]);
-                  a[g] = fmaf(qq.y, k1, a[g]);
-                }
-              }
-            }
-          } else {
-            for (int d = 0; d < D; ++d) {
-              const float kv = load_elem(p.rk, p.r_dtype, rb + d);
-#pragma unroll
-              for (int g = 0; g < GM; ++g) a[g] = fmaf(qs[g * D + d], kv, a[g]);
-            }
-          }
-#pragma unroll
-          for (int g = 0; g < GM; ++g) sc[g] = a[g] * p.scale;
-        }
-        st.softmax_chunk(sc, GM);
-#pragma unroll
-        for (int jb = 0; jb < 4; ++jb) {
-          float v[8][4];
-#pragma unroll
-          for (int jj = 0; jj < 8; ++jj) {
-            const int j = jb * 8 + jj;
-            if (j < nvalid) {
-              const int64_t rb = b * p.r_sb + (tb + j) * p.r_st + h * p.r_sh + lane * 4;
-              if (p.r_dtype == SMAQ_BF16) {
-                const uint2 u =
-                    __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p.rv) + rb));
-                v[jj][0] = bf16lo(u.x); v[jj][1] = bf16hi(u.x); v[jj][2] = bf16lo(u.y); v[jj][3] = bf16hi(u.y);
-              } else {
-#pragma unroll
-                for (int e = 0; e < 4; ++e) v[jj][e] = load_elem(p.rv, p.r_dtype, rb + e);
-              }
-            } else {
-#pragma unroll
-              for (int e = 0; e < 4; ++e) v[jj][e] = 0.f;
-            }
-          }
-#pragma unroll
-          for (int jj = 0; jj < 8; ++jj) {
-#pragma unroll
-            for (int g = 0; g < GM; ++g) {
-              const float pj = __shfl_sync(0xffffffffu, sc[g], jb * 8 + jj);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) st.acc[g][e] = fmaf(pj, v[jj][e], st.acc[g][e]);
-            }
-          }
-        }
-      }
-#pragma unroll
-      for (int g = 0; g < GM; ++g) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) rec[g * D + lane * 4 + e] = st.acc[g][e];
-        if (lane == 0) {
-          rec[GM * D + g * 2] = st.m[g];
-          rec[GM * D + g * 2 + 1] = st.l[g];
-        }
-      }
-      __syncthreads();
-      v3_merge<GM, WARPS>(p, reinterpret_cast<const float*>(wreg0), C::WARP_BYTES / 4, c + s);
-      continue;
-    }
+    if (s & 1) continue;  // the exact window is attended by decode_finish_kernel
 
     // ---------------- compressed history
     const int ntok = int(t1 - t0);
@@ -454,7 +359,17 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
         v3_issue(p, src, b, h, t0, min(CH, ntok - kc * CH), kc, wreg + i * STAGE_BYTES, &wbar[i]);
       }
     }
-    __syncthreads();  // qs complete
+    if (!cb_ready) {  // first history segment: copy the codebook while its first chunks load
+      // codebook -> shared, entry (block b, code cc) at cc * 256 + sigma(b) * 16
+      for (int u = threadIdx.x; u < 16 * 256; u += blockDim.x) {
+        const int blk = u >> 8, cc = u & 255;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (cc < p.nc) v = __ldg(reinterpret_cast<const uint4*>(cb16) + blk * p.nc + cc);
+        *reinterpret_cast<uint4*>(cb + cc * 256 + cb_sigma(blk) * 16) = v;
+      }
+      cb_ready = true;
+    }
+    __syncthreads();  // qs and codebook complete
     // A fragments of the score MMA: rows (head gid, half 0) and (head gid, half 1); k-step ks
     // covers dims 8*(8*half + 4*(ks>>1) + tig) + 4*(ks&1) + {0,1 | 2,3}
     uint32_t qa[4][4];
