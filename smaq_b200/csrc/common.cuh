@@ -46,6 +46,57 @@ __device__ __forceinline__ float rnd<BF16>(float x) { return __bfloat162float(__
 template <>
 __device__ __forceinline__ float rnd<F16>(float x) { return __half2float(__float2half_rn(x)); }
 
+// Two values rounded to the storage type at once (one packed conversion for bf16 / fp16).
+template <class DT>
+__device__ __forceinline__ void rnd2(float& a, float& b);
+template <>
+__device__ __forceinline__ void rnd2<F32>(float&, float&) {}
+template <>
+__device__ __forceinline__ void rnd2<BF16>(float& a, float& b) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  a = __uint_as_float(r << 16);
+  b = __uint_as_float(r & 0xFFFF0000u);
+}
+template <>
+__device__ __forceinline__ void rnd2<F16>(float& a, float& b) {
+  const float2 f = __half22float2(__floats2half2_rn(a, b));
+  a = f.x;
+  b = f.y;
+}
+
+// Correctly rounded x / d, kept out of line so that the rare exact-division paths below stay
+// branches instead of being if-converted into every element.
+static __device__ __noinline__ float div_exact(float x, float d) { return __fdiv_rn(x, d); }
+
+// A quotient q with rnd<DT>(q) == rnd<DT>(x / d) for x, d values of DT, given rcp = 1/d
+// rounded to nearest; x * rcp is within 2^-22 relative of x / d.
+//  - bf16: a quotient of two bf16 values is never exactly a bf16 rounding midpoint
+//    (X * 2^p = m * D has no solution with X, D 8-bit significands and m an odd 9-bit integer:
+//    the odd part of the left side is at most 255), and otherwise lies at least
+//    1 / (511 * 255) > 2^-17 relative from every midpoint, so x * rcp rounds like x / d.  Only a
+//    quotient below 2^-126 (an fp32 subnormal product) can differ, by 2^-149; the callers
+//    either clamp such values away (value scales and codes) or feed them to an fp32 contraction
+//    whose rounding band is far wider (unit keys).
+//  - fp16 (11-bit significands) has no such margin: x * rcp is used unless it lies within a few
+//    fp32 ulps of an fp16 rounding midpoint or outside fp16's normal range, where the exact
+//    division is evaluated.
+//  - fp32 storage needs the exact quotient and always divides.
+template <class DT>
+__device__ __forceinline__ float quot(float x, float d, float rcp);
+template <>
+__device__ __forceinline__ float quot<F32>(float x, float d, float) { return __fdiv_rn(x, d); }
+template <>
+__device__ __forceinline__ float quot<BF16>(float x, float, float rcp) { return x * rcp; }
+template <>
+__device__ __forceinline__ float quot<F16>(float x, float d, float rcp) {
+  const float q = x * rcp;
+  const uint32_t u = __float_as_uint(q);
+  const uint32_t ex = (u >> 23) & 0xFFu;  // fp16 normal range: biased fp32 exponent 113..142
+  if (((u + 32u) & 0x1FC0u) == 0x1000u || (ex < 113u && (u << 1) != 0u) || ex > 142u) return div_exact(x, d);
+  return q;
+}
+
 template <class DT>
 __device__ __forceinline__ typename DT::T from_f(float x);
 template <>
@@ -113,12 +164,60 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// Store-row index of chunk token t, head h (see include/smaq_b200.h).
-__device__ __forceinline__ int64_t store_row(const int64_t* slots, int64_t slot_offset,
-                                             int64_t page_size, int n_heads, int64_t t, int h) {
-  const int64_t s = slots ? slots[t] : slot_offset + t;
-  const int64_t page = s / page_size;
-  return (page * n_heads + h) * page_size + (s - page * page_size);
+// n / d for 0 <= n < 2^31 by a multiply-high and a shift (Granlund & Montgomery, "Division by
+// invariant integers using multiplication", 1994): l = ceil(log2 d), m = floor(2^32 (2^l - d) / d) + 1,
+// n / d = (umulhi(n, m) + n) >> l.  d == 0 marks a divisor beyond 2^31 - 1 (callers divide in 64 bits).
+struct FastDiv {
+  uint32_t d, m, l;
+};
+inline FastDiv make_fastdiv(int64_t d) {
+  FastDiv f{0u, 0u, 0u};
+  if (d < 1 || d >= (int64_t(1) << 31)) return f;
+  uint32_t l = 0;
+  while ((uint64_t(1) << l) < uint64_t(d)) ++l;
+  f.d = uint32_t(d);
+  f.m = uint32_t(((uint64_t(1) << 32) * ((uint64_t(1) << l) - uint64_t(d))) / uint64_t(d) + 1);
+  f.l = l;
+  return f;
+}
+
+// Destination rows of an append (see include/smaq_b200.h): chunk row r = t * n_heads + h,
+// token t lands in slot s = slots ? slots[t] : slot_offset + t, and
+// row = (s / page_size * n_heads + h) * page_size + s % page_size.
+struct RowMap {
+  const int64_t* slots;
+  int64_t slot_offset;
+  int64_t page_size;
+  int n_heads;
+  FastDiv hdiv, pdiv;
+
+  __device__ __forceinline__ void token_head(int64_t r, int64_t& t, int& h) const {
+    if (r < (int64_t(1) << 31))
+      t = int64_t((__umulhi(uint32_t(r), hdiv.m) + uint32_t(r)) >> hdiv.l);
+    else
+      t = r / n_heads;
+    h = int(r - t * n_heads);
+  }
+  __device__ __forceinline__ int64_t row(int64_t t, int h) const {
+    const int64_t s = slots ? slots[t] : slot_offset + t;
+    int64_t page;
+    if (pdiv.d != 0u && s >= 0 && s < (int64_t(1) << 31))
+      page = int64_t((__umulhi(uint32_t(s), pdiv.m) + uint32_t(s)) >> pdiv.l);
+    else
+      page = s / page_size;
+    return (page * n_heads + h) * page_size + (s - page * page_size);
+  }
+};
+
+inline RowMap make_rowmap(const smaq_append_args& a) {
+  RowMap m;
+  m.slots = a.slots;
+  m.slot_offset = a.slot_offset;
+  m.page_size = a.page_size;
+  m.n_heads = a.n_heads;
+  m.hdiv = make_fastdiv(a.n_heads);
+  m.pdiv = make_fastdiv(a.page_size);
+  return m;
 }
 
 }  // namespace smaq

@@ -22,7 +22,7 @@ namespace smaq {
 template <class DT, int EPL, int BITS>
 __global__ void __launch_bounds__(256) value_quant_kernel(
     const typename DT::T* __restrict__ v, int64_t n_tokens, int n_heads, int64_t st, int64_t sh,
-    const int64_t* __restrict__ slots, int64_t slot_offset, int64_t page_size, int group_size,
+    const RowMap rm, int group_size,
     uint8_t* __restrict__ data, typename DT::T* __restrict__ scales, typename DT::T* __restrict__ zeros,
     int layout) {
   constexpr int D = 32 * EPL;
@@ -35,8 +35,9 @@ __global__ void __launch_bounds__(256) value_quant_kernel(
   const int ng = D / group_size;
   const float floor_ = rnd<DT>(1e-10f);
   for (int64_t r = warp; r < n_rows; r += nwarps) {
-    const int64_t t = r / n_heads;
-    const int h = int(r - t * n_heads);
+    int64_t t;
+    int h;
+    rm.token_head(r, t, h);
     float x[EPL];
     load_vec<DT, EPL>(v + t * st + h * sh + lane * EPL, x);
     float mn = x[0], mx = x[0];
@@ -50,17 +51,29 @@ __global__ void __launch_bounds__(256) value_quant_kernel(
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     }
     // scale = ((max - min) / n_levels).clamp(min=1e-10); zero = min   (kv_cache.py:78-83)
-    float scale = rnd<DT>(__fdiv_rn(rnd<DT>(mx - mn), float(NL)));
+    float scale = rnd<DT>(quot<DT>(rnd<DT>(mx - mn), float(NL), 1.0f / float(NL)));
     if (scale < floor_) scale = floor_;
+    const float rscale = __frcp_rn(scale);
+    // ((v - zero) / scale).round().clamp(0, n_levels)   (kv_cache.py:85).  Clamping before the
+    // round-half-even is the same as after it (the bounds are integers); the rounding is the
+    // 1.5 * 2^23 addition, whose low mantissa bits are then the code.  NaN -> 0 like the
+    // reference's uint8 cast.
+    float d[EPL];
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) d[i] = x[i] - mn;
+#pragma unroll
+    for (int i = 0; i < EPL; i += 2) rnd2<DT>(d[i], d[i + 1]);
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) d[i] = quot<DT>(d[i], scale, rscale);
+#pragma unroll
+    for (int i = 0; i < EPL; i += 2) rnd2<DT>(d[i], d[i + 1]);
     uint32_t packed = 0;
 #pragma unroll
     for (int i = 0; i < EPL; ++i) {
-      // ((v - zero) / scale).round().clamp(0, n_levels)   (kv_cache.py:85)
-      float q = rnd<DT>(__fdiv_rn(rnd<DT>(x[i] - mn), scale));
-      q = fminf(fmaxf(rintf(q), 0.0f), float(NL));  // NaN -> 0 like the reference's uint8 cast
-      packed |= uint32_t(q) << (i * BITS);
+      const float q = fminf(fmaxf(d[i], 0.0f), float(NL)) + 12582912.0f;
+      packed |= (__float_as_uint(q) - 0x4B400000u) << (i * BITS);
     }
-    const int64_t row = store_row(slots, slot_offset, page_size, n_heads, t, h);
+    const int64_t row = rm.row(t, h);
     constexpr int LANE_BITS = EPL * BITS;
     uint8_t* dst = data + row * (D * BITS / 8);
     if constexpr (LANE_BITS >= 8) {
@@ -97,7 +110,7 @@ constexpr int SQ_ROWS = 8;
 template <class DT, int EPL, int BITS>
 __global__ void __launch_bounds__(SQ_WARPS * 32) scalar_key_kernel(
     const typename DT::T* __restrict__ k, int64_t n_tokens, int n_heads, int64_t st, int64_t sh,
-    const int64_t* __restrict__ slots, int64_t slot_offset, int64_t page_size,
+    const RowMap rm,
     const float* __restrict__ E, const float* __restrict__ bnd, uint8_t* __restrict__ codes,
     typename DT::T* __restrict__ norms) {
   constexpr int D = 32 * EPL;
@@ -129,8 +142,9 @@ __global__ void __launch_bounds__(SQ_WARPS * 32) scalar_key_kernel(
       const int64_t r = r0 + rr;
       float x[EPL];
       if (r < n_rows) {
-        const int64_t t = r / n_heads;
-        const int h = int(r - t * n_heads);
+        int64_t t;
+        int h;
+        rm.token_head(r, t, h);
         load_vec<DT, EPL>(k + t * st + h * sh + lane * EPL, x);
       } else {
 #pragma unroll
@@ -144,8 +158,13 @@ __global__ void __launch_bounds__(SQ_WARPS * 32) scalar_key_kernel(
       const float n = rnd<DT>(sqrtf(ss));
       nrm[rr] = n;
       const float den = rnd<DT>(n + 1e-10f);
+      const float rden = __frcp_rn(den);
 #pragma unroll
-      for (int i = 0; i < EPL; ++i) ku[rr * D + lane * EPL + i] = rnd<DT>(__fdiv_rn(x[i], den));
+      for (int i = 0; i < EPL; ++i) x[i] = quot<DT>(x[i], den, rden);
+#pragma unroll
+      for (int i = 0; i < EPL; i += 2) rnd2<DT>(x[i], x[i + 1]);
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) ku[rr * D + lane * EPL + i] = x[i];
     }
     __syncwarp();
     // y = k_unit.float() @ E.T  (quantizer.py:142)
@@ -176,9 +195,10 @@ __global__ void __launch_bounds__(SQ_WARPS * 32) scalar_key_kernel(
     for (int rr = 0; rr < SQ_ROWS; ++rr) {
       const int64_t r = r0 + rr;
       if (r >= n_rows) break;
-      const int64_t t = r / n_heads;
-      const int h = int(r - t * n_heads);
-      const int64_t row = store_row(slots, slot_offset, page_size, n_heads, t, h);
+      int64_t t;
+      int h;
+      rm.token_head(r, t, h);
+      const int64_t row = rm.row(t, h);
       // searchsorted(decision_boundaries, y), right=False: count of boundaries < y  (:143)
       uint32_t c[EPL];
 #pragma unroll
@@ -219,7 +239,7 @@ constexpr int BQ_ROWS = 4;
 template <class DT, int EPL>
 __global__ void __launch_bounds__(BQ_WARPS * 32) bvq_key_kernel(
     const typename DT::T* __restrict__ k, int64_t n_tokens, int n_heads, int64_t st, int64_t sh,
-    const int64_t* __restrict__ slots, int64_t slot_offset, int64_t page_size,
+    const RowMap rm,
     const float* __restrict__ Eb, const float* __restrict__ cent, int nc, uint8_t* __restrict__ out,
     int layout) {
   constexpr int D = 32 * EPL;
@@ -252,8 +272,9 @@ __global__ void __launch_bounds__(BQ_WARPS * 32) bvq_key_kernel(
       const int64_t r = r0 + rr;
       float x[EPL];
       if (r < n_rows) {
-        const int64_t t = r / n_heads;
-        const int h = int(r - t * n_heads);
+        int64_t t;
+        int h;
+        rm.token_head(r, t, h);
         load_vec<DT, EPL>(k + t * st + h * sh + lane * EPL, x);
       } else {
 #pragma unroll
@@ -337,9 +358,10 @@ __global__ void __launch_bounds__(BQ_WARPS * 32) bvq_key_kernel(
         for (int rr = 0; rr < BQ_ROWS; ++rr) {
           const int64_t r = r0 + rr;
           if (r < n_rows) {
-            const int64_t t = r / n_heads;
-            const int h = int(r - t * n_heads);
-            const int64_t row = store_row(slots, slot_offset, page_size, n_heads, t, h);
+            int64_t t;
+            int h;
+            rm.token_head(r, t, h);
+            const int64_t row = rm.row(t, h);
             int64_t off = row * NBLK + blk;
             if (layout == SMAQ_LAYOUT_DECODE)  // see include/smaq_b200.h
               off = row * NBLK + 2 * (4 * (blk >> 3) + (blk & 3)) + ((blk >> 2) & 1);
@@ -370,13 +392,13 @@ static int launch_values_t(const smaq_append_args& a, cudaStream_t s) {
   using T = typename DT::T;
   if (a.value_bits == 2)
     value_quant_kernel<DT, EPL, 2><<<grid, 256, 0, s>>>(
-        static_cast<const T*>(a.v), a.n_tokens, a.n_heads, a.v_stride_t, a.v_stride_h, a.slots,
-        a.slot_offset, a.page_size, a.group_size, a.v_data, static_cast<T*>(a.v_scales),
+        static_cast<const T*>(a.v), a.n_tokens, a.n_heads, a.v_stride_t, a.v_stride_h, make_rowmap(a),
+        a.group_size, a.v_data, static_cast<T*>(a.v_scales),
         static_cast<T*>(a.v_zeros), a.layout);
   else
     value_quant_kernel<DT, EPL, 4><<<grid, 256, 0, s>>>(
-        static_cast<const T*>(a.v), a.n_tokens, a.n_heads, a.v_stride_t, a.v_stride_h, a.slots,
-        a.slot_offset, a.page_size, a.group_size, a.v_data, static_cast<T*>(a.v_scales),
+        static_cast<const T*>(a.v), a.n_tokens, a.n_heads, a.v_stride_t, a.v_stride_h, make_rowmap(a),
+        a.group_size, a.v_data, static_cast<T*>(a.v_scales),
         static_cast<T*>(a.v_zeros), SMAQ_LAYOUT_REFERENCE);
   return cuda_status(cudaGetLastError(), "value_quant_kernel");
 }
@@ -402,7 +424,7 @@ static int launch_scalar_t(const smaq_append_args& a, cudaStream_t s) {
   const int grid = grid_for((rows + SQ_ROWS - 1) / SQ_ROWS, SQ_WARPS, 2);
   using T = typename DT::T;
   kern<<<grid, SQ_WARPS * 32, sm, s>>>(static_cast<const T*>(a.k), a.n_tokens, a.n_heads, a.k_stride_t,
-                                       a.k_stride_h, a.slots, a.slot_offset, a.page_size, a.E,
+                                       a.k_stride_h, make_rowmap(a), a.E,
                                        a.boundaries, a.key_codes, static_cast<T*>(a.key_norms));
   return cuda_status(cudaGetLastError(), "scalar_key_kernel");
 }
@@ -420,7 +442,7 @@ static int launch_scalar_b(const smaq_append_args& a, cudaStream_t s) {
 template <class DT>
 static int launch_scalar_d(const smaq_append_args& a, cudaStream_t s) {
   if constexpr (std::is_same<DT, BF16>::value) {
-    if (a.head_dim == 128 && tc_rotate_enabled()) return launch_scalar_keys_tc(a, s);
+    if (tc_rotate_eligible(a)) return launch_scalar_keys_tc(a, s);
   }
   switch (a.head_dim) {
     case 64: return launch_scalar_b<DT, 2>(a, s);
@@ -442,7 +464,7 @@ static int launch_bvq_t(const smaq_append_args& a, cudaStream_t s) {
   const int grid = grid_for((rows + BQ_ROWS - 1) / BQ_ROWS, BQ_WARPS, 1);
   using T = typename DT::T;
   kern<<<grid, BQ_WARPS * 32, sm, s>>>(static_cast<const T*>(a.k), a.n_tokens, a.n_heads, a.k_stride_t,
-                                       a.k_stride_h, a.slots, a.slot_offset, a.page_size, a.E_blocks,
+                                       a.k_stride_h, make_rowmap(a), a.E_blocks,
                                        a.centroids, nc, a.key_codes, a.layout);
   return cuda_status(cudaGetLastError(), "bvq_key_kernel");
 }
