@@ -100,6 +100,117 @@ __global__ void __launch_bounds__(256) value_quant_kernel(
 }
 
 // =====================================================================================
+// values, bf16 / head_dim 128 / group 32 / 2 bits: one thread per group of 32 elements (four
+// threads per row).  Every step is a packed bf16x2 operation where the reference's fp32-then-bf16
+// rounding allows it: bf16 subtraction and min/max are exact-then-rounded; the division goes
+// through the reciprocal (see quot<BF16>); round-half-even is the bf16 addition of 192, whose
+// ulp is 1 on [128, 256), so the code is the low bits of the sum.
+// =====================================================================================
+__device__ __forceinline__ uint32_t bf2_sub(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf2_add(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf2_min(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("min.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf2_max(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf2_pack(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__global__ void __launch_bounds__(256) value_bf16_g32_kernel(
+    const __nv_bfloat16* __restrict__ v, int64_t n_tokens, int n_heads, int64_t st, int64_t sh, const RowMap rm,
+    uint8_t* __restrict__ data, __nv_bfloat16* __restrict__ scales, __nv_bfloat16* __restrict__ zeros, int layout) {
+  const int64_t gid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t n_rows = n_tokens * n_heads;
+  const int64_t r = gid >> 2;
+  const int g = int(gid & 3);
+  const bool live = r < n_rows;
+  int64_t t = 0;
+  int h = 0;
+  uint32_t x[16];
+  if (live) {
+    rm.token_head(r, t, h);
+    const uint4* src = reinterpret_cast<const uint4*>(v + t * st + h * sh + 32 * g);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 u = __ldg(src + i);
+      x[4 * i] = u.x; x[4 * i + 1] = u.y; x[4 * i + 2] = u.z; x[4 * i + 3] = u.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) x[i] = 0u;
+  }
+  // min / max over the group (NaN-ignoring, like fminf)
+  uint32_t mn2 = x[0], mx2 = x[0];
+#pragma unroll
+  for (int i = 1; i < 16; ++i) {
+    mn2 = bf2_min(mn2, x[i]);
+    mx2 = bf2_max(mx2, x[i]);
+  }
+  const float mn = fminf(__uint_as_float(mn2 << 16), __uint_as_float(mn2 & 0xFFFF0000u));
+  const float mx = fmaxf(__uint_as_float(mx2 << 16), __uint_as_float(mx2 & 0xFFFF0000u));
+  // scale = ((max - min) / 3).clamp(min=1e-10); zero = min   (kv_cache.py:78-83)
+  float scale = rnd<BF16>(quot<BF16>(rnd<BF16>(mx - mn), 3.0f, 1.0f / 3.0f));
+  const float floor_ = rnd<BF16>(1e-10f);
+  if (scale < floor_) scale = floor_;
+  const float rscale = __frcp_rn(scale);
+  const uint32_t mnb = __float_as_uint(mn) >> 16;
+  const uint32_t mn_pair = mnb | (mnb << 16);
+  // ((v - zero) / scale).round().clamp(0, 3)   (kv_cache.py:85); NaN -> 0
+  const uint32_t zero2 = 0u, three2 = 0x40404040u, magic2 = 0x43404340u;  // bf16 pairs 0, 3, 192
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t d = bf2_sub(x[i], mn_pair);
+    uint32_t q = bf2_pack(__uint_as_float(d << 16) * rscale, __uint_as_float(d & 0xFFFF0000u) * rscale);
+    q = bf2_add(bf2_min(bf2_max(q, zero2), three2), magic2);
+    const uint32_t c = ((q - magic2) & 0x3u) | (((q - magic2) >> 14) & 0xCu);  // codes 2i, 2i+1
+    if (i < 8) lo |= c << (4 * i);
+    else hi |= c << (4 * (i - 8));
+  }
+  if (layout == SMAQ_LAYOUT_DECODE) {
+    // byte 4 * b + g of the row holds reference byte 8 * g + b (b < 8): transpose the 4 x 8
+    // byte matrix held by the row's four threads.  16-bit chunk c of thread g = bytes 2c, 2c+1.
+    uint32_t send = (g & 2) ? lo : hi;
+    uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 2);
+    if (g & 2) lo = recv; else hi = recv;
+    // now lo = chunks {2*b1, 2*b1+1}... of sources with bit1 = 0, hi = of sources with bit1 = 1
+    send = (g & 1) ? __byte_perm(lo, hi, 0x5410) : __byte_perm(lo, hi, 0x7632);
+    recv = __shfl_xor_sync(0xffffffffu, send, 1);
+    uint32_t c01, c23;  // chunk g of sources (0, 1) and (2, 3)
+    if (g & 1) {
+      c01 = __byte_perm(recv, lo, 0x7610);  // source 0 from partner (low), source 1 own (lo high)
+      c23 = __byte_perm(recv, hi, 0x7632);  // source 2 from partner (high), source 3 own (hi high)
+    } else {
+      c01 = __byte_perm(lo, recv, 0x5410);  // source 0 own (lo low), source 1 from partner (low)
+      c23 = __byte_perm(hi, recv, 0x7610);  // source 2 own (hi low), source 3 from partner (high)
+    }
+    lo = __byte_perm(c01, c23, 0x6420);  // byte 2g of sources 0..3
+    hi = __byte_perm(c01, c23, 0x7531);  // byte 2g + 1 of sources 0..3
+  }
+  if (!live) return;  // after the shuffles: whole rows are live or not, warps stay converged
+  const int64_t row = rm.row(t, h);
+  reinterpret_cast<uint2*>(data + row * 32)[g] = make_uint2(lo, hi);
+  scales[row * 4 + g] = __float2bfloat16_rn(scale);
+  zeros[row * 4 + g] = __float2bfloat16_rn(mn);
+}
+
+// =====================================================================================
 // scalar keys (SIMT path): a warp quantizes R rows at a time; E^T and the k_unit rows are
 // staged in shared memory.  Used for fp32/fp16 keys and for head_dim != 128; bf16 keys at
 // head_dim 128 take the tcgen05 path in tc_rotate.cuh.
@@ -405,6 +516,19 @@ static int launch_values_t(const smaq_append_args& a, cudaStream_t s) {
 
 template <class DT>
 static int launch_values_d(const smaq_append_args& a, cudaStream_t s) {
+  if constexpr (std::is_same<DT, BF16>::value) {
+    if (a.head_dim == 128 && a.group_size == 32 && a.value_bits == 2 &&
+        reinterpret_cast<uintptr_t>(a.v) % 16 == 0 && a.v_stride_t % 8 == 0 && a.v_stride_h % 8 == 0 &&
+        reinterpret_cast<uintptr_t>(a.v_data) % 8 == 0) {
+      const int64_t threads = a.n_tokens * a.n_heads * 4;
+      const int64_t blocks = (threads + 255) / 256;
+      if (blocks > 0)
+        value_bf16_g32_kernel<<<unsigned(blocks), 256, 0, s>>>(
+            static_cast<const __nv_bfloat16*>(a.v), a.n_tokens, a.n_heads, a.v_stride_t, a.v_stride_h, make_rowmap(a),
+            a.v_data, static_cast<__nv_bfloat16*>(a.v_scales), static_cast<__nv_bfloat16*>(a.v_zeros), a.layout);
+      return cuda_status(cudaGetLastError(), "value_bf16_g32_kernel");
+    }
+  }
   switch (a.head_dim) {
     case 64: return launch_values_t<DT, 2>(a, s);
     case 128: return launch_values_t<DT, 4>(a, s);

@@ -4,22 +4,24 @@
 //   norms = k.norm(-1); k_unit = k / (norms + 1e-10); y = k_unit.float() @ E.T;
 //   idx = searchsorted(decision_boundaries, y); pack LSB-first.
 //
-// The d x d contraction runs on the 5th-generation tensor cores.  k_unit is a bf16 tensor, so it
-// is exact as the A operand.  E is fp32; it is split into three bf16 matrices
-// E = E_hi + E_mid + E_lo (each the bf16 rounding of what the previous ones leave), which holds
-// E to ~2^-27 relative, and the three products accumulate in one fp32 TMEM accumulator:
-// y = A E_lo^T + A E_mid^T + A E_hi^T.  The result agrees with the reference's fp32 matmul up to
-// fp32 accumulation-order differences, the same band the SIMT kernel has.
+// The d x d contraction runs on the 5th-generation tensor cores in split precision.  k_unit is
+// a bf16 tensor, so it is exact as the A operand.  E is fp32; it is split into three bf16
+// matrices E = E_hi + E_mid + E_lo (each the bf16 rounding of what the previous ones leave),
+// which holds E to ~2^-27 relative, and the three products accumulate in one fp32 TMEM
+// accumulator: y = A E_lo^T + A E_mid^T + A E_hi^T.  The result agrees with the reference's fp32
+// matmul up to fp32 accumulation-order differences, the band the SIMT kernel has as well.
 //
 // Persistent kernel, one CTA per SM, 128 token-head rows per tile, warp-specialised:
-//   warp 16       TMA: two 3-D tensor loads (d 0..63, 64..127) of 128 rows into an A stage,
-//                 128-byte swizzled, i.e. already the UMMA K-major SWIZZLE_128B layout;
-//   warps 0-7     two threads per row: norm (in the SIMT kernel's summation order), k_unit in
-//                 place (bf16), norm written out;
-//   warp 17       one thread issues 3 x 8 tcgen05.mma (M=128, N=128, K=16) per tile into one of
-//                 two TMEM accumulators and commits to mbarriers;
+//   warp 16       TMA: two 3-D tensor loads (d 0..63, 64..127) of 128 rows into a shared-memory
+//                 stage (128-byte swizzled);
+//   warps 0-7     warp w holds rows 32 (w % 4) + lane, half w / 4 of each row: norm (in the SIMT
+//                 kernel's summation order, halves exchanged through shared memory), k_unit
+//                 (bf16) written to a TMEM A buffer with tcgen05.st, norm written out;
+//   warp 17       one thread issues 3 x 8 tcgen05.mma (M=128, N=128, K=16, A from TMEM, B = E
+//                 splits from shared memory) per tile into one of two TMEM accumulators;
 //   warps 8-15    epilogue: tcgen05.ld of a 32-row x 64-column quarter-half each, searchsorted
-//                 against the boundaries, pack, 16-byte stores of the code row.
+//                 against the boundaries (table lookup), pack, 16-byte stores of the code row.
+// TMEM columns: accumulators [0,128) and [128,256), A buffers [256,320) and [320,384).
 // Every mbarrier wait is bounded; a wait that runs out sets g_tc_rotate_fault and the CTA drains.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -35,24 +37,27 @@ namespace {
 
 constexpr int TR_ROWS = 128;                  // rows per tile (= UMMA M, = TMEM lanes)
 constexpr int TR_D = 128;                     // head_dim (= UMMA N = K)
-constexpr int TR_STAGES = 3;                  // A-operand ring depth
+constexpr int TR_STAGES = 3;                  // raw key ring depth
 constexpr int TR_ATOM = TR_ROWS * 128;        // one 64-wide K atom of a 128-row operand: 16 KiB
-constexpr int TR_TILE = 2 * TR_ATOM;          // 32 KiB per 128 x 128 bf16 operand
+constexpr int TR_TILE = 2 * TR_ATOM;          // 32 KiB per 128 x 128 16-bit operand
 constexpr int TR_B_BYTES = 3 * TR_TILE;       // E_hi, E_mid, E_lo
-constexpr int TR_LUT_BYTES = 256 * 8;        // searchsorted table
-constexpr int TR_SMEM = TR_B_BYTES + TR_STAGES * TR_TILE + 256 + TR_LUT_BYTES + 1024;  // + barriers, alignment
+constexpr int TR_LUT = 256;                   // searchsorted table entries
+constexpr int TR_XCH_BYTES = 2 * TR_ROWS * 2 * 32;  // norm partial-sum exchange, double-buffered
+constexpr int TR_SMEM = TR_B_BYTES + TR_STAGES * TR_TILE + TR_XCH_BYTES + TR_LUT * 8 + 256 + 1024;
 constexpr int TR_NORM_WARPS = 8, TR_EPI_WARPS = 8;
 constexpr int TR_TMA_WARP = TR_NORM_WARPS + TR_EPI_WARPS;  // 16
 constexpr int TR_MMA_WARP = TR_TMA_WARP + 1;               // 17
 constexpr int TR_THREADS = (TR_MMA_WARP + 1) * 32;         // 576
-constexpr uint32_t TR_TMEM_COLS = 256;                     // two 128-column fp32 accumulators
+constexpr uint32_t TR_TMEM_COLS = 512;
+constexpr uint32_t TR_TMEM_A = 256;                        // first A-buffer column
 
 __device__ unsigned int g_tc_rotate_fault;
 
 struct TrBars {
   uint64_t a_full[TR_STAGES];   // TMA bytes landed
-  uint64_t a_ready[TR_STAGES];  // k_unit written (256 arrivals)
-  uint64_t a_empty[TR_STAGES];  // MMAs that read the stage finished (tcgen05.commit)
+  uint64_t a_empty[TR_STAGES];  // raw stage read (256 arrivals)
+  uint64_t at_ready[2];         // TMEM A buffer written (256 arrivals)
+  uint64_t at_free[2];          // MMAs that read the A buffer finished (tcgen05.commit)
   uint64_t acc_full[2];         // accumulator complete (tcgen05.commit)
   uint64_t acc_empty[2];        // accumulator drained (256 arrivals)
   uint32_t tmem_base;
@@ -65,6 +70,9 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void named_bar(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
   asm volatile(
@@ -84,11 +92,12 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
 constexpr uint32_t kIdescBf16 = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(TR_D >> 3) << 17) |
                                 (uint32_t(TR_ROWS >> 4) << 24);
 
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+// D (TMEM) (+)= A (TMEM) * B (shared memory)^T
+__device__ __forceinline__ void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(da), "l"(db), "r"(kIdescBf16), "r"(accumulate)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(db), "r"(kIdescBf16), "r"(accumulate)
       : "memory");
 }
 
@@ -111,6 +120,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Byte offset of the 16-byte chunk holding elements [8c, 8c+8) of row r in a 128-row
 // K-major SWIZZLE_128B operand (two 64-element atoms of 128-byte rows, chunk index XOR row%8).
@@ -140,7 +159,6 @@ __device__ __forceinline__ uint32_t gtu_mask(float x, float b) {
   asm("set.gtu.u32.f32 %0, %1, %2;" : "=r"(r) : "f"(x), "f"(b));
   return r;
 }
-
 // 0xFFFFFFFF when x > b (ordered: NaN gives 0), else 0.
 __device__ __forceinline__ uint32_t gt_mask(float x, float b) {
   uint32_t r;
@@ -160,26 +178,28 @@ __device__ __forceinline__ float fma_sat(float a, float b, float c) {
 // k = 0 and -inf for k = G).  Entry k holds base = #{b <= window start - step/4} and the single
 // boundary t in the window widened by step/4 on each side (+inf if none; the widened window is
 // 2.5 steps < gap_min long), so code(x) = #{b < x} = base + (x > t).  NaN gives k = 0, whose
-// entry is (NB, +inf): NaN sorts after every boundary, as searchsorted places it.
+// entry is (NB, +inf): NaN sorts after every boundary, as searchsorted places it.  The t values
+// and the bases sit in separate 4-byte tables, so a warp's lookups of up to 32 distinct cells
+// hit distinct banks.
 struct SearchGrid {
   float neg_inv_span, c0, g, step, hi;
   int G;
   bool ok;
 };
 template <int NB>
-__device__ __forceinline__ SearchGrid search_grid(const float* __restrict__ bnd) {
+__device__ __forceinline__ SearchGrid search_grid(const float* __restrict__ bnd, float sc) {
   SearchGrid sg;
   sg.ok = false;
   float gap = INFINITY;
 #pragma unroll
-  for (int j = 0; j + 1 < NB; ++j) gap = fminf(gap, __ldg(bnd + j + 1) - __ldg(bnd + j));
-  const float b0 = __ldg(bnd), bl = __ldg(bnd + NB - 1);
-  if (NB == 1) gap = fmaxf(fabsf(b0), 1.0f);
+  for (int j = 0; j + 1 < NB; ++j) gap = fminf(gap, __ldg(bnd + j + 1) * sc - __ldg(bnd + j) * sc);
+  const float b0 = __ldg(bnd) * sc, bl = __ldg(bnd + NB - 1) * sc;
+  if (NB == 1) gap = fmaxf(fabsf(b0), sc);
   if (!(gap > 0.f) || !(gap < INFINITY) || !(fabsf(b0) < INFINITY) || !(fabsf(bl) < INFINITY)) return sg;
   sg.step = gap / 3.0f;
   sg.hi = bl + 2.0f * sg.step;
   const float Gf = ceilf((sg.hi - (b0 - 2.0f * sg.step)) / sg.step);
-  if (!(Gf <= 254.0f)) return sg;
+  if (!(Gf <= float(TR_LUT - 2))) return sg;
   sg.G = int(Gf);
   const float span = Gf * sg.step;
   sg.neg_inv_span = -1.0f / span;
@@ -189,30 +209,32 @@ __device__ __forceinline__ SearchGrid search_grid(const float* __restrict__ bnd)
   return sg;
 }
 template <int NB>
-__device__ __forceinline__ uint2 search_entry(const float* __restrict__ bnd, const SearchGrid& sg, int k) {
+__device__ __forceinline__ void search_entry(const float* __restrict__ bnd, float sc, const SearchGrid& sg, int k,
+                                             float* lut_t, uint32_t* lut_b) {
   const float eps = 0.25f * sg.step;
   const float lo_w = sg.hi - float(k + 1) * sg.step - eps, hi_w = sg.hi - float(k - 1) * sg.step + eps;
   uint32_t base = 0;
   float t = INFINITY;
 #pragma unroll
   for (int j = 0; j < NB; ++j) {
-    const float b = __ldg(bnd + j);
+    const float b = __ldg(bnd + j) * sc;
     if (b <= lo_w) ++base;
     else if (b <= hi_w || k == 0) t = b;
   }
-  return make_uint2(base, __float_as_uint(t));
+  lut_t[k] = t;
+  lut_b[k] = base;
 }
-__device__ __forceinline__ uint32_t search_lut(float x, const SearchGrid& sg, const uint2* lut) {
+__device__ __forceinline__ uint32_t search_lut(float x, const SearchGrid& sg, const float* lut_t, const uint32_t* lut_b) {
   const float f = fmaf(fma_sat(x, sg.neg_inv_span, sg.c0), sg.g, 8388608.0f);
-  const uint2 e = lut[__float_as_uint(f) - 0x4B000000u];
-  return e.x - gt_mask(x, __uint_as_float(e.y));
+  const uint32_t k = __float_as_uint(f) - 0x4B000000u;
+  return lut_b[k] - gt_mask(x, lut_t[k]);
 }
 
 // Codes of 32 consecutive coordinates, packed LSB-first (2-bit: 4 per byte, 3/4-bit: 2 per
 // byte) into 32 * BITS' / 8 bytes, BITS' = 2 or 4.
 template <int BITS, bool LUT>
-__device__ __forceinline__ void encode32(const float (&y)[32], uint32_t* w, const SearchGrid& sg, const uint2* lut,
-                                         const float* __restrict__ bnd) {
+__device__ __forceinline__ void encode32(const float (&y)[32], uint32_t* w, const SearchGrid& sg, const float* lut_t,
+                                         const uint32_t* lut_b, const float* __restrict__ bnd, float sc) {
   constexpr int NB = (1 << BITS) - 1;
   constexpr int VPB = BITS == 2 ? 4 : 2;
 #pragma unroll
@@ -223,13 +245,13 @@ __device__ __forceinline__ void encode32(const float (&y)[32], uint32_t* w, cons
       const float x = y[4 * VPB * k + u];
       uint32_t c;
       if constexpr (LUT) {
-        c = search_lut(x, sg, lut);
+        c = search_lut(x, sg, lut_t, lut_b);
       } else {  // degenerate boundaries: count them (>u puts NaN after every boundary)
         c = 0;
 #pragma unroll
-        for (int j = 0; j < NB; ++j) c -= gtu_mask(x, __ldg(bnd + j));
+        for (int j = 0; j < NB; ++j) c -= gtu_mask(x, __ldg(bnd + j) * sc);
       }
-      v |= c << ((u / VPB) * 8 + (u % VPB) * BITS);
+      v += c << ((u / VPB) * 8 + (u % VPB) * BITS);
     }
     w[k] = v;
   }
@@ -238,23 +260,28 @@ __device__ __forceinline__ void encode32(const float (&y)[32], uint32_t* w, cons
 // ---------------------------------------------------------------- kernel
 template <int BITS>
 __global__ void __launch_bounds__(TR_THREADS, 1) tc_scalar_key_kernel(
-    const __grid_constant__ CUtensorMap kmap, int64_t n_tokens, int n_heads, const RowMap rm, const float* __restrict__ E, const float* __restrict__ bnd,
-    uint8_t* __restrict__ codes, __nv_bfloat16* __restrict__ norms) {
+    const __grid_constant__ CUtensorMap kmap, int64_t n_tokens, int n_heads, const RowMap rm,
+    const float* __restrict__ E, const float* __restrict__ bnd, uint8_t* __restrict__ codes,
+    __nv_bfloat16* __restrict__ norms) {
   constexpr int NB = (1 << BITS) - 1;
   constexpr int VPB = BITS == 2 ? 4 : 2;      // codes per byte (3-bit packs two per byte)
   constexpr int PD = TR_D / VPB;              // bytes per code row
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* Bs = smem;                         // [3][2 atoms][128 rows][128 B]
-  uint8_t* As = smem + TR_B_BYTES;            // [STAGES][2 atoms][128 rows][128 B]
-  TrBars* bars = reinterpret_cast<TrBars*>(As + TR_STAGES * TR_TILE);
-  uint2* lut = reinterpret_cast<uint2*>(As + TR_STAGES * TR_TILE + 256);
+  uint8_t* Bs = smem;                                          // [2 splits][2 atoms][128 rows][128 B]
+  uint8_t* Rs = smem + TR_B_BYTES;                             // [STAGES][2 atoms][128 rows][128 B]
+  float* xch = reinterpret_cast<float*>(Rs + TR_STAGES * TR_TILE);  // [2][128 rows][2 halves][8]
+  float* lut_t = xch + TR_XCH_BYTES / 4;                       // [TR_LUT]
+  uint32_t* lut_b = reinterpret_cast<uint32_t*>(lut_t + TR_LUT);  // [TR_LUT]
+  TrBars* bars = reinterpret_cast<TrBars*>(lut_b + TR_LUT);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n_rows = n_tokens * n_heads;
   const int tok_per_tile = TR_ROWS / n_heads;
   const int64_t n_tiles = (n_tokens + tok_per_tile - 1) / tok_per_tile;
 
-  // ---- split E into three bf16 operands, written in the swizzled B layout (row n = E[n, :])
+  // ---- E = E_hi + E_mid + E_lo in bf16 (each the bf16 rounding of what the previous ones
+  // leave), written in the swizzled B layout (row n = E[n, :])
+  const float sc = 1.0f;  // boundaries in the accumulator's units
   for (int idx = threadIdx.x; idx < TR_D * (TR_D / 8); idx += blockDim.x) {
     const int n = idx >> 4, c = idx & 15;
     const float4 e0 = __ldg(reinterpret_cast<const float4*>(E + n * TR_D + c * 8));
@@ -265,28 +292,29 @@ __global__ void __launch_bounds__(TR_THREADS, 1) tc_scalar_key_kernel(
     for (int j = 0; j < 8; j += 2) {
       float r0 = ev[j], r1 = ev[j + 1];
 #pragma unroll
-      for (int s = 0; s < 3; ++s) {
-        const __nv_bfloat16 h0 = __float2bfloat16_rn(r0), h1 = __float2bfloat16_rn(r1);
-        w[s][j / 2] = uint32_t(__bfloat16_as_ushort(h0)) | (uint32_t(__bfloat16_as_ushort(h1)) << 16);
-        r0 -= __bfloat162float(h0);
-        r1 -= __bfloat162float(h1);
+      for (int sp = 0; sp < 3; ++sp) {
+        const uint32_t h = pack_bf16x2(r0, r1);
+        w[sp][j / 2] = h;
+        r0 -= bf_lo(h);
+        r1 -= bf_hi(h);
       }
     }
 #pragma unroll
-    for (int s = 0; s < 3; ++s)
-      *reinterpret_cast<uint4*>(Bs + s * TR_TILE + sw128_chunk(n, c)) = make_uint4(w[s][0], w[s][1], w[s][2], w[s][3]);
+    for (int sp = 0; sp < 3; ++sp)
+      *reinterpret_cast<uint4*>(Bs + sp * TR_TILE + sw128_chunk(n, c)) = make_uint4(w[sp][0], w[sp][1], w[sp][2], w[sp][3]);
   }
-  const SearchGrid sgrid = search_grid<NB>(bnd);
+  const SearchGrid sgrid = search_grid<NB>(bnd, sc);
   if (sgrid.ok)
-    for (int k = threadIdx.x; k <= sgrid.G; k += blockDim.x) lut[k] = search_entry<NB>(bnd, sgrid, k);
+    for (int k = threadIdx.x; k <= sgrid.G; k += blockDim.x) search_entry<NB>(bnd, sc, sgrid, k, lut_t, lut_b);
   fence_async_smem();
   if (threadIdx.x == 0) {
     for (int s = 0; s < TR_STAGES; ++s) {
       mbar_init(&bars->a_full[s], 1);
-      mbar_init(&bars->a_ready[s], TR_NORM_WARPS * 32);
-      mbar_init(&bars->a_empty[s], 1);
+      mbar_init(&bars->a_empty[s], TR_NORM_WARPS * 32);
     }
     for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->at_ready[b], TR_NORM_WARPS * 32);
+      mbar_init(&bars->at_free[b], 1);
       mbar_init(&bars->acc_full[b], 1);
       mbar_init(&bars->acc_empty[b], TR_EPI_WARPS * 32);
     }
@@ -312,31 +340,35 @@ __global__ void __launch_bounds__(TR_THREADS, 1) tc_scalar_key_kernel(
         const int s = i % TR_STAGES;
         if (!mbar_wait(&bars->a_empty[s], ((i / TR_STAGES) & 1) ^ 1)) { failed = true; break; }
         mbar_arrive_expect_tx(&bars->a_full[s], TR_TILE);
-        uint8_t* dst = As + s * TR_TILE;
+        uint8_t* dst = Rs + s * TR_TILE;
         const int z = int(tile * tok_per_tile);
         tma_load_3d(dst, &kmap, 0, 0, z, &bars->a_full[s]);
         tma_load_3d(dst + TR_ATOM, &kmap, 64, 0, z, &bars->a_full[s]);
       }
     }
   } else if (warp < TR_NORM_WARPS) {
-    // ---- k_unit = k / (norm + 1e-10) in place.  Two threads per row (lanes 2r, 2r+1 of a warp
-    // hold row 16 * warp + r); half h owns chunks {4h..4h+3, 8+4h..8+4h+3}, i.e. the partial sums
-    // of SIMT lanes {8h..8h+7, 16+8h..16+8h+7}, so the first level of the warp_sum tree
-    // (lanes 16 apart) stays inside a thread and the second (8 apart) is one exchange.
-    const int t = 16 * warp + (lane >> 1), hf = lane & 1;
+    // ---- k_unit = k / (norm + 1e-10).  Thread (warp w, lane) holds row t = 32 (w % 4) + lane
+    // (its TMEM lane) and half hf = w / 4, which owns chunks {4hf..4hf+3, 8+4hf..8+4hf+3}, i.e.
+    // the 4-element partial sums of SIMT lanes {8hf..8hf+7, 16+8hf..16+8hf+7}: the first level of
+    // the warp_sum tree (lanes 16 apart) stays inside a thread, the second (8 apart) pairs the
+    // two halves, whose warps swap 8 sums through shared memory.
+    const int q = warp & 3, hf = warp >> 2;
+    const int t = 32 * q + lane;
     int i = 0;
     for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++i) {
-      const int s = i % TR_STAGES;
+      const int s = i % TR_STAGES, ab = i & 1;
       if (!mbar_wait(&bars->a_full[s], (i / TR_STAGES) & 1)) { failed = true; break; }
-      uint8_t* A = As + s * TR_TILE;
+      const uint8_t* R = Rs + s * TR_TILE;
+      uint4 raw[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) raw[j] = *reinterpret_cast<const uint4*>(R + sw128_chunk(t, (j < 4 ? j : j + 4) + 4 * hf));
+      mbar_arrive(&bars->a_empty[s]);  // the stage may be refilled once every row is in registers
       // sum of squares in the SIMT kernel's order: partials of 4 elements (fma chain) per SIMT
       // lane, then the xor-butterfly tree of warp_sum (lanes 16 apart, then 8, 4, 2, 1)
-      float p[16];  // p[j] = partial of SIMT lane (j < 8 ? 8h + j : 16 + 8h + j - 8)
+      float p[16];  // p[j] = partial of SIMT lane (j < 8 ? 8hf + j : 16 + 8hf + j - 8)
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int c = (j < 4 ? j : j + 4) + 4 * hf;
-        const uint4 u = *reinterpret_cast<const uint4*>(A + sw128_chunk(t, c));
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+        const uint32_t w[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           float a = 0.f;
@@ -347,39 +379,45 @@ __global__ void __launch_bounds__(TR_THREADS, 1) tc_scalar_key_kernel(
           p[2 * (j & 3) + hh + 8 * (j >> 2)] = a;
         }
       }
-      // level 16: lane l (< 16) = p_l + p_{l+16}: this thread's lanes 8h + m, m < 8
+      // level 16: SIMT lane l (< 16) = p_l + p_{l+16}; this thread holds lanes 8hf + m, m < 8
       float s1[8];
 #pragma unroll
       for (int m = 0; m < 8; ++m) s1[m] = p[m] + p[m + 8];
-      // level 8: lane m (< 8) = lane m + lane m + 8: half 0 holds lanes 0..7, half 1 lanes 8..15
+      float* mine = xch + ((ab * TR_ROWS + t) * 2 + hf) * 8;
+      float* other = xch + ((ab * TR_ROWS + t) * 2 + (hf ^ 1)) * 8;
+      reinterpret_cast<float4*>(mine)[0] = make_float4(s1[0], s1[1], s1[2], s1[3]);
+      reinterpret_cast<float4*>(mine)[1] = make_float4(s1[4], s1[5], s1[6], s1[7]);
+      named_bar(1 + q, 64);  // warps q and q + 4
+      const float4 o0 = reinterpret_cast<const float4*>(other)[0], o1 = reinterpret_cast<const float4*>(other)[1];
+      const float o[8] = {o0.x, o0.y, o0.z, o0.w, o1.x, o1.y, o1.z, o1.w};
+      // level 8: lane m (< 8) = lane m + lane m + 8 (half 0 holds lanes 0..7, half 1 lanes 8..15)
       float s2[8];
 #pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        const float o = __shfl_xor_sync(0xffffffffu, s1[m], 1);
-        s2[m] = hf ? o + s1[m] : s1[m] + o;
-      }
+      for (int m = 0; m < 8; ++m) s2[m] = hf ? o[m] + s1[m] : s1[m] + o[m];
 #pragma unroll
-      for (int o = 4; o > 0; o >>= 1)
+      for (int oo = 4; oo > 0; oo >>= 1)
 #pragma unroll
-        for (int l = 0; l < o; ++l) s2[l] = s2[l] + s2[l + o];
+        for (int l = 0; l < oo; ++l) s2[l] = s2[l] + s2[l + oo];
       const float nrm = rnd<BF16>(sqrtf(s2[0]));
       const float den = rnd<BF16>(nrm + 1e-10f);
       const float rcp = __frcp_rn(den);
+      // k_unit in bf16 (the reference's storage type); column j of the A buffer holds elements
+      // 2j, 2j+1
+      uint32_t cols[2][16];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int c = (j < 4 ? j : j + 4) + 4 * hf;
-        const uint4 u = *reinterpret_cast<const uint4*>(A + sw128_chunk(t, c));
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-        float qv[8];
+        const uint32_t w[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) qv[e] = ((e & 1) ? bf_hi(w[e >> 1]) : bf_lo(w[e >> 1])) * rcp;
-        uint32_t o[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) o[e] = pack_bf16x2(qv[2 * e], qv[2 * e + 1]);
-        *reinterpret_cast<uint4*>(A + sw128_chunk(t, c)) = make_uint4(o[0], o[1], o[2], o[3]);
+        for (int e = 0; e < 4; ++e) cols[j >> 2][(j & 3) * 4 + e] = pack_bf16x2(bf_lo(w[e]) * rcp, bf_hi(w[e]) * rcp);
       }
-      fence_async_smem();
-      mbar_arrive(&bars->a_ready[s]);
+      if (!mbar_wait(&bars->at_free[ab], ((i >> 1) & 1) ^ 1)) { failed = true; break; }
+      tc_fence_after();
+      const uint32_t ta = tmem + (uint32_t(32 * q) << 16) + TR_TMEM_A + uint32_t(ab * 64 + 16 * hf);
+      tmem_st16(ta, cols[0]);        // elements 32hf .. 32hf+31
+      tmem_st16(ta + 32, cols[1]);   // elements 64+32hf .. 64+32hf+31
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&bars->at_ready[ab]);
       const int64_t r = tile * TR_ROWS + t;
       if (hf == 0 && r < n_rows) {
         int64_t tok;
@@ -390,25 +428,26 @@ __global__ void __launch_bounds__(TR_THREADS, 1) tc_scalar_key_kernel(
     }
   } else if (warp == TR_MMA_WARP) {
     if (lane == 0) {
-      const uint32_t a0 = smem_u32(As), b0 = smem_u32(Bs);
+      const uint32_t b0 = smem_u32(Bs);
       int i = 0;
       for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++i) {
-        const int s = i % TR_STAGES, ab = i & 1;
-        if (!mbar_wait(&bars->a_ready[s], (i / TR_STAGES) & 1)) { failed = true; break; }
+        const int ab = i & 1;
+        if (!mbar_wait(&bars->at_ready[ab], (i >> 1) & 1)) { failed = true; break; }
         if (!mbar_wait(&bars->acc_empty[ab], ((i >> 1) & 1) ^ 1)) { failed = true; break; }
         tc_fence_after();
         const uint32_t d = tmem + uint32_t(ab * TR_D);
+        const uint32_t a = tmem + TR_TMEM_A + uint32_t(ab * 64);
         uint32_t acc = 0;
 #pragma unroll
-        for (int sp = 2; sp >= 0; --sp) {  // smallest terms first
+        for (int sp = 2; sp >= 0; --sp) {  // smaller terms first
 #pragma unroll
           for (int ks = 0; ks < TR_D / 16; ++ks) {
             const uint32_t off = uint32_t((ks >> 2) * TR_ATOM + (ks & 3) * 32);
-            umma_bf16(d, umma_desc_sw128(a0 + s * TR_TILE + off), umma_desc_sw128(b0 + sp * TR_TILE + off), acc);
+            umma_bf16_ts(d, a + uint32_t(ks * 8), umma_desc_sw128(b0 + sp * TR_TILE + off), acc);
             acc = 1;
           }
         }
-        umma_commit(&bars->a_empty[s]);
+        umma_commit(&bars->at_free[ab]);
         umma_commit(&bars->acc_full[ab]);
       }
     }
@@ -435,17 +474,16 @@ __global__ void __launch_bounds__(TR_THREADS, 1) tc_scalar_key_kernel(
           mbar_arrive(&bars->acc_empty[ab]);
         }
         if (sgrid.ok)
-          encode32<BITS, true>(y, w + part * (PD / 16), sgrid, lut, bnd);
+          encode32<BITS, true>(y, w + part * (PD / 16), sgrid, lut_t, lut_b, bnd, sc);
         else
-          encode32<BITS, false>(y, w + part * (PD / 16), sgrid, lut, bnd);
+          encode32<BITS, false>(y, w + part * (PD / 16), sgrid, lut_t, lut_b, bnd, sc);
       }
       const int64_t r = tile * TR_ROWS + t;
       if (r >= n_rows) continue;
       int64_t tok;
       int h;
       rm.token_head(r, tok, h);
-      uint4* dst = reinterpret_cast<uint4*>(codes + rm.row(tok, h) * PD +
-                                            half * (PD / 2));
+      uint4* dst = reinterpret_cast<uint4*>(codes + rm.row(tok, h) * PD + half * (PD / 2));
 #pragma unroll
       for (int k = 0; k < PD / 32; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
     }
