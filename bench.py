@@ -6,7 +6,11 @@ keys: 8-dim blocks, 256-entry fp16-valued codebook k-means-fit on 16K calibratio
 values in groups of 32) plus a 128-token exact bf16 window, one decode token per sequence.
 A step = the attention of all 32 layers for one decode token of every sequence.
 
-    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--workload append]
+
+``--workload append`` measures BASELINE.json configs[2] instead: a batch of 8 x 8192 new tokens x
+8 KV heads x head_dim 128 in bf16 quantized into store rows (tcgen05 rotation + 3-bit scalar key
+codes, 2-bit values in groups of 32); GB/s counts input plus output bytes.
 
 N > 1 (torchrun, one rank per GPU): every rank serves its own 16 sequences (sequences are
 independent units; no collective on the data path) -> ``scaling: weak``.
@@ -48,6 +52,7 @@ def parse():
     ap.add_argument("--hq", type=int, default=32)
     ap.add_argument("--hkv", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="decode", choices=["decode", "append"])
     return ap.parse_args()
 
 
@@ -248,12 +253,226 @@ def run_reference(a, rank: int, world: int):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- append
+APPEND_METRIC = "compressed-KV append GB/s (in+out)"
+AP_B, AP_T, AP_H, AP_D, AP_BITS = 8, 8192, 8, 128, 3
+
+
+def append_config():
+    return {"workload": "cfg2_append_bf16", "batch": AP_B, "new_tokens": AP_T, "n_kv_heads": AP_H, "head_dim": AP_D,
+            "keys": "scalar 3-bit (metric rotation on tcgen05, 3-split bf16)", "values": "2-bit g32",
+            "l2": "inputs larger than L2 (no flush)"}
+
+
+def append_bytes():
+    rows = AP_B * AP_T * AP_H
+    k_in = v_in = rows * AP_D * 2
+    k_out = rows * (AP_D // 2 + 2)            # 3-bit codes two per byte + bf16 norm
+    v_out = rows * (AP_D // 4 + 2 * 2 * (AP_D // 32))
+    return k_in, v_in, k_out, v_out
+
+
+def append_cpu_sample(seconds_cap: float = 20.0):
+    """The reference's append path restated in torch CPU ops (oracle.torch_append: norm, divide,
+    fp32 matmul, searchsorted, pack; value codec) on all host threads, on a bounded sample of
+    token-heads, scaled to the full batch."""
+    import torch
+    from oracle import smaq_oracle as O
+    from smaq_b200 import synthetic as syn
+    from smaq_b200.quantizer import SMAQQuantizer
+    torch.set_num_threads(os.cpu_count() or 1)
+    rows = 65536
+    k = torch.from_numpy(syn.keys((rows,), AP_D, seed=31)).to(torch.bfloat16)
+    v = torch.from_numpy(syn.values((rows,), AP_D, seed=32)).to(torch.bfloat16)
+    quant = SMAQQuantizer(AP_D, bits=AP_BITS, device=torch.device("cpu"))
+    quant.fit(torch.from_numpy(syn.calibration_queries(512, AP_D)))
+    E, bnd = quant.E.float(), quant.decision_boundaries.float().contiguous()
+    runs = []
+    t_end = time.perf_counter() + seconds_cap
+    while True:
+        t0 = time.perf_counter()
+        O.torch_append(k, v, E, bnd, AP_BITS)
+        runs.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end or len(runs) >= 5:
+            break
+    t = statistics.median(runs)
+    total = sum(append_bytes())
+    scale = AP_B * AP_T * AP_H / rows
+    return {"value": total / (t * scale) / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{rows} token-heads, median of {len(runs)} runs = {t*1e3:.1f} ms, scaled x{scale:.0f}"}
+
+
+def run_append(a, rank: int, world: int):
+    import torch
+    import torch.distributed as dist
+    from smaq_b200 import build, ops, synthetic as syn
+    from smaq_b200._lib import SMAQ_KEYS_SCALAR, SMAQ_LAYOUT_DECODE
+    from smaq_b200.quantizer import SMAQQuantizer
+    build.build()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    quant = SMAQQuantizer(AP_D, bits=AP_BITS, device=dev)
+    quant.fit(torch.from_numpy(syn.calibration_queries(512, AP_D)).to(dev))
+    U_np, outl = syn.basis(AP_D)
+    U = torch.from_numpy(U_np.astype(np.float32)).to(dev)
+    lam = torch.from_numpy(np.sqrt(syn.spectrum(AP_D)).astype(np.float32)).to(dev)
+    outl = torch.from_numpy(outl).to(dev)
+    gen = torch.Generator(device=dev).manual_seed(100 + rank)
+    N = AP_B * AP_T
+    k = spectral_keys_gpu(N * AP_H, gen, U, lam, outl, torch.bfloat16).reshape(N, AP_H, AP_D)
+    v = torch.randn((N, AP_H, AP_D), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    rows = N * AP_H
+    codes = torch.empty((rows, AP_D // 2), dtype=torch.uint8, device=dev)
+    norms = torch.empty((rows,), dtype=torch.bfloat16, device=dev)
+    vd = torch.empty((rows, AP_D // 4), dtype=torch.uint8, device=dev)
+    vs = torch.empty((rows, AP_D // 32), dtype=torch.bfloat16, device=dev)
+    vz = torch.empty_like(vs)
+    E, bnd = quant.E.contiguous(), quant.decision_boundaries.contiguous()
+
+    def step(kk=k, vv=v, keys=True, values=True):
+        # every sequence's 8192 new tokens land in its own store page (page_size 8192)
+        ops.append(kk if keys else None, vv if values else None, n_heads=AP_H, page_size=AP_T,
+                   key_format=SMAQ_KEYS_SCALAR, key_bits=AP_BITS, E=E, boundaries=bnd, key_codes=codes,
+                   key_norms=norms, v_data=vd, v_scales=vs, v_zeros=vz, layout=SMAQ_LAYOUT_DECODE)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(max(3, a.warmup)):
+        step()
+    torch.cuda.synchronize()
+    # one step captured as a CUDA graph (two kernel launches), replayed K times
+    g = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream()
+    with torch.cuda.stream(cs):
+        with torch.cuda.graph(g, stream=cs):
+            step()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1) / a.steps
+    ck = clocks.stop()
+    # the keys kernel alone (dominant launch) for the roofline
+    for _ in range(2):
+        step(values=False)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(a.steps):
+        step(values=False)
+    e1.record()
+    torch.cuda.synchronize()
+    key_ms = e0.elapsed_time(e1) / a.steps
+    # end to end: pinned host K/V -> device, append, compressed rows back to the host
+    hk = torch.empty(k.shape, dtype=k.dtype).pin_memory()
+    hv = torch.empty(v.shape, dtype=v.dtype).pin_memory()
+    hk.copy_(k.cpu())
+    hv.copy_(v.cpu())
+    outs = [codes, norms, vd, vs, vz]
+    houts = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in outs]
+    dk, dv = torch.empty_like(k), torch.empty_like(v)
+
+    def e2e_step():
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        step(dk, dv)
+        for h, t in zip(houts, outs):
+            h.copy_(t, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0.record()
+    for _ in range(a.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / a.steps
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms, key_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms, key_ms = t.tolist()
+    k_in, v_in, k_out, v_out = append_bytes()
+    total = k_in + v_in + k_out + v_out
+    try:
+        peaks = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))
+        peak_gbs, peak_tf, src = float(peaks["hbm_gbs"]), float(peaks["bf16_tflops"]), "measured"
+    except Exception:
+        peak_gbs, peak_tf, src = 6650.0, 1590.0, "fallback"
+    key_bytes = k_in + k_out
+    achieved = key_bytes / (key_ms * 1e-3) / 1e9
+    flops = 3 * 2 * (AP_B * AP_T * AP_H) * AP_D * AP_D    # three bf16 splits of the d x d rotation
+    if rank == 0:
+        line = {
+            "metric": APPEND_METRIC, "value": world * total / (ms * 1e-3) / 1e9, "unit": "GB/s", "n_gpus": world,
+            "steps": a.steps, "warmup": max(3, a.warmup), "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16-io/f32-accum", "data": "synthetic",
+            "config": append_config(),
+            "tokens_per_s": world * AP_B * AP_T / (ms * 1e-3),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s",
+                         "frac": achieved / peak_gbs, "traffic": None, "peak_source": src,
+                         "kernel": "tc_scalar_key_kernel (keys: bf16 in, codes + norms out)",
+                         "algorithmic_bytes_per_launch": key_bytes,
+                         "tensor_tflops": flops / (key_ms * 1e-3) / 1e12,
+                         "tensor_frac": flops / (key_ms * 1e-3) / 1e12 / peak_tf},
+            "e2e": {"value": world * total / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": k_in + v_in,
+                    "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in outs)},
+            "gpu_launches": 2 * a.steps,
+            "clocks": ck,
+        }
+        if world == 1 and not a.no_cpu_baseline:
+            line["cpu_baseline"] = append_cpu_sample()
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_append_reference(a, rank: int):
+    if rank != 0:
+        return
+    vals, info = [], None
+    for _ in range(max(1, a.steps)):
+        info = append_cpu_sample(seconds_cap=max(2.0, 60.0 / max(1, a.steps)))
+        vals.append(info["value"])
+    v = statistics.median(vals)
+    total = sum(append_bytes())
+    line = {"impl": "reference", "metric": APPEND_METRIC, "value": v, "unit": "GB/s",
+            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": 1e3 * total / (v * 1e9), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16-io/f32-matmul", "data": "synthetic", "config": append_config(),
+            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": info["cores"], "kind": "port",
+                             "sample": info["sample"]},
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 # ----------------------------------------------------------------------------- main
 def main():
     a = parse()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.workload == "append":
+        if a.impl == "reference":
+            run_append_reference(a, rank)
+        else:
+            run_append(a, rank, world)
+        return
     if a.impl == "reference":
         run_reference(a, rank, world)
         return
