@@ -52,11 +52,17 @@ def parse():
     ap.add_argument("--hq", type=int, default=32)
     ap.add_argument("--hkv", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "append"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "append", "longctx"])
     return ap.parse_args()
 
 
 def config_of(a):
+    if a.workload == "longctx":
+        return {"workload": "cfg4_llama3_70b_bvq_longctx", "layers": a.layers, "batch": a.batch,
+                "n_q_heads": a.hq_total, "n_kv_heads": a.hkv_total, "head_dim": 128, "history_tokens": a.ctx,
+                "window_tokens": a.window, "keys": "block-VQ 8x256 (fp16 codebook)", "values": "2-bit g32",
+                "parallelism": f"kv-head x{a.head_groups}" + (f", sequence x{a.seq_splits}" if a.seq_splits > 1 else ""),
+                "per_gpu": {"n_q_heads": a.hq, "n_kv_heads": a.hkv}, "l2": "inputs larger than L2 (no flush)"}
     return {"workload": "cfg1_llama3_8b_bvq_decode", "layers": a.layers, "batch_per_gpu": a.batch,
             "n_q_heads": a.hq, "n_kv_heads": a.hkv, "head_dim": 128, "history_tokens": a.ctx,
             "window_tokens": a.window, "keys": "block-VQ 8x256 (fp16 codebook)", "values": "2-bit g32",
@@ -245,7 +251,7 @@ def run_reference(a, rank: int, world: int):
     v = statistics.median(vals)
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * a.batch / v, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "strong" if a.workload == "longctx" else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": config_of(a),
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": info["cores"], "kind": "port",
                              "sample": info["sample"]},
@@ -473,6 +479,20 @@ def main():
         else:
             run_append(a, rank, world)
         return
+    if a.workload == "longctx":
+        # Llama-3-70B KV shape, 4 x 128K, 80 layers; strong scaling,
+        # KV heads sharded over the ranks (smaq_b200.distributed.make_plan)
+        from smaq_b200.distributed import make_plan
+        plan = make_plan(world, 8)
+        if plan.seq_splits > 1:
+            raise SystemExit("longctx: more ranks than KV heads is not benchmarked")
+        a.batch, a.ctx, a.layers, a.window = 4, 131072, 80, 128
+        a.hq_total, a.hkv_total = 64, 8
+        a.head_groups, a.seq_splits = plan.head_groups, plan.seq_splits
+        if a.impl != "reference":  # the CPU reference arm times the whole (unsharded) layer
+            a.hq, a.hkv = 64 // plan.head_groups, 8 // plan.head_groups
+        else:
+            a.hq, a.hkv = 64, 8
     if a.impl == "reference":
         run_reference(a, rank, world)
         return
@@ -568,13 +588,14 @@ def main():
     h2d = sum(t.numel() * t.element_size() for t in hq)
     d2h = sum(t.numel() * t.element_size() for t in ho)
     if rank == 0:
-        tokens = a.batch * world
+        strong = a.workload == "longctx"
+        tokens = a.batch if strong else a.batch * world
         line = {
             "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
             "steps": a.steps, "warmup": max(3, a.warmup), "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32-accum/bf16-io", "data": "synthetic",
-            "config": config_of(a),
-            "hbm_gbs": bpl * a.layers / (ms * 1e-3) / 1e9,
+            "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "f32-accum/bf16-io",
+            "data": "synthetic", "config": config_of(a),
+            "hbm_gbs": world * bpl * a.layers / (ms * 1e-3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s",
                          "frac": achieved / peak_gbs, "traffic": traffic, "peak_source": peak_src,
                          "kernel": "smaq_decode (plan+decode+merge) per layer",
