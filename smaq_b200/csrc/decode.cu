@@ -17,6 +17,8 @@
 // then combines the partials of each (batch, kv-head) with a log-sum-exp rescale.
 #include <math.h>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "decode_common.cuh"
 
@@ -528,8 +530,9 @@ __global__ void merge_partials_kernel(const float* __restrict__ parts, int R, in
 // ---------------------------------------------------------------- host
 static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-// [n_seg] prefix costs, total, per-CTA slice, device error word
-static size_t plan_bytes(int n_seg) { return align_up(sizeof(int64_t) * (n_seg + 4), 256); }
+// [n_seg] prefix costs, total, per-CTA slice, device error word | per-pair arrival counters
+static size_t plan_table_bytes(int n_seg) { return align_up(sizeof(int64_t) * (n_seg + 4), 256); }
+static size_t plan_bytes(int n_seg) { return plan_table_bytes(n_seg) + align_up(sizeof(uint64_t) * (n_seg / 2), 256); }
 
 static size_t dec_smem(int GM, int KB, int nc) {
   const int D = 128;
@@ -671,7 +674,7 @@ extern "C" int smaq_decode(const smaq_decode_args* args, void* stream) {
   p.n_seg = 2 * a.batch * a.n_kv_heads;
   p.layout = a.layout;
   p.cent16 = a.key_format == SMAQ_KEYS_BVQ ? static_cast<const uint16_t*>(a.centroids_f16) : nullptr;
-  p.recent_in_merge = (kb == 0 && decode_v2_eligible(p, SMAQ_KEYS_BVQ, a.value_bits, p.q_dtype)) ? 1 : 0;
+  p.recent_in_merge = 0;  // every kernel attends the exact window itself
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int grid = 0;
   int st = dispatch_decode(p, kb, a.value_bits, a.num_ctas, s, &grid, true);
@@ -680,8 +683,23 @@ extern "C" int smaq_decode(const smaq_decode_args* args, void* stream) {
   if (!a.workspace || a.workspace_bytes < need)
     return fail(SMAQ_ERR_WORKSPACE, "decode: workspace %zu bytes < %zu needed", a.workspace_bytes, need);
   p.plan = static_cast<int64_t*>(a.workspace);
+  p.pair_cnt = reinterpret_cast<uint64_t*>(static_cast<char*>(a.workspace) + plan_table_bytes(p.n_seg));
   p.slots = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + plan_bytes(p.n_seg));
   p.grid = grid;
+  if (kb == 0 && decode_v2_eligible(p, SMAQ_KEYS_BVQ, a.value_bits, p.q_dtype) &&
+      p.n_seg <= decode_v2_max_fused_segments()) {
+    // one launch: partition, history, window and the per-pair merge in the tensor-core kernel
+    static std::atomic<uint32_t> epochs{0};
+    uint32_t e = ++epochs;
+    if (e == 0) e = ++epochs;
+    p.fused = 1;
+    p.epoch = e;
+    p.out = a.out;
+    p.o_sb = a.o_stride_b;
+    p.o_sh = a.o_stride_h;
+    p.partial_out = a.partial_out;
+    return dispatch_decode(p, kb, a.value_bits, grid, s, &grid, false);
+  }
   decode_plan_kernel<<<1, 1024, 0, s>>>(p);
   st = cuda_status(cudaGetLastError(), "decode_plan_kernel");
   if (st) return st;

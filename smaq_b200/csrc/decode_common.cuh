@@ -43,6 +43,14 @@ struct DecodeParams {
   int layout;
   const uint16_t* cent16;  // bvq: fp16 copy of the decoded centroids (exact), or null
   int recent_in_merge;     // 1: the exact window is attended by the merge kernel, not the main one
+  // single-launch mode of the tensor-core kernel: the partition is computed in every CTA and
+  // the last CTA to finish a (sequence, kv head) pair merges its slots into the outputs
+  int fused;
+  uint32_t epoch;          // nonzero, different for consecutive calls (tags pair_cnt values)
+  uint64_t* pair_cnt;      // [B * Hkv] (epoch << 32 | slots written), reset by the merging CTA
+  void* out;
+  int64_t o_sb, o_sh;
+  float* partial_out;
 };
 
 __device__ __forceinline__ int seg_tokens(const DecodeParams& p, int s) {
@@ -149,5 +157,6 @@ __device__ void cta_flush(const DecodeParams& p, WarpState<GM>& st, float* red, 
 // Fast path (block-VQ keys, decode layout, 2-bit values, head_dim 128): see decode_v2.cu.
 bool decode_v2_eligible(const DecodeParams& p, int key_format, int value_bits, int q_dtype);
 int launch_decode_v2(DecodeParams& p, int grid_req, cudaStream_t s, int* grid_out, bool query_only);
+int decode_v2_max_fused_segments();
 
 }  // namespace smaq

@@ -1,5 +1,5 @@
 // Fast hybrid decode for block-VQ keys with an fp16 codebook (sm_100a): TMA-staged streams,
-// tensor-core scores and tensor-core P.V.
+// tensor-core scores and tensor-core P.V; the exact recent window in the same launch.
 //
 // Reference semantics: compute_hybrid_attention (smaq/score.py:23-72) with SMAQBlockVQ scores
 // q . decoded_centroid[idx] * scale (smaq/block_vq.py:246-297) and 2-bit group-32 values
@@ -54,7 +54,9 @@ struct V3Cfg {
   static constexpr int SZ_BYTES = 2 * 4 * CH * 2;                // fp16 scales | zeros [j][ks][slot]
   static constexpr int WARP_BYTES = STAGES * STAGE_BYTES + SZ_BYTES + 256;  // ring | s,z | misc
   static constexpr int BAR_BYTES = WARPS * STAGES * 8;
-  static constexpr int SMEM = CB_BYTES + Q_BYTES + WARPS * WARP_BYTES + BAR_BYTES;
+  static constexpr int MAX_FUSED_SEG = 2048;                     // in-kernel partition table
+  static constexpr int PLAN_BYTES = (MAX_FUSED_SEG + 4) * 8 + 33 * 8 + 16;  // table | scan scratch | flag
+  static constexpr int SMEM = CB_BYTES + Q_BYTES + WARPS * WARP_BYTES + BAR_BYTES + PLAN_BYTES;
   static_assert(GM * (128 + 2) * 4 <= STAGES * STAGE_BYTES, "merge record must fit in a ring");
   static_assert(SMEM <= 232448, "shared memory budget");
 };
@@ -262,6 +264,226 @@ __device__ __forceinline__ void v3_chunk(uint32_t st, uint32_t cb_s, uint32_t sz
   __syncwarp();
 }
 
+// One chunk of up to 32 exact recent-window tokens for one warp (lane = token): fp32 scores
+// against the bf16/fp16 keys, online softmax, then P.V with lane owning dims [4 lane, 4 lane + 4).
+// This is _exact_scores / _apply_weights of smaq/score.py:99-124 in the kernel's softmax units.
+template <int GM>
+__device__ __forceinline__ void v3_window_chunk(const DecodeParams& p, const float* qs, int b, int h, int64_t tb,
+                                                int nvalid, WarpState<GM>& st) {
+  constexpr int D = 128;
+  const int lane = threadIdx.x & 31;
+  const int G = p.G;
+  const bool valid = lane < nvalid;
+  float a[GM];
+#pragma unroll
+  for (int g = 0; g < GM; ++g) a[g] = 0.f;
+  if (valid) {
+    const int64_t rb = b * p.r_sb + (tb + lane) * p.r_st + h * p.r_sh;
+    if (p.r_dtype == SMAQ_BF16 || p.r_dtype == SMAQ_F16) {
+      const bool bf = p.r_dtype == SMAQ_BF16;
+      const uint4* kr = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.rk) + rb);
+#pragma unroll 8
+      for (int c8 = 0; c8 < D / 8; ++c8) {
+        const uint4 w = __ldg(kr + c8);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        float k[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (bf) {
+            k[2 * e] = bf16lo(ws[e]);
+            k[2 * e + 1] = bf16hi(ws[e]);
+          } else {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ws[e]));
+            k[2 * e] = f.x;
+            k[2 * e + 1] = f.y;
+          }
+        }
+#pragma unroll
+        for (int g = 0; g < GM; ++g) {
+          if (g >= G) break;
+          const float* qg = qs + g * D + c8 * 8;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) a[g] = fmaf(qg[e], k[e], a[g]);
+        }
+      }
+    } else {
+      for (int d = 0; d < D; ++d) {
+        const float kv = load_elem(p.rk, p.r_dtype, rb + d);
+#pragma unroll
+        for (int g = 0; g < GM; ++g) {
+          if (g >= G) break;
+          a[g] = fmaf(qs[g * D + d], kv, a[g]);
+        }
+      }
+    }
+  }
+  float sc[GM];
+#pragma unroll
+  for (int g = 0; g < GM; ++g) sc[g] = valid ? a[g] * p.scale : -INFINITY;
+  st.softmax_chunk(sc, G);
+  // value rows in batches of 8, all loads of a batch in flight together
+  const int64_t vb = b * p.r_sb + tb * p.r_st + h * p.r_sh + lane * 4;
+  for (int j0 = 0; j0 < nvalid; j0 += 8) {
+    float v[8][4];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = j0 + u < nvalid ? j0 + u : j0;
+      const int64_t rb = vb + int64_t(j) * p.r_st;
+      if (p.r_dtype == SMAQ_BF16) {
+        const uint2 w = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.rv) + rb));
+        v[u][0] = bf16lo(w.x); v[u][1] = bf16hi(w.x); v[u][2] = bf16lo(w.y); v[u][3] = bf16hi(w.y);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[u][e] = load_elem(p.rv, p.r_dtype, rb + e);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+#pragma unroll
+      for (int g = 0; g < GM; ++g) {
+        if (g >= G) break;
+        float pj = __shfl_sync(0xffffffffu, sc[g], (j0 + u) & 31);
+        if (j0 + u >= nvalid) pj = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) st.acc[g][e] = fmaf(pj, v[u][e], st.acc[g][e]);
+      }
+    }
+  }
+}
+
+// The stream-K partition (what decode_plan_kernel writes) computed by one CTA into shared
+// memory: prefix cost of every segment, then total and per-CTA slice.  Block-wide scan.
+__device__ void v3_plan(const DecodeParams& p, int64_t* plan, int64_t* scratch /* [33] */) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (threadIdx.x == 0) scratch[32] = 0;
+  __syncthreads();
+  for (int base = 0; base < p.n_seg; base += blockDim.x) {
+    const int s = base + threadIdx.x;
+    const int64_t c = (s < p.n_seg) ? seg_span(p, s) : 0;
+    int64_t x = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int64_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) scratch[wid] = x;
+    __syncthreads();
+    if (wid == 0) {
+      int64_t w = lane < nw ? scratch[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int64_t y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      if (lane < nw) scratch[lane] = w;
+    }
+    __syncthreads();
+    const int64_t excl = scratch[32] + x - c + (wid ? scratch[wid - 1] : 0);
+    if (s < p.n_seg) plan[s] = excl;
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) scratch[32] = excl + c;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const int64_t total = scratch[32];
+    plan[p.n_seg] = total;
+    int64_t per = (total + gridDim.x - 1) / gridDim.x;
+    per = (per + 15) & ~int64_t(15);
+    if (per < 16) per = 16;
+    plan[p.n_seg + 1] = per;
+  }
+  __syncthreads();
+}
+
+// CTAs c0..c1 wrote a partial slot for segment s (none if c1 < c0).
+__device__ __forceinline__ void v3_seg_ctas(const DecodeParams& p, const int64_t* plan, int s, int& c0, int& c1) {
+  const int64_t per = plan[p.n_seg + 1];
+  const int n = seg_tokens(p, s);
+  const int64_t S = plan[s];
+  c0 = int(S / per);
+  c1 = n ? int((S + int64_t(n - 1) * seg_cost(s)) / per) : c0 - 1;
+}
+
+// Merge every partial slot of pair (b, h) into the outputs (what decode_merge_kernel does for
+// one pair), reading other CTAs' slots through L2.
+__device__ void v3_final_merge(const DecodeParams& p, const int64_t* plan, int pair) {
+  constexpr int D = 128;
+  const int b = pair / p.Hkv, h = pair - b * p.Hkv;
+  const int G = p.G;
+  const int slot_f = G * (D + 2);
+  int c0[2], c1[2];
+  for (int k = 0; k < 2; ++k) v3_seg_ctas(p, plan, pair * 2 + k, c0[k], c1[k]);
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    const int g = i / D, d = i - g * D;
+    float M = -INFINITY;
+    for (int k = 0; k < 2; ++k)
+      for (int c = c0[k]; c <= c1[k]; ++c) M = fmaxf(M, __ldcg(p.slots + int64_t(c + pair * 2 + k) * slot_f + G * D + g * 2));
+    float L = 0.f, acc[2] = {0.f, 0.f};
+    for (int k = 0; k < 2; ++k) {
+      for (int c = c0[k]; c <= c1[k]; ++c) {
+        const float* sl = p.slots + int64_t(c + pair * 2 + k) * slot_f;
+        const float mr = __ldcg(sl + G * D + g * 2);
+        const float f = (mr == -INFINITY) ? 0.f : expf(mr - M);
+        acc[k] += __ldcg(sl + g * D + d) * f;
+        L += __ldcg(sl + G * D + g * 2 + 1) * f;
+      }
+    }
+    const int hq = h * G + g;
+    if (p.partial_out) {
+      float* po = p.partial_out + (int64_t(b) * p.Hq + hq) * (2 * D + 2);
+      po[d] = acc[0];
+      po[D + d] = acc[1];
+      if (d == 0) {
+        po[2 * D] = M;
+        po[2 * D + 1] = L;
+      }
+    }
+    if (p.out) {
+      float oh = 0.f, orr = 0.f;
+      if (L > 0.f) {
+        oh = acc[0] / L;
+        orr = acc[1] / L;
+      }
+      // each part is cast to the query dtype, then the parts are summed in it (score.py:70-72)
+      const float o = round_dtype(round_dtype(oh, p.q_dtype) + round_dtype(orr, p.q_dtype), p.q_dtype);
+      store_elem(p.out, p.q_dtype, b * p.o_sb + hq * p.o_sh + d, o);
+    }
+  }
+}
+
+// After this CTA wrote its slot for segment s: count it for the pair; the CTA whose slot
+// completes the pair merges it.  Counter values carry the call's epoch so that a workspace
+// never zeroed reads as "no slots yet"; the merging CTA resets the counter to 0.
+__device__ void v3_arrive(const DecodeParams& p, const int64_t* plan, int s, int* flag) {
+  const int pair = s >> 1;
+  if (threadIdx.x == 0) {
+    int expected = 0;
+    for (int k = 0; k < 2; ++k) {
+      int c0, c1;
+      v3_seg_ctas(p, plan, pair * 2 + k, c0, c1);
+      expected += c1 - c0 + 1;
+    }
+    __threadfence();  // this CTA's slot stores before the count
+    unsigned long long* cnt = reinterpret_cast<unsigned long long*>(p.pair_cnt + pair);
+    unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(cnt), next;
+    for (;;) {
+      const uint32_t n = (uint32_t(old >> 32) == p.epoch) ? uint32_t(old) + 1u : 1u;
+      next = (uint64_t(p.epoch) << 32) | n;
+      const unsigned long long seen = atomicCAS(cnt, old, next);
+      if (seen == old) break;
+      old = seen;
+    }
+    const bool last = int(uint32_t(next)) == expected;
+    if (last) {
+      *reinterpret_cast<volatile unsigned long long*>(cnt) = 0ull;
+      __threadfence();  // every other slot store is visible before the merge reads them
+    }
+    *flag = last;
+  }
+  __syncthreads();
+  if (*flag) v3_final_merge(p, plan, pair);
+}
+
 template <int GM>
 __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(DecodeParams p,
                                                                           const uint16_t* __restrict__ cb16) {
@@ -289,8 +511,26 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
   uint32_t phase = 0;
   bool failed = false;
 
-  const int64_t total = p.plan[p.n_seg];
-  const int64_t per = p.plan[p.n_seg + 1];
+  // partition: computed here in single-launch mode, else read from decode_plan_kernel's output
+  int64_t* splan = reinterpret_cast<int64_t*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);
+  int* arrive_flag = reinterpret_cast<int*>(splan + C::MAX_FUSED_SEG + 4 + 33);
+  const int64_t* plan = p.plan;
+  if (p.fused) {
+    v3_plan(p, splan, splan + C::MAX_FUSED_SEG + 4);
+    plan = splan;
+    // pairs nobody attends (no usable history, no window): zero output, empty partials
+    for (int pair = blockIdx.x; pair < p.B * p.Hkv; pair += gridDim.x) {
+      int e = 0;
+      for (int k = 0; k < 2; ++k) {
+        int c0, c1;
+        v3_seg_ctas(p, plan, pair * 2 + k, c0, c1);
+        e += c1 - c0 + 1;
+      }
+      if (e == 0) v3_final_merge(p, plan, pair);
+    }
+  }
+  const int64_t total = plan[p.n_seg];
+  const int64_t per = plan[p.n_seg + 1];
   const int c = blockIdx.x;
   const int64_t lo = int64_t(c) * per, hi = min(lo + per, total);
   if (lo >= hi) return;
@@ -318,11 +558,11 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
   int sa = 0, sb_ = p.n_seg - 1;
   while (sa < sb_) {
     const int mid = (sa + sb_) >> 1;
-    if (p.plan[mid + 1] > lo) sb_ = mid; else sa = mid + 1;
+    if (plan[mid + 1] > lo) sb_ = mid; else sa = mid + 1;
   }
   const float lscale = p.scale * kLog2e;
   for (int s = sa; s < p.n_seg; ++s) {
-    const int64_t S = p.plan[s];
+    const int64_t S = plan[s];
     if (S >= hi) break;
     const int n = seg_tokens(p, s);
     if (n == 0) continue;
@@ -336,7 +576,30 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
       const int g = i / D, d = i - g * D;
       qs[i] = g < G ? load_elem(p.q, p.q_dtype, b * p.q_sb + int64_t(h * G + g) * p.q_sh + d) : 0.f;
     }
-    if (s & 1) continue;  // the exact window is attended by decode_finish_kernel
+    if (s & 1) {
+      // ---------------- exact recent window: warp w takes 8-token chunks w, w + WARPS, ...
+      __syncthreads();  // qs complete
+      const int ntok = int(t1 - t0);
+      WarpState<GM> ws;
+      ws.init();
+      // 8 tokens per warp and round: the window is short, so spreading it over every warp
+      // keeps its latency (key row loads, then value row loads) to about one round
+      for (int ch = wid; ch * 8 < ntok; ch += WARPS)
+        v3_window_chunk<GM>(p, qs, b, h, t0 + int64_t(ch) * 8, min(8, ntok - ch * 8), ws);
+#pragma unroll
+      for (int g = 0; g < GM; ++g) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) rec[g * D + lane * 4 + e] = g < G ? ws.acc[g][e] : 0.f;
+        if (lane == 0) {
+          rec[GM * D + g * 2] = g < G ? ws.m[g] : -INFINITY;
+          rec[GM * D + g * 2 + 1] = g < G ? ws.l[g] : 0.f;
+        }
+      }
+      __syncthreads();
+      v3_merge<GM, WARPS>(p, reinterpret_cast<const float*>(wreg0), C::WARP_BYTES / 4, c + s);
+      if (p.fused) v3_arrive(p, plan, s, arrive_flag);
+      continue;
+    }
 
     // ---------------- compressed history
     const int ntok = int(t1 - t0);
@@ -445,6 +708,7 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
     }
     __syncthreads();
     v3_merge<GM, WARPS>(p, reinterpret_cast<const float*>(wreg0), C::WARP_BYTES / 4, c + s);
+    if (p.fused) v3_arrive(p, plan, s, arrive_flag);
   }
   if (failed && lane == 0) atomicExch(reinterpret_cast<int*>(p.plan + p.n_seg + 2), 1);
 }
@@ -468,6 +732,8 @@ static int launch_v3_t(DecodeParams& p, int grid_req, cudaStream_t s, int* grid_
   kern<<<grid, V3Cfg<GM>::THREADS, sm, s>>>(p, p.cent16);
   return cuda_status(cudaGetLastError(), "decode_v3_kernel");
 }
+
+int decode_v2_max_fused_segments() { return V3Cfg<4>::MAX_FUSED_SEG; }
 
 int launch_decode_v2(DecodeParams& p, int grid_req, cudaStream_t s, int* grid_out, bool query_only) {
   if (p.G <= 4) return launch_v3_t<4>(p, grid_req, s, grid_out, query_only);
