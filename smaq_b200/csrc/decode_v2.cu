@@ -267,6 +267,121 @@ __device__ __forceinline__ void v3_chunk(uint32_t st, uint32_t cb_s, uint32_t sz
 // One chunk of up to 32 exact recent-window tokens for one warp (lane = token): fp32 scores
 // against the bf16/fp16 keys, online softmax, then P.V with lane owning dims [4 lane, 4 lane + 4).
 // This is _exact_scores / _apply_weights of smaq/score.py:99-124 in the kernel's softmax units.
+// G <= 4: scores from a per-pair lookup table instead of the tensor cores.  Entry (code c,
+// block b) at shared offset c * 256 + b * 16 holds, for the four query heads,
+// scale * log2(e) * q_g[8b .. 8b+8) . decoded_centroid[b][c] in fp32, so a token's score is the
+// sum of its 16 entries.  Lane = token.  Lane L visits block j ^ (L & 15) at step j, so the
+// eight lanes of every load phase hit eight distinct 16-byte bank groups.  The softmax keeps
+// one reference maximum per head for the warp and rescales only when a score exceeds it.
+struct LutLane {
+  uint32_t xl;     // (L & 15) << 4
+  uint32_t sel;    // byte_perm selector: byte i <- byte i ^ (L & 3)
+  bool swp8, swp4; // word-pair / word swaps of the XOR permutation
+};
+
+template <bool FULL>
+__device__ __forceinline__ void v3_chunk_lut(uint32_t st, uint32_t szs, uint32_t pb, const V3Lane& L,
+                                             const LutLane& X, int nv, float (&acc)[8][4], float (&zacc)[4],
+                                             float (&mref)[4], float (&lsum)[4]) {
+  const int lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  // ---- the chunk's value scales and zeros as fp16, in MMA k-slot order (one token per lane)
+  {
+    uint2 s2 = lds64(st + ST_S + lane * 8);
+    uint2 z2 = lds64(st + ST_Z + lane * 8);
+    if (!FULL && lane >= nv) s2 = z2 = make_uint2(0u, 0u);  // rows past the end may hold anything
+    const uint32_t sp0 = pack_f16x2(bf16lo(s2.x), bf16hi(s2.x)), sp1 = pack_f16x2(bf16lo(s2.y), bf16hi(s2.y));
+    const uint32_t zp0 = pack_f16x2(bf16lo(z2.x), bf16hi(z2.x)), zp1 = pack_f16x2(bf16lo(z2.y), bf16hi(z2.y));
+    const uint32_t o = szs + L.sz_off;
+    sts16(o + 0, uint16_t(sp0)); sts16(o + 64, uint16_t(sp0 >> 16));
+    sts16(o + 128, uint16_t(sp1)); sts16(o + 192, uint16_t(sp1 >> 16));
+    sts16(o + 256, uint16_t(zp0)); sts16(o + 320, uint16_t(zp0 >> 16));
+    sts16(o + 384, uint16_t(zp1)); sts16(o + 448, uint16_t(zp1 >> 16));
+  }
+  // ---- scores of token `lane`
+  const uint4 w = *reinterpret_cast<const uint4*>(sm + st + ST_IDX + lane * 16);
+  // decode-layout byte order -> natural block order, then XOR-permute the bytes by (L & 15)
+  uint32_t n0 = __byte_perm(w.x, w.y, 0x6420), n1 = __byte_perm(w.x, w.y, 0x7531);
+  uint32_t n2 = __byte_perm(w.z, w.w, 0x6420), n3 = __byte_perm(w.z, w.w, 0x7531);
+  if (X.swp8) { const uint32_t a = n0, b = n1; n0 = n2; n1 = n3; n2 = a; n3 = b; }
+  if (X.swp4) { const uint32_t a = n0, b = n2; n0 = n1; n1 = a; n2 = n3; n3 = b; }
+  const uint32_t r[4] = {__byte_perm(n0, 0, X.sel), __byte_perm(n1, 0, X.sel), __byte_perm(n2, 0, X.sel),
+                         __byte_perm(n3, 0, X.sel)};
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const uint32_t c256 = __byte_perm(r[j >> 2], 0, 0x4404 | ((j & 3) << 4));  // code * 256
+    const float4 e = *reinterpret_cast<const float4*>(sm + (c256 | (X.xl ^ uint32_t(j << 4))));
+    s[0] += e.x; s[1] += e.y; s[2] += e.z; s[3] += e.w;
+  }
+  if (!FULL && lane >= nv) s[0] = s[1] = s[2] = s[3] = -INFINITY;
+  // ---- softmax: p = exp2(s - mref); the reference maximum only moves up
+  const bool grow = (s[0] > mref[0]) | (s[1] > mref[1]) | (s[2] > mref[2]) | (s[3] > mref[3]);
+  if (__any_sync(0xffffffffu, grow)) {
+    float al[4];
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const float mn = fmaxf(mref[g], warp_max(s[g]));
+      al[g] = fast_exp2(mref[g] - mn);  // first chunk: exp2(-inf) = 0
+      mref[g] = mn;
+      lsum[g] *= al[g];
+    }
+    // acc / zacc columns 2tig, 2tig+1 belong to heads 2tig, 2tig+1 (heads >= 4 unused)
+    const float aa = tig == 0 ? al[0] : tig == 1 ? al[2] : 1.f;
+    const float ab = tig == 0 ? al[1] : tig == 1 ? al[3] : 1.f;
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      acc[m][0] *= aa; acc[m][1] *= ab; acc[m][2] *= aa; acc[m][3] *= ab;
+    }
+    zacc[0] *= aa; zacc[1] *= ab; zacc[2] *= aa; zacc[3] *= ab;
+  }
+  // p in fp16, k-slot order per head (the B operand layout of the P.V MMA)
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const float pg = fast_exp2(s[g] - mref[g]);  // 0 for masked tokens
+    lsum[g] += pg;
+    sts16(pb + g * 64 + L.sz_off, __half_as_ushort(__float2half_rn(pg)));
+  }
+  __syncwarp();  // p, fp16 scales / zeros visible to the warp
+  // ---- P.V: k-step ks covers tokens 16ks + tig + 4u (u = 0..3)
+#pragma unroll
+  for (int ks = 0; ks < 2; ++ks) {
+    const uint32_t p01 = gid < 4 ? lds32(pb + gid * 64 + ks * 32 + tig * 4) : 0u;        // k-slots 2tig, 2tig+1
+    const uint32_t p23 = gid < 4 ? lds32(pb + gid * 64 + ks * 32 + tig * 4 + 16) : 0u;   // k-slots 2tig+8, 2tig+9
+    const uint32_t sb = szs + ks * 32 + tig * 4;
+    uint32_t b0[4], b1[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      b0[j] = hmul2(p01, lds32(sb + j * 64));
+      b1[j] = hmul2(p23, lds32(sb + j * 64 + 16));
+    }
+    {
+      uint32_t az[4] = {0u, 0u, 0u, 0u};
+      if (gid < 4) {
+        az[0] = lds32(sb + 256 + gid * 64);
+        az[2] = lds32(sb + 256 + gid * 64 + 16);
+      }
+      mma_f16_16816(zacc, az, p01, p23);
+    }
+    const uint32_t vb = st + ST_V + (16 * ks + tig) * 32 + gid * 4;
+    const uint32_t w0 = lds32(vb), w1 = lds32(vb + 128), w2 = lds32(vb + 256), w3 = lds32(vb + 384);
+    const uint32_t u01 = __byte_perm(w0, w1, 0x5410), v01 = __byte_perm(w0, w1, 0x7632);
+    const uint32_t u23 = __byte_perm(w2, w3, 0x5410), v23 = __byte_perm(w2, w3, 0x7632);
+    const uint32_t x01[4] = {u01, u01 >> 8, v01, v01 >> 8};
+    const uint32_t x23[4] = {u23, u23 >> 8, v23, v23 >> 8};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const uint32_t m0 = 0x00030003u << (4 * hh), m1 = 0x00030003u << (4 * hh + 2);
+        const uint32_t a[4] = {x01[j] & m0, x01[j] & m1, x23[j] & m0, x23[j] & m1};
+        mma_f16_16816(acc[2 * j + hh], a, b0[j], b1[j]);
+      }
+    }
+  }
+  __syncwarp();
+}
+
 template <int GM>
 __device__ __forceinline__ void v3_window_chunk(const DecodeParams& p, const float* qs, int b, int h, int64_t tb,
                                                 int nvalid, WarpState<GM>& st) {
@@ -622,7 +737,32 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
         v3_issue(p, src, b, h, t0, min(CH, ntok - kc * CH), kc, wreg + i * STAGE_BYTES, &wbar[i]);
       }
     }
-    if (!cb_ready) {  // first history segment: copy the codebook while its first chunks load
+    if constexpr (GM == 4) {
+      // this pair's score table (see v3_chunk_lut); built while the first chunks load
+      __syncthreads();  // qs complete
+      for (int u = threadIdx.x; u < 256 * 16; u += blockDim.x) {
+        const int cc = u >> 4, blk = u & 15;
+        float r4[4] = {0.f, 0.f, 0.f, 0.f};
+        if (cc < p.nc) {
+          const float4 c0 = __ldg(reinterpret_cast<const float4*>(p.cent + (int64_t(blk) * p.nc + cc) * 8));
+          const float4 c1 = __ldg(reinterpret_cast<const float4*>(p.cent + (int64_t(blk) * p.nc + cc) * 8 + 4));
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const float* qg = qs + g * D + blk * 8;
+            float a = qg[0] * c0.x;
+            a = fmaf(qg[1], c0.y, a);
+            a = fmaf(qg[2], c0.z, a);
+            a = fmaf(qg[3], c0.w, a);
+            a = fmaf(qg[4], c1.x, a);
+            a = fmaf(qg[5], c1.y, a);
+            a = fmaf(qg[6], c1.z, a);
+            a = fmaf(qg[7], c1.w, a);
+            r4[g] = a * lscale;
+          }
+        }
+        *reinterpret_cast<float4*>(cb + u * 16) = make_float4(r4[0], r4[1], r4[2], r4[3]);
+      }
+    } else if (!cb_ready) {  // first history segment: copy the codebook while its first chunks load
       // codebook -> shared, entry (block b, code cc) at cc * 256 + sigma(b) * 16
       for (int u = threadIdx.x; u < 16 * 256; u += blockDim.x) {
         const int blk = u >> 8, cc = u & 255;
@@ -638,6 +778,7 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
     uint32_t qa[4][4];
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
+      if constexpr (GM == 4) break;
       const int kp = ks >> 1, s4 = 4 * (ks & 1);
       const float* q0 = qs + gid * D + 8 * (4 * kp + tig) + s4;
       const float* q1 = qs + gid * D + 8 * (8 + 4 * kp + tig) + s4;
@@ -654,16 +795,32 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
       for (int e = 0; e < 4; ++e) acc[m][e] = 0.f;
     float zacc[4] = {0.f, 0.f, 0.f, 0.f};
     float mrun = -INFINITY, lrun = 0.f;
+    float mref[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY}, lsum[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint32_t pb = uint32_t(reinterpret_cast<uint8_t*>(misc) - sm);
+    LutLane X;
+    X.xl = uint32_t(lane & 15) << 4;
+    X.sel = 0u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) X.sel |= uint32_t(i ^ (lane & 3)) << (4 * i);
+    X.swp8 = (lane & 8) != 0;
+    X.swp4 = (lane & 4) != 0;
     for (int i = 0; i < mine; ++i) {
       const int stg = i % ST;
       uint8_t* stage = wreg + stg * STAGE_BYTES;
       if (!failed && !mbar_wait(&wbar[stg], (phase >> stg) & 1u)) failed = true;
       phase ^= 1u << stg;
       const int nv = min(CH, ntok - (wid + WARPS * i) * CH);
-      if (nv == CH)
-        v3_chunk<true>(ring_s + stg * STAGE_BYTES, cb_s, szs, L, qa, G, lscale, nv, acc, zacc, mrun, lrun);
-      else
-        v3_chunk<false>(ring_s + stg * STAGE_BYTES, cb_s, szs, L, qa, G, lscale, nv, acc, zacc, mrun, lrun);
+      if constexpr (GM == 4) {
+        if (nv == CH)
+          v3_chunk_lut<true>(ring_s + stg * STAGE_BYTES, szs, pb, L, X, nv, acc, zacc, mref, lsum);
+        else
+          v3_chunk_lut<false>(ring_s + stg * STAGE_BYTES, szs, pb, L, X, nv, acc, zacc, mref, lsum);
+      } else {
+        if (nv == CH)
+          v3_chunk<true>(ring_s + stg * STAGE_BYTES, cb_s, szs, L, qa, G, lscale, nv, acc, zacc, mrun, lrun);
+        else
+          v3_chunk<false>(ring_s + stg * STAGE_BYTES, cb_s, szs, L, qa, G, lscale, nv, acc, zacc, mrun, lrun);
+      }
       if (lane < 4 && i + ST < mine) {
         const int kc = wid + WARPS * (i + ST);
         v3_issue(p, src, b, h, t0, min(CH, ntok - kc * CH), kc, stage, &wbar[stg]);
@@ -671,12 +828,24 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
     }
 
     // ---- warp epilogue: per head (m, l, zero term) -> misc, then the value sums -> record
-    float l = lrun;
-    l += __shfl_xor_sync(0xffffffffu, l, 1);
-    l += __shfl_xor_sync(0xffffffffu, l, 2);
-    if (tig == 0 && gid < GM) {
-      rec[GM * D + gid * 2] = (mine && mrun != -INFINITY) ? mrun * kLn2 : -INFINITY;  // natural log
-      rec[GM * D + gid * 2 + 1] = l;
+    if constexpr (GM == 4) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const float l = warp_sum(lsum[g]);
+        if (lane == 0) {
+          rec[GM * D + g * 2] = (mine && mref[g] != -INFINITY) ? mref[g] * kLn2 : -INFINITY;  // natural log
+          rec[GM * D + g * 2 + 1] = l;
+        }
+      }
+      __syncwarp();  // p buffer (misc) reads done before the zero terms reuse it
+    } else {
+      float l = lrun;
+      l += __shfl_xor_sync(0xffffffffu, l, 1);
+      l += __shfl_xor_sync(0xffffffffu, l, 2);
+      if (tig == 0 && gid < GM) {
+        rec[GM * D + gid * 2] = (mine && mrun != -INFINITY) ? mrun * kLn2 : -INFINITY;  // natural log
+        rec[GM * D + gid * 2 + 1] = l;
+      }
     }
     // zero term: zacc row gid = value group j (< 4), columns 2tig, 2tig+1 = heads
     if (gid < 4) {
