@@ -35,6 +35,19 @@ namespace smaq {
 #ifndef SMAQ_ABL
 #define SMAQ_ABL 0  // profiling builds only: bit 1 skips P.V, 2 skips score MMAs, 4 skips staging
 #endif
+#ifdef SMAQ_PROF  // profiling builds only: per-phase clock totals of thread 0 of every CTA
+__device__ unsigned long long g_v3_prof[8];
+#define V3_PROF(k)                                                \
+  do {                                                            \
+    if (threadIdx.x == 0) {                                       \
+      const long long now_ = clock64();                           \
+      atomicAdd(&g_v3_prof[k], (unsigned long long)(now_ - prof_t)); \
+      prof_t = now_;                                              \
+    }                                                             \
+  } while (0)
+#else
+#define V3_PROF(k) do {} while (0)
+#endif
 constexpr int CH = 32;  // tokens per chunk
 constexpr int ST_IDX = 0, ST_V = CH * 16, ST_S = CH * 48, ST_Z = CH * 56, STAGE_BYTES = CH * 64;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -264,9 +277,6 @@ __device__ __forceinline__ void v3_chunk(uint32_t st, uint32_t cb_s, uint32_t sz
   __syncwarp();
 }
 
-// One chunk of up to 32 exact recent-window tokens for one warp (lane = token): fp32 scores
-// against the bf16/fp16 keys, online softmax, then P.V with lane owning dims [4 lane, 4 lane + 4).
-// This is _exact_scores / _apply_weights of smaq/score.py:99-124 in the kernel's softmax units.
 // G <= 4: scores from a per-pair lookup table instead of the tensor cores.  Entry (code c,
 // block b) at shared offset c * 256 + b * 16 holds, for the four query heads,
 // scale * log2(e) * q_g[8b .. 8b+8) . decoded_centroid[b][c] in fp32, so a token's score is the
@@ -382,25 +392,32 @@ __device__ __forceinline__ void v3_chunk_lut(uint32_t st, uint32_t szs, uint32_t
   __syncwarp();
 }
 
+// One chunk of up to 8 exact recent-window tokens for one warp: lanes 4j..4j+3 score token j
+// (quarter q of the lane holds dims [32q, 32q + 32)), fp32 against the bf16/fp16 keys; online
+// softmax; then P.V with lane owning dims [4 lane, 4 lane + 4).  This is _exact_scores /
+// _apply_weights of smaq/score.py:99-124 in the kernel's softmax units.
 template <int GM>
 __device__ __forceinline__ void v3_window_chunk(const DecodeParams& p, const float* qs, int b, int h, int64_t tb,
                                                 int nvalid, WarpState<GM>& st) {
   constexpr int D = 128;
   const int lane = threadIdx.x & 31;
   const int G = p.G;
-  const bool valid = lane < nvalid;
+  const int tok = lane >> 2, qt = lane & 3;
+  const bool valid = tok < nvalid;
   float a[GM];
 #pragma unroll
   for (int g = 0; g < GM; ++g) a[g] = 0.f;
   if (valid) {
-    const int64_t rb = b * p.r_sb + (tb + lane) * p.r_st + h * p.r_sh;
+    const int64_t rb = b * p.r_sb + (tb + tok) * p.r_st + h * p.r_sh + 32 * qt;
     if (p.r_dtype == SMAQ_BF16 || p.r_dtype == SMAQ_F16) {
       const bool bf = p.r_dtype == SMAQ_BF16;
       const uint4* kr = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.rk) + rb);
-#pragma unroll 8
-      for (int c8 = 0; c8 < D / 8; ++c8) {
-        const uint4 w = __ldg(kr + c8);
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+      uint4 kw[4];
+#pragma unroll
+      for (int c8 = 0; c8 < 4; ++c8) kw[c8] = __ldg(kr + c8);
+#pragma unroll
+      for (int c8 = 0; c8 < 4; ++c8) {
+        const uint32_t ws[4] = {kw[c8].x, kw[c8].y, kw[c8].z, kw[c8].w};
         float k[8];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -416,34 +433,29 @@ __device__ __forceinline__ void v3_window_chunk(const DecodeParams& p, const flo
 #pragma unroll
         for (int g = 0; g < GM; ++g) {
           if (g >= G) break;
-          const float* qg = qs + g * D + c8 * 8;
+          const float* qg = qs + g * D + 32 * qt + c8 * 8;
 #pragma unroll
           for (int e = 0; e < 8; ++e) a[g] = fmaf(qg[e], k[e], a[g]);
         }
       }
     } else {
-      for (int d = 0; d < D; ++d) {
+      for (int d = 0; d < 32; ++d) {
         const float kv = load_elem(p.rk, p.r_dtype, rb + d);
 #pragma unroll
         for (int g = 0; g < GM; ++g) {
           if (g >= G) break;
-          a[g] = fmaf(qs[g * D + d], kv, a[g]);
+          a[g] = fmaf(qs[g * D + 32 * qt + d], kv, a[g]);
         }
       }
     }
   }
-  float sc[GM];
-#pragma unroll
-  for (int g = 0; g < GM; ++g) sc[g] = valid ? a[g] * p.scale : -INFINITY;
-  st.softmax_chunk(sc, G);
-  // value rows in batches of 8, all loads of a batch in flight together
-  const int64_t vb = b * p.r_sb + tb * p.r_st + h * p.r_sh + lane * 4;
-  for (int j0 = 0; j0 < nvalid; j0 += 8) {
-    float v[8][4];
+  // the chunk's value rows (lane owns dims [4 lane, 4 lane + 4)), loaded before the softmax
+  float v[8][4];
+  {
+    const int64_t vb = b * p.r_sb + tb * p.r_st + h * p.r_sh + lane * 4;
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
-      const int j = j0 + u < nvalid ? j0 + u : j0;
-      const int64_t rb = vb + int64_t(j) * p.r_st;
+      const int64_t rb = vb + int64_t(u < nvalid ? u : 0) * p.r_st;
       if (p.r_dtype == SMAQ_BF16) {
         const uint2 w = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.rv) + rb));
         v[u][0] = bf16lo(w.x); v[u][1] = bf16hi(w.x); v[u][2] = bf16lo(w.y); v[u][3] = bf16hi(w.y);
@@ -452,16 +464,24 @@ __device__ __forceinline__ void v3_window_chunk(const DecodeParams& p, const flo
         for (int e = 0; e < 4; ++e) v[u][e] = load_elem(p.rv, p.r_dtype, rb + e);
       }
     }
+  }
+  float sc[GM];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
+  for (int g = 0; g < GM; ++g) {
+    float r = a[g] + __shfl_xor_sync(0xffffffffu, a[g], 1);
+    r += __shfl_xor_sync(0xffffffffu, r, 2);
+    sc[g] = (valid && qt == 0) ? r * p.scale : -INFINITY;
+  }
+  st.softmax_chunk(sc, G);
 #pragma unroll
-      for (int g = 0; g < GM; ++g) {
-        if (g >= G) break;
-        float pj = __shfl_sync(0xffffffffu, sc[g], (j0 + u) & 31);
-        if (j0 + u >= nvalid) pj = 0.f;
+  for (int u = 0; u < 8; ++u) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) st.acc[g][e] = fmaf(pj, v[u][e], st.acc[g][e]);
-      }
+    for (int g = 0; g < GM; ++g) {
+      if (g >= G) break;
+      float pj = __shfl_sync(0xffffffffu, sc[g], u * 4);
+      if (u >= nvalid) pj = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) st.acc[g][e] = fmaf(pj, v[u][e], st.acc[g][e]);
     }
   }
 }
@@ -630,6 +650,10 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
   int64_t* splan = reinterpret_cast<int64_t*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);
   int* arrive_flag = reinterpret_cast<int*>(splan + C::MAX_FUSED_SEG + 4 + 33);
   const int64_t* plan = p.plan;
+#ifdef SMAQ_PROF
+  long long prof_t = clock64();
+  if (threadIdx.x == 0) atomicAdd(&g_v3_prof[7], 1ull);
+#endif
   if (p.fused) {
     v3_plan(p, splan, splan + C::MAX_FUSED_SEG + 4);
     plan = splan;
@@ -648,6 +672,7 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
   const int64_t per = plan[p.n_seg + 1];
   const int c = blockIdx.x;
   const int64_t lo = int64_t(c) * per, hi = min(lo + per, total);
+  V3_PROF(0);
   if (lo >= hi) return;
 
   // per-lane constants of the score gather (B column = (token gid>>1, half gid&1), block quad tig)
@@ -674,6 +699,33 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
   while (sa < sb_) {
     const int mid = (sa + sb_) >> 1;
     if (plan[mid + 1] > lo) sb_ = mid; else sa = mid + 1;
+  }
+  // warm L2 with what this CTA reads outside its bulk-copied streams (the streams of the whole
+  // step do not fit in L2, so these lines would otherwise come from HBM at full load latency):
+  // the score-table codebook, and the exact window rows of its window segments
+  {
+    if (GM == 4 && threadIdx.x < 16) {
+      const char* cbase = reinterpret_cast<const char*>(p.cent);
+      const uint32_t bytes = uint32_t(p.nc) * 32u;  // one block's [nc][8] fp32 rows
+      if ((reinterpret_cast<uintptr_t>(cbase) & 15) == 0)
+        l2_prefetch(cbase + size_t(threadIdx.x) * bytes, bytes);
+    }
+    for (int s2 = sa; s2 < p.n_seg && plan[s2] < hi; ++s2) {
+      if (!(s2 & 1) || (p.r_dtype != SMAQ_BF16 && p.r_dtype != SMAQ_F16)) continue;
+      const int n2 = seg_tokens(p, s2);
+      if (n2 == 0) continue;
+      const int64_t S2 = plan[s2];
+      int64_t u0 = (lo <= S2) ? 0 : (lo - S2 + RECENT_COST - 1) / RECENT_COST;
+      int64_t u1 = (hi - S2 + RECENT_COST - 1) / RECENT_COST;
+      if (u1 > n2) u1 = n2;
+      const int pair = s2 >> 1, b2 = pair / p.Hkv, h2 = pair - b2 * p.Hkv;
+      for (int64_t i = threadIdx.x; i < 2 * (u1 - u0); i += blockDim.x) {
+        const int64_t t = u0 + (i >> 1);
+        const uint16_t* base = static_cast<const uint16_t*>((i & 1) ? p.rv : p.rk);
+        const char* row = reinterpret_cast<const char*>(base + b2 * p.r_sb + t * p.r_st + h2 * p.r_sh);
+        if ((reinterpret_cast<uintptr_t>(row) & 15) == 0) l2_prefetch(row, 256u);
+      }
+    }
   }
   const float lscale = p.scale * kLog2e;
   for (int s = sa; s < p.n_seg; ++s) {
@@ -713,6 +765,7 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
       __syncthreads();
       v3_merge<GM, WARPS>(p, reinterpret_cast<const float*>(wreg0), C::WARP_BYTES / 4, c + s);
       if (p.fused) v3_arrive(p, plan, s, arrive_flag);
+      V3_PROF(1);
       continue;
     }
 
@@ -738,30 +791,45 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
       }
     }
     if constexpr (GM == 4) {
-      // this pair's score table (see v3_chunk_lut); built while the first chunks load
+      // this pair's score table (see v3_chunk_lut); built while the first chunks load.  Thread t
+      // keeps block t % 16 of the four query rows in registers and fills codes t / 16 + 32 k.
+      V3_PROF(2);
       __syncthreads();  // qs complete
-      for (int u = threadIdx.x; u < 256 * 16; u += blockDim.x) {
-        const int cc = u >> 4, blk = u & 15;
-        float r4[4] = {0.f, 0.f, 0.f, 0.f};
-        if (cc < p.nc) {
-          const float4 c0 = __ldg(reinterpret_cast<const float4*>(p.cent + (int64_t(blk) * p.nc + cc) * 8));
-          const float4 c1 = __ldg(reinterpret_cast<const float4*>(p.cent + (int64_t(blk) * p.nc + cc) * 8 + 4));
+      {
+        const int blk = threadIdx.x & 15;
+        float qv[4][8];
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const float* qg = qs + g * D + blk * 8;
-            float a = qg[0] * c0.x;
-            a = fmaf(qg[1], c0.y, a);
-            a = fmaf(qg[2], c0.z, a);
-            a = fmaf(qg[3], c0.w, a);
-            a = fmaf(qg[4], c1.x, a);
-            a = fmaf(qg[5], c1.y, a);
-            a = fmaf(qg[6], c1.z, a);
-            a = fmaf(qg[7], c1.w, a);
-            r4[g] = a * lscale;
+        for (int g = 0; g < 4; ++g)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) qv[g][e] = qs[g * D + blk * 8 + e] * lscale;
+        const float4* cent4 = reinterpret_cast<const float4*>(p.cent) + int64_t(blk) * p.nc * 2;
+        for (int c0 = threadIdx.x >> 4; c0 < 256; c0 += 4 * (C::THREADS >> 4)) {
+          float4 cv[4][2];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int cc = c0 + k * (C::THREADS >> 4);
+            cv[k][0] = cc < p.nc ? __ldg(cent4 + cc * 2) : make_float4(0.f, 0.f, 0.f, 0.f);
+            cv[k][1] = cc < p.nc ? __ldg(cent4 + cc * 2 + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int cc = c0 + k * (C::THREADS >> 4);
+            if (cc >= 256) break;
+            const float x[8] = {cv[k][0].x, cv[k][0].y, cv[k][0].z, cv[k][0].w,
+                                cv[k][1].x, cv[k][1].y, cv[k][1].z, cv[k][1].w};
+            float r4[4];
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              float a = qv[g][0] * x[0];
+#pragma unroll
+              for (int e = 1; e < 8; ++e) a = fmaf(qv[g][e], x[e], a);
+              r4[g] = a;
+            }
+            *reinterpret_cast<float4*>(cb + (cc * 16 + blk) * 16) = make_float4(r4[0], r4[1], r4[2], r4[3]);
           }
         }
-        *reinterpret_cast<float4*>(cb + u * 16) = make_float4(r4[0], r4[1], r4[2], r4[3]);
       }
+      V3_PROF(3);
     } else if (!cb_ready) {  // first history segment: copy the codebook while its first chunks load
       // codebook -> shared, entry (block b, code cc) at cc * 256 + sigma(b) * 16
       for (int u = threadIdx.x; u < 16 * 256; u += blockDim.x) {
@@ -804,6 +872,7 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
     for (int i = 0; i < 4; ++i) X.sel |= uint32_t(i ^ (lane & 3)) << (4 * i);
     X.swp8 = (lane & 8) != 0;
     X.swp4 = (lane & 4) != 0;
+    V3_PROF(4);
     for (int i = 0; i < mine; ++i) {
       const int stg = i % ST;
       uint8_t* stage = wreg + stg * STAGE_BYTES;
@@ -827,6 +896,7 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
       }
     }
 
+    V3_PROF(5);
     // ---- warp epilogue: per head (m, l, zero term) -> misc, then the value sums -> record
     if constexpr (GM == 4) {
 #pragma unroll
@@ -878,6 +948,7 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
     __syncthreads();
     v3_merge<GM, WARPS>(p, reinterpret_cast<const float*>(wreg0), C::WARP_BYTES / 4, c + s);
     if (p.fused) v3_arrive(p, plan, s, arrive_flag);
+    V3_PROF(6);
   }
   if (failed && lane == 0) atomicExch(reinterpret_cast<int*>(p.plan + p.n_seg + 2), 1);
 }
@@ -903,6 +974,18 @@ static int launch_v3_t(DecodeParams& p, int grid_req, cudaStream_t s, int* grid_
 }
 
 int decode_v2_max_fused_segments() { return V3Cfg<4>::MAX_FUSED_SEG; }
+
+#ifdef SMAQ_PROF
+extern "C" int smaq_debug_v3_prof(unsigned long long* out8, int reset) {
+  cudaDeviceSynchronize();
+  cudaMemcpyFromSymbol(out8, g_v3_prof, sizeof(unsigned long long) * 8);
+  if (reset) {
+    unsigned long long z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    cudaMemcpyToSymbol(g_v3_prof, z, sizeof(z));
+  }
+  return 0;
+}
+#endif
 
 int launch_decode_v2(DecodeParams& p, int grid_req, cudaStream_t s, int* grid_out, bool query_only) {
   if (p.G <= 4) return launch_v3_t<4>(p, grid_req, s, grid_out, query_only);

@@ -51,6 +51,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Prefetch [src, src + bytes) into L2 (bulk, no shared-memory destination).  src 16-byte
+// aligned, bytes a multiple of 16.
+__device__ __forceinline__ void l2_prefetch(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // D[16x8] += A[16x16] * B[16x8], fp16 inputs, fp32 accumulate.
 __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm(
