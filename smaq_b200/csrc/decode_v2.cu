@@ -36,7 +36,7 @@ namespace smaq {
 #define SMAQ_ABL 0  // profiling builds only: bit 1 skips P.V, 2 skips score MMAs, 4 skips staging
 #endif
 #ifdef SMAQ_PROF  // profiling builds only: per-phase clock totals of thread 0 of every CTA
-__device__ unsigned long long g_v3_prof[8];
+__device__ unsigned long long g_v3_prof[16];
 #define V3_PROF(k)                                                \
   do {                                                            \
     if (threadIdx.x == 0) {                                       \
@@ -68,7 +68,7 @@ struct V3Cfg {
   static constexpr int WARP_BYTES = STAGES * STAGE_BYTES + SZ_BYTES + 256;  // ring | s,z | misc
   static constexpr int BAR_BYTES = WARPS * STAGES * 8;
   static constexpr int MAX_FUSED_SEG = 2048;                     // in-kernel partition table
-  static constexpr int PLAN_BYTES = (MAX_FUSED_SEG + 4) * 8 + 33 * 8 + 16;  // table | scan scratch | flag
+  static constexpr int PLAN_BYTES = (MAX_FUSED_SEG + 4) * 8 + 33 * 8 + 16 + MAX_FUSED_SEG * 4;  // table | scan | flag | tokens
   static constexpr int SMEM = CB_BYTES + Q_BYTES + WARPS * WARP_BYTES + BAR_BYTES + PLAN_BYTES;
   static_assert(GM * (128 + 2) * 4 <= STAGES * STAGE_BYTES, "merge record must fit in a ring");
   static_assert(SMEM <= 232448, "shared memory budget");
@@ -488,13 +488,15 @@ __device__ __forceinline__ void v3_window_chunk(const DecodeParams& p, const flo
 
 // The stream-K partition (what decode_plan_kernel writes) computed by one CTA into shared
 // memory: prefix cost of every segment, then total and per-CTA slice.  Block-wide scan.
-__device__ void v3_plan(const DecodeParams& p, int64_t* plan, int64_t* scratch /* [33] */) {
+__device__ void v3_plan(const DecodeParams& p, int64_t* plan, int64_t* scratch /* [33] */, int* ntab) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   if (threadIdx.x == 0) scratch[32] = 0;
   __syncthreads();
   for (int base = 0; base < p.n_seg; base += blockDim.x) {
     const int s = base + threadIdx.x;
-    const int64_t c = (s < p.n_seg) ? seg_span(p, s) : 0;
+    const int n = (s < p.n_seg) ? seg_tokens(p, s) : 0;
+    if (s < p.n_seg) ntab[s] = n;
+    const int64_t c = (int64_t(n) * seg_cost(s) + 15) & ~int64_t(15);
     int64_t x = c;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -531,9 +533,15 @@ __device__ void v3_plan(const DecodeParams& p, int64_t* plan, int64_t* scratch /
 }
 
 // CTAs c0..c1 wrote a partial slot for segment s (none if c1 < c0).
-__device__ __forceinline__ void v3_seg_ctas(const DecodeParams& p, const int64_t* plan, int s, int& c0, int& c1) {
+// Tokens of segment s: from the in-kernel table in single-launch mode (ntab), else from global.
+__device__ __forceinline__ int v3_ntok(const DecodeParams& p, const int* ntab, int s) {
+  return ntab ? ntab[s] : seg_tokens(p, s);
+}
+
+__device__ __forceinline__ void v3_seg_ctas(const DecodeParams& p, const int64_t* plan, const int* ntab, int s, int& c0,
+                                            int& c1) {
   const int64_t per = plan[p.n_seg + 1];
-  const int n = seg_tokens(p, s);
+  const int n = v3_ntok(p, ntab, s);
   const int64_t S = plan[s];
   c0 = int(S / per);
   c1 = n ? int((S + int64_t(n - 1) * seg_cost(s)) / per) : c0 - 1;
@@ -541,26 +549,48 @@ __device__ __forceinline__ void v3_seg_ctas(const DecodeParams& p, const int64_t
 
 // Merge every partial slot of pair (b, h) into the outputs (what decode_merge_kernel does for
 // one pair), reading other CTAs' slots through L2.
-__device__ void v3_final_merge(const DecodeParams& p, const int64_t* plan, int pair) {
+__device__ void v3_final_merge(const DecodeParams& p, const int64_t* plan, const int* ntab, int pair) {
   constexpr int D = 128;
   const int b = pair / p.Hkv, h = pair - b * p.Hkv;
   const int G = p.G;
   const int slot_f = G * (D + 2);
   int c0[2], c1[2];
-  for (int k = 0; k < 2; ++k) v3_seg_ctas(p, plan, pair * 2 + k, c0[k], c1[k]);
+  for (int k = 0; k < 2; ++k) v3_seg_ctas(p, plan, ntab, pair * 2 + k, c0[k], c1[k]);
+  const int nh = c1[0] - c0[0] + 1, nt = nh + (c1[1] - c0[1] + 1);
   for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
     const int g = i / D, d = i - g * D;
-    float M = -INFINITY;
-    for (int k = 0; k < 2; ++k)
-      for (int c = c0[k]; c <= c1[k]; ++c) M = fmaxf(M, __ldcg(p.slots + int64_t(c + pair * 2 + k) * slot_f + G * D + g * 2));
-    float L = 0.f, acc[2] = {0.f, 0.f};
-    for (int k = 0; k < 2; ++k) {
-      for (int c = c0[k]; c <= c1[k]; ++c) {
-        const float* sl = p.slots + int64_t(c + pair * 2 + k) * slot_f;
-        const float mr = __ldcg(sl + G * D + g * 2);
-        const float f = (mr == -INFINITY) ? 0.f : expf(mr - M);
-        acc[k] += __ldcg(sl + g * D + d) * f;
-        L += __ldcg(sl + G * D + g * 2 + 1) * f;
+    // every slot's (m, l, acc) requested at once (up to 8 per pass), then combined
+    float M = -INFINITY, L = 0.f, acc[2] = {0.f, 0.f};
+    for (int j0 = 0; j0 < nt; j0 += 8) {
+      float mr[8], lr[8], ar[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = j0 + u;
+        mr[u] = -INFINITY;
+        lr[u] = ar[u] = 0.f;
+        if (j < nt) {
+          const int k = j < nh ? 0 : 1;
+          const int c = k ? c0[1] + (j - nh) : c0[0] + j;
+          const float* sl = p.slots + int64_t(c + pair * 2 + k) * slot_f;
+          mr[u] = __ldcg(sl + G * D + g * 2);
+          lr[u] = __ldcg(sl + G * D + g * 2 + 1);
+          ar[u] = __ldcg(sl + g * D + d);
+        }
+      }
+      float Mn = M;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) Mn = fmaxf(Mn, mr[u]);
+      if (Mn == -INFINITY) continue;
+      const float sc = (M == -INFINITY) ? 0.f : expf(M - Mn);
+      acc[0] *= sc;
+      acc[1] *= sc;
+      L *= sc;
+      M = Mn;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float f = (mr[u] == -INFINITY) ? 0.f : expf(mr[u] - M);
+        acc[j0 + u < nh ? 0 : 1] += ar[u] * f;
+        L += lr[u] * f;
       }
     }
     const int hq = h * G + g;
@@ -589,13 +619,13 @@ __device__ void v3_final_merge(const DecodeParams& p, const int64_t* plan, int p
 // After this CTA wrote its slot for segment s: count it for the pair; the CTA whose slot
 // completes the pair merges it.  Counter values carry the call's epoch so that a workspace
 // never zeroed reads as "no slots yet"; the merging CTA resets the counter to 0.
-__device__ void v3_arrive(const DecodeParams& p, const int64_t* plan, int s, int* flag) {
+__device__ void v3_arrive(const DecodeParams& p, const int64_t* plan, const int* ntab, int s, int* flag) {
   const int pair = s >> 1;
   if (threadIdx.x == 0) {
     int expected = 0;
     for (int k = 0; k < 2; ++k) {
       int c0, c1;
-      v3_seg_ctas(p, plan, pair * 2 + k, c0, c1);
+      v3_seg_ctas(p, plan, ntab, pair * 2 + k, c0, c1);
       expected += c1 - c0 + 1;
     }
     __threadfence();  // this CTA's slot stores before the count
@@ -616,7 +646,7 @@ __device__ void v3_arrive(const DecodeParams& p, const int64_t* plan, int s, int
     *flag = last;
   }
   __syncthreads();
-  if (*flag) v3_final_merge(p, plan, pair);
+  if (*flag) v3_final_merge(p, plan, ntab, pair);
 }
 
 template <int GM>
@@ -649,23 +679,26 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
   // partition: computed here in single-launch mode, else read from decode_plan_kernel's output
   int64_t* splan = reinterpret_cast<int64_t*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);
   int* arrive_flag = reinterpret_cast<int*>(splan + C::MAX_FUSED_SEG + 4 + 33);
+  int* sntab = arrive_flag + 4;
   const int64_t* plan = p.plan;
+  const int* ntab = nullptr;
 #ifdef SMAQ_PROF
   long long prof_t = clock64();
-  if (threadIdx.x == 0) atomicAdd(&g_v3_prof[7], 1ull);
+  if (threadIdx.x == 0) atomicAdd(&g_v3_prof[15], 1ull);
 #endif
   if (p.fused) {
-    v3_plan(p, splan, splan + C::MAX_FUSED_SEG + 4);
+    v3_plan(p, splan, splan + C::MAX_FUSED_SEG + 4, sntab);
     plan = splan;
+    ntab = sntab;
     // pairs nobody attends (no usable history, no window): zero output, empty partials
     for (int pair = blockIdx.x; pair < p.B * p.Hkv; pair += gridDim.x) {
       int e = 0;
       for (int k = 0; k < 2; ++k) {
         int c0, c1;
-        v3_seg_ctas(p, plan, pair * 2 + k, c0, c1);
+        v3_seg_ctas(p, plan, ntab, pair * 2 + k, c0, c1);
         e += c1 - c0 + 1;
       }
-      if (e == 0) v3_final_merge(p, plan, pair);
+      if (e == 0) v3_final_merge(p, plan, ntab, pair);
     }
   }
   const int64_t total = plan[p.n_seg];
@@ -705,14 +738,20 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
   // the score-table codebook, and the exact window rows of its window segments
   {
     if (GM == 4 && threadIdx.x < 16) {
-      const char* cbase = reinterpret_cast<const char*>(p.cent);
-      const uint32_t bytes = uint32_t(p.nc) * 32u;  // one block's [nc][8] fp32 rows
+      const char* cbase = reinterpret_cast<const char*>(cb16);
+      const uint32_t bytes = uint32_t(p.nc) * 16u;  // one block's [nc][8] fp16 rows
       if ((reinterpret_cast<uintptr_t>(cbase) & 15) == 0)
         l2_prefetch(cbase + size_t(threadIdx.x) * bytes, bytes);
     }
     for (int s2 = sa; s2 < p.n_seg && plan[s2] < hi; ++s2) {
+      if (threadIdx.x < G && !(s2 & 1)) {  // the pair's query rows
+        const int pair = s2 >> 1, b2 = pair / p.Hkv, h2 = pair - b2 * p.Hkv;
+        const size_t es = p.q_dtype == SMAQ_F32 ? 4 : 2;
+        const char* qrow = static_cast<const char*>(p.q) + (b2 * p.q_sb + int64_t(h2 * G + threadIdx.x) * p.q_sh) * es;
+        if ((reinterpret_cast<uintptr_t>(qrow) & 15) == 0) l2_prefetch(qrow, uint32_t(128 * es));
+      }
       if (!(s2 & 1) || (p.r_dtype != SMAQ_BF16 && p.r_dtype != SMAQ_F16)) continue;
-      const int n2 = seg_tokens(p, s2);
+      const int n2 = v3_ntok(p, ntab, s2);
       if (n2 == 0) continue;
       const int64_t S2 = plan[s2];
       int64_t u0 = (lo <= S2) ? 0 : (lo - S2 + RECENT_COST - 1) / RECENT_COST;
@@ -731,7 +770,7 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
   for (int s = sa; s < p.n_seg; ++s) {
     const int64_t S = plan[s];
     if (S >= hi) break;
-    const int n = seg_tokens(p, s);
+    const int n = v3_ntok(p, ntab, s);
     if (n == 0) continue;
     const int cs = seg_cost(s);
     int64_t t0 = (lo <= S) ? 0 : (lo - S + cs - 1) / cs;
@@ -746,6 +785,7 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
     if (s & 1) {
       // ---------------- exact recent window: warp w takes 8-token chunks w, w + WARPS, ...
       __syncthreads();  // qs complete
+      V3_PROF(8);
       const int ntok = int(t1 - t0);
       WarpState<GM> ws;
       ws.init();
@@ -753,6 +793,7 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
       // keeps its latency (key row loads, then value row loads) to about one round
       for (int ch = wid; ch * 8 < ntok; ch += WARPS)
         v3_window_chunk<GM>(p, qs, b, h, t0 + int64_t(ch) * 8, min(8, ntok - ch * 8), ws);
+      V3_PROF(9);
 #pragma unroll
       for (int g = 0; g < GM; ++g) {
 #pragma unroll
@@ -763,8 +804,10 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
         }
       }
       __syncthreads();
+      V3_PROF(10);
       v3_merge<GM, WARPS>(p, reinterpret_cast<const float*>(wreg0), C::WARP_BYTES / 4, c + s);
-      if (p.fused) v3_arrive(p, plan, s, arrive_flag);
+      V3_PROF(11);
+      if (p.fused) v3_arrive(p, plan, ntab, s, arrive_flag);
       V3_PROF(1);
       continue;
     }
@@ -792,41 +835,49 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
     }
     if constexpr (GM == 4) {
       // this pair's score table (see v3_chunk_lut); built while the first chunks load.  Thread t
-      // keeps block t % 16 of the four query rows in registers and fills codes t / 16 + 32 k.
-      V3_PROF(2);
-      __syncthreads();  // qs complete
+      // fills block t % 16 for codes t / 16 + 32 k; its fp16 codebook rows are requested before
+      // the barrier that publishes the query rows.
       {
-        const int blk = threadIdx.x & 15;
+        constexpr int NK = 256 / (C::THREADS >> 4);
+        const int blk = threadIdx.x & 15, c0 = threadIdx.x >> 4;
+        const uint4* cb4 = reinterpret_cast<const uint4*>(cb16) + int64_t(blk) * p.nc;
+        uint4 cw[NK];
+#pragma unroll
+        for (int k = 0; k < NK; ++k) {
+          const int cc = c0 + k * (C::THREADS >> 4);
+          cw[k] = cc < p.nc ? __ldg(cb4 + cc) : make_uint4(0u, 0u, 0u, 0u);
+        }
+        V3_PROF(2);
+        __syncthreads();  // qs complete
         float qv[4][8];
 #pragma unroll
-        for (int g = 0; g < 4; ++g)
+        for (int g = 0; g < 4; ++g) {
+          const float4 a0 = *reinterpret_cast<const float4*>(qs + g * D + blk * 8);
+          const float4 a1 = *reinterpret_cast<const float4*>(qs + g * D + blk * 8 + 4);
+          const float q8[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
-          for (int e = 0; e < 8; ++e) qv[g][e] = qs[g * D + blk * 8 + e] * lscale;
-        const float4* cent4 = reinterpret_cast<const float4*>(p.cent) + int64_t(blk) * p.nc * 2;
-        for (int c0 = threadIdx.x >> 4; c0 < 256; c0 += 4 * (C::THREADS >> 4)) {
-          float4 cv[4][2];
+          for (int e = 0; e < 8; ++e) qv[g][e] = q8[e] * lscale;
+        }
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int cc = c0 + k * (C::THREADS >> 4);
-            cv[k][0] = cc < p.nc ? __ldg(cent4 + cc * 2) : make_float4(0.f, 0.f, 0.f, 0.f);
-            cv[k][1] = cc < p.nc ? __ldg(cent4 + cc * 2 + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = 0; k < NK; ++k) {
+          const int cc = c0 + k * (C::THREADS >> 4);
+          const uint32_t hw[4] = {cw[k].x, cw[k].y, cw[k].z, cw[k].w};
+          float x[8];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hw[e]));
+            x[2 * e] = f.x;
+            x[2 * e + 1] = f.y;
           }
+          float r4[4];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int cc = c0 + k * (C::THREADS >> 4);
-            if (cc >= 256) break;
-            const float x[8] = {cv[k][0].x, cv[k][0].y, cv[k][0].z, cv[k][0].w,
-                                cv[k][1].x, cv[k][1].y, cv[k][1].z, cv[k][1].w};
-            float r4[4];
+          for (int g = 0; g < 4; ++g) {
+            float acc4 = qv[g][0] * x[0];
 #pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              float a = qv[g][0] * x[0];
-#pragma unroll
-              for (int e = 1; e < 8; ++e) a = fmaf(qv[g][e], x[e], a);
-              r4[g] = a;
-            }
-            *reinterpret_cast<float4*>(cb + (cc * 16 + blk) * 16) = make_float4(r4[0], r4[1], r4[2], r4[3]);
+            for (int e = 1; e < 8; ++e) acc4 = fmaf(qv[g][e], x[e], acc4);
+            r4[g] = acc4;
           }
+          *reinterpret_cast<float4*>(cb + (cc * 16 + blk) * 16) = make_float4(r4[0], r4[1], r4[2], r4[3]);
         }
       }
       V3_PROF(3);
@@ -946,8 +997,10 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
       }
     }
     __syncthreads();
+    V3_PROF(12);
     v3_merge<GM, WARPS>(p, reinterpret_cast<const float*>(wreg0), C::WARP_BYTES / 4, c + s);
-    if (p.fused) v3_arrive(p, plan, s, arrive_flag);
+    V3_PROF(13);
+    if (p.fused) v3_arrive(p, plan, ntab, s, arrive_flag);
     V3_PROF(6);
   }
   if (failed && lane == 0) atomicExch(reinterpret_cast<int*>(p.plan + p.n_seg + 2), 1);
@@ -978,9 +1031,9 @@ int decode_v2_max_fused_segments() { return V3Cfg<4>::MAX_FUSED_SEG; }
 #ifdef SMAQ_PROF
 extern "C" int smaq_debug_v3_prof(unsigned long long* out8, int reset) {
   cudaDeviceSynchronize();
-  cudaMemcpyFromSymbol(out8, g_v3_prof, sizeof(unsigned long long) * 8);
+  cudaMemcpyFromSymbol(out8, g_v3_prof, sizeof(unsigned long long) * 16);
   if (reset) {
-    unsigned long long z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    unsigned long long z[16] = {};
     cudaMemcpyToSymbol(g_v3_prof, z, sizeof(z));
   }
   return 0;
