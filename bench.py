@@ -8,6 +8,9 @@ A step = the attention of all 32 layers for one decode token of every sequence.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--workload append]
 
+``--workload paged`` measures configs[3] (Qwen2.5-7B KV shape, 64 sequences of 1K-64K tokens in
+a 16-token paged store, 4-bit scalar keys, 64-token window); ``--workload longctx`` configs[4]
+(Llama-3-70B KV shape, 4 x 128K, KV heads sharded over the ranks, strong scaling).
 ``--workload append`` measures BASELINE.json configs[2] instead: a batch of 8 x 8192 new tokens x
 8 KV heads x head_dim 128 in bf16 quantized into store rows (tcgen05 rotation + 3-bit scalar key
 codes, 2-bit values in groups of 32); GB/s counts input plus output bytes.
@@ -52,7 +55,7 @@ def parse():
     ap.add_argument("--hq", type=int, default=32)
     ap.add_argument("--hkv", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "append", "longctx"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "append", "longctx", "paged"])
     return ap.parse_args()
 
 
@@ -467,6 +470,186 @@ def run_append_reference(a, rank: int):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- paged
+PG_B, PG_HQ, PG_HKV, PG_LAYERS, PG_PAGE, PG_W, PG_BITS = 64, 28, 4, 28, 16, 64, 4
+
+
+def paged_lengths():
+    from smaq_b200 import synthetic as syn
+    return syn.seq_lengths(PG_B, 1024, 65536)
+
+
+def paged_bytes_per_layer(lens) -> int:
+    D = 128
+    per_tok = (D // 2 + 2) + (D // 4 + 2 * 2 * (D // 32))     # 4-bit codes + norm, values
+    return int(sum(lens)) * PG_HKV * per_tok + PG_B * (PG_HKV * PG_W * 2 * D * 2 + PG_HQ * D * 2 * 2)
+
+
+def paged_config():
+    return {"workload": "cfg3_qwen2.5_7b_paged_scalar4", "layers": PG_LAYERS, "batch": PG_B, "n_q_heads": PG_HQ,
+            "n_kv_heads": PG_HKV, "head_dim": 128, "page_size": PG_PAGE, "lengths": "U[1024, 65536] seed 4",
+            "window_tokens": PG_W, "keys": "scalar 4-bit", "values": "2-bit g32",
+            "l2": "inputs larger than L2 (no flush)"}
+
+
+def paged_cpu_sample(seconds_cap: float = 20.0):
+    """The reference's hybrid attention (oracle port, fp32) for one layer x one sequence of the
+    mean length, scaled to the step."""
+    from oracle import smaq_oracle as O
+    from smaq_b200 import synthetic as syn
+    lens = paged_lengths()
+    n = int(np.mean(lens))
+    rng = np.random.default_rng(6)
+    D = 128
+    codes = rng.integers(0, 256, size=(PG_HKV, n, 64), dtype=np.uint8)
+    norms = np.abs(rng.standard_normal((PG_HKV, n))).astype(np.float32)
+    Einv = np.linalg.qr(rng.standard_normal((D, D)))[0].astype(np.float32)
+    cent = np.linspace(-2, 2, 16).astype(np.float32)
+    vdata = rng.integers(0, 256, size=(PG_HKV, n, 32), dtype=np.uint8)
+    vs = np.abs(rng.standard_normal((PG_HKV, n, 4))).astype(np.float32)
+    vz = rng.standard_normal((PG_HKV, n, 4)).astype(np.float32)
+    q = syn.queries((1, PG_HQ), D, seed=9)
+    rk = syn.keys((PG_W, PG_HKV), D, seed=10)
+    rv = syn.values((PG_W, PG_HKV), D, seed=11)
+    runs = []
+    t_end = time.perf_counter() + seconds_cap
+    while True:
+        t0 = time.perf_counter()
+        K = O.scalar_score_keys(codes, norms, PG_BITS, Einv, cent, D)
+        V = O.dequantize_values(vdata, vs, vz, 2, 32)
+        O.hybrid_attention(q, "bf16", K, V, rk, rv, PG_HQ, PG_HKV, work=np.float32)
+        runs.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end or len(runs) >= 5:
+            break
+    t = statistics.median(runs)
+    step_s = t * PG_LAYERS * PG_B
+    return {"value": PG_B / step_s, "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"1 layer x 1 sequence of {n} tokens, median of {len(runs)} runs = {t*1e3:.1f} ms, "
+                      f"scaled x{PG_LAYERS * PG_B}"}
+
+
+def run_paged(a, rank: int, world: int):
+    import torch
+    from smaq_b200 import build, ops, synthetic as syn
+    from smaq_b200._lib import SMAQ_KEYS_SCALAR
+    from smaq_b200.quantizer import SMAQQuantizer
+    build.build()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    D = 128
+    lens = paged_lengths()
+    quant = SMAQQuantizer(D, bits=PG_BITS, device=dev)
+    quant.fit(torch.from_numpy(syn.calibration_queries(512, D)).to(dev))
+    U_np, outl = syn.basis(D)
+    U = torch.from_numpy(U_np.astype(np.float32)).to(dev)
+    lam = torch.from_numpy(np.sqrt(syn.spectrum(D)).astype(np.float32)).to(dev)
+    outl = torch.from_numpy(outl).to(dev)
+    pages = [(int(n) + PG_PAGE - 1) // PG_PAGE for n in lens]
+    n_pages, maxp = sum(pages), max(pages)
+    rng = np.random.default_rng(40 + rank)
+    bf = torch.bfloat16
+    layers = []
+    for li in range(PG_LAYERS):
+        gen = torch.Generator(device=dev).manual_seed(1000 * (rank + 1) + li)
+        perm = rng.permutation(n_pages)
+        bt = np.zeros((PG_B, maxp), np.int32)
+        o = 0
+        for b in range(PG_B):
+            bt[b, :pages[b]] = perm[o:o + pages[b]]
+            o += pages[b]
+        L = {"codes": torch.empty((n_pages, PG_HKV, PG_PAGE, D // 2), dtype=torch.uint8, device=dev),
+             "norms": torch.empty((n_pages, PG_HKV, PG_PAGE), dtype=bf, device=dev),
+             "vdata": torch.empty((n_pages, PG_HKV, PG_PAGE, D // 4), dtype=torch.uint8, device=dev),
+             "vs": torch.empty((n_pages, PG_HKV, PG_PAGE, D // 32), dtype=bf, device=dev),
+             "vz": torch.empty((n_pages, PG_HKV, PG_PAGE, D // 32), dtype=bf, device=dev),
+             "bt": torch.from_numpy(bt).to(dev)}
+        for b in range(PG_B):
+            n = int(lens[b])
+            k = spectral_keys_gpu(n * PG_HKV, gen, U, lam, outl, bf).reshape(n, PG_HKV, D)
+            v = torch.randn((n, PG_HKV, D), generator=gen, device=dev, dtype=torch.float32).to(bf)
+            t = torch.arange(n, device=dev)
+            slots = L["bt"][b, t // PG_PAGE].to(torch.int64) * PG_PAGE + t % PG_PAGE
+            ops.append(k, v, n_heads=PG_HKV, slots=slots, page_size=PG_PAGE, key_format=SMAQ_KEYS_SCALAR,
+                       key_bits=PG_BITS, E=quant.E, boundaries=quant.decision_boundaries, key_codes=L["codes"],
+                       key_norms=L["norms"], v_data=L["vdata"], v_scales=L["vs"], v_zeros=L["vz"])
+        L["rk"] = spectral_keys_gpu(PG_B * PG_W * PG_HKV, gen, U, lam, outl, bf).reshape(PG_B, PG_W, PG_HKV, D)
+        L["rv"] = torch.randn((PG_B, PG_W, PG_HKV, D), generator=gen, device=dev, dtype=torch.float32).to(bf)
+        L["q"] = torch.randn((PG_B, PG_HQ, D), generator=gen, device=dev, dtype=torch.float32).to(bf)
+        L["out"] = torch.empty((PG_B, PG_HQ, D), dtype=bf, device=dev)
+        layers.append(L)
+    torch.cuda.synchronize()
+    hl = torch.from_numpy(lens.astype(np.int32)).to(dev)
+    rl = torch.full((PG_B,), PG_W, dtype=torch.int32, device=dev)
+    ws = torch.empty(ops.decode_workspace_bytes(PG_B, PG_HQ, PG_HKV, D), dtype=torch.uint8, device=dev)
+
+    def dec(L, q=None):
+        ops.decode(L["q"] if q is None else q, n_kv_heads=PG_HKV, key_format=SMAQ_KEYS_SCALAR, key_bits=PG_BITS,
+                   E_inv=quant.E_inv, centroids=quant.centroids, key_norms=L["norms"], key_codes=L["codes"],
+                   v_data=L["vdata"], v_scales=L["vs"], v_zeros=L["vz"], hist_len=hl, page_size=PG_PAGE,
+                   block_table=L["bt"], recent_k=L["rk"], recent_v=L["rv"], recent_len=rl, out=L["out"], workspace=ws)
+
+    def step():
+        for L in layers:
+            dec(L)
+
+    for _ in range(max(3, a.warmup)):
+        step()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.steps
+    ck = clocks.stop()
+    hq = [torch.empty_like(L["q"], device="cpu").pin_memory() for L in layers]
+    for h, L in zip(hq, layers):
+        h.copy_(L["q"].cpu())
+    ho = [torch.empty_like(L["out"], device="cpu").pin_memory() for L in layers]
+    dq = [torch.empty_like(L["q"]) for L in layers]
+
+    def e2e_step():
+        for i, L in enumerate(layers):
+            dq[i].copy_(hq[i], non_blocking=True)
+            dec(L, dq[i])
+            ho[i].copy_(L["out"], non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(a.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / a.steps
+    bpl = paged_bytes_per_layer(lens)
+    try:
+        peak = float(json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))["hbm_gbs"])
+    except Exception:
+        peak = 6650.0
+    achieved = bpl * PG_LAYERS / (ms * 1e-3) / 1e9
+    line = {"metric": METRIC, "value": PG_B / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": a.steps,
+            "warmup": max(3, a.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32-accum/bf16-io", "data": "synthetic", "config": paged_config(),
+            "hbm_gbs": achieved,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "kernel": "smaq_decode (scalar keys, paged) per step",
+                         "algorithmic_bytes_per_launch": bpl},
+            "e2e": {"value": PG_B / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in hq),
+                    "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in ho)},
+            "gpu_launches": 3 * PG_LAYERS * a.steps, "clocks": ck}
+    if not a.no_cpu_baseline:
+        line["cpu_baseline"] = paged_cpu_sample()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 # ----------------------------------------------------------------------------- main
 def main():
     a = parse()
@@ -478,6 +661,20 @@ def main():
             run_append_reference(a, rank)
         else:
             run_append(a, rank, world)
+        return
+    if a.workload == "paged":
+        if a.impl == "reference":
+            if rank == 0:
+                info = paged_cpu_sample(seconds_cap=max(2.0, 60.0 / max(1, a.steps)))
+                print(json.dumps({"impl": "reference", "metric": METRIC, "value": info["value"], "unit": "tokens/s",
+                                  "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+                                  "ms_per_step": 1e3 * PG_B / info["value"], "higher_is_better": True,
+                                  "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                                  "config": paged_config(), "cpu_baseline": info,
+                                  "e2e": {"value": info["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                          "d2h_bytes_per_step": 0}}), flush=True)
+        else:
+            run_paged(a, rank, world)
         return
     if a.workload == "longctx":
         # Llama-3-70B KV shape, 4 x 128K, 80 layers; strong scaling,
