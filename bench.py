@@ -531,7 +531,7 @@ def paged_cpu_sample(seconds_cap: float = 20.0):
 def run_paged(a, rank: int, world: int):
     import torch
     from smaq_b200 import build, ops, synthetic as syn
-    from smaq_b200._lib import SMAQ_KEYS_SCALAR
+    from smaq_b200._lib import SMAQ_KEYS_SCALAR, SMAQ_LAYOUT_DECODE
     from smaq_b200.quantizer import SMAQQuantizer
     build.build()
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -572,7 +572,8 @@ def run_paged(a, rank: int, world: int):
             slots = L["bt"][b, t // PG_PAGE].to(torch.int64) * PG_PAGE + t % PG_PAGE
             ops.append(k, v, n_heads=PG_HKV, slots=slots, page_size=PG_PAGE, key_format=SMAQ_KEYS_SCALAR,
                        key_bits=PG_BITS, E=quant.E, boundaries=quant.decision_boundaries, key_codes=L["codes"],
-                       key_norms=L["norms"], v_data=L["vdata"], v_scales=L["vs"], v_zeros=L["vz"])
+                       key_norms=L["norms"], v_data=L["vdata"], v_scales=L["vs"], v_zeros=L["vz"],
+                       layout=SMAQ_LAYOUT_DECODE)
         L["rk"] = spectral_keys_gpu(PG_B * PG_W * PG_HKV, gen, U, lam, outl, bf).reshape(PG_B, PG_W, PG_HKV, D)
         L["rv"] = torch.randn((PG_B, PG_W, PG_HKV, D), generator=gen, device=dev, dtype=torch.float32).to(bf)
         L["q"] = torch.randn((PG_B, PG_HQ, D), generator=gen, device=dev, dtype=torch.float32).to(bf)
@@ -587,7 +588,8 @@ def run_paged(a, rank: int, world: int):
         ops.decode(L["q"] if q is None else q, n_kv_heads=PG_HKV, key_format=SMAQ_KEYS_SCALAR, key_bits=PG_BITS,
                    E_inv=quant.E_inv, centroids=quant.centroids, key_norms=L["norms"], key_codes=L["codes"],
                    v_data=L["vdata"], v_scales=L["vs"], v_zeros=L["vz"], hist_len=hl, page_size=PG_PAGE,
-                   block_table=L["bt"], recent_k=L["rk"], recent_v=L["rv"], recent_len=rl, out=L["out"], workspace=ws)
+                   block_table=L["bt"], recent_k=L["rk"], recent_v=L["rv"], recent_len=rl, out=L["out"], workspace=ws,
+                   layout=SMAQ_LAYOUT_DECODE)
 
     def step():
         for L in layers:
@@ -643,7 +645,7 @@ def run_paged(a, rank: int, world: int):
             "e2e": {"value": PG_B / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in hq),
                     "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in ho)},
-            "gpu_launches": 3 * PG_LAYERS * a.steps, "clocks": ck}
+            "gpu_launches": PG_LAYERS * a.steps, "clocks": ck}
     if not a.no_cpu_baseline:
         line["cpu_baseline"] = paged_cpu_sample()
     if rank == 0:

@@ -39,7 +39,9 @@
  *     the index of block b, so the pair of blocks (b, b + 4) a tensor-core lane gathers for
  *     one token sits in one 16-bit half of one 32-bit word;
  *   2-bit values (head_dim 128): byte 4 * g + j of a row holds reference byte 8 * j + g
- *     (g < 8, j < 4), so each 32-bit word carries one byte of every value group.
+ *     (g < 8, j < 4), so each 32-bit word carries one byte of every value group;
+ *   3/4-bit scalar key codes (head_dim 128, 64-byte rows): byte 16 * (p % 4) + p / 4 holds
+ *     reference byte p, so the 16 bytes a tensor-core lane needs for one token are contiguous.
  * Reference-layout bytes are recovered by the inverse permutation.
  */
 #ifndef SMAQ_B200_H_

@@ -584,6 +584,7 @@ static int launch_decode_g(DecodeParams& p, int kb, int vb, int grid_req, cudaSt
 
 static int dispatch_decode(DecodeParams& p, int kb, int vb, int grid_req, cudaStream_t s, int* grid_out,
                            bool query_only) {
+  if (kb != 0 && decode_s_eligible(p, kb, vb)) return launch_decode_s(p, grid_req, s, grid_out, query_only);
   if (kb == 0 && decode_v2_eligible(p, SMAQ_KEYS_BVQ, vb, p.q_dtype))
     return launch_decode_v2(p, grid_req, s, grid_out, query_only);
   if (p.G <= 1) return launch_decode_g<1>(p, kb, vb, grid_req, s, grid_out, query_only);
@@ -686,8 +687,9 @@ extern "C" int smaq_decode(const smaq_decode_args* args, void* stream) {
   p.pair_cnt = reinterpret_cast<uint64_t*>(static_cast<char*>(a.workspace) + plan_table_bytes(p.n_seg));
   p.slots = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + plan_bytes(p.n_seg));
   p.grid = grid;
-  if (kb == 0 && decode_v2_eligible(p, SMAQ_KEYS_BVQ, a.value_bits, p.q_dtype) &&
-      p.n_seg <= decode_v2_max_fused_segments()) {
+  if ((kb == 0 && decode_v2_eligible(p, SMAQ_KEYS_BVQ, a.value_bits, p.q_dtype) &&
+       p.n_seg <= decode_v2_max_fused_segments()) ||
+      (kb != 0 && decode_s_eligible(p, kb, a.value_bits))) {
     // one launch: partition, history, window and the per-pair merge in the tensor-core kernel
     static std::atomic<uint32_t> epochs{0};
     uint32_t e = ++epochs;

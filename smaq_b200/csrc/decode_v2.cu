@@ -1006,6 +1006,451 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
   if (failed && lane == 0) atomicExch(reinterpret_cast<int*>(p.plan + p.n_seg + 2), 1);
 }
 
+// =====================================================================================
+// Scalar 3/4-bit keys (SMAQQuantizer.attention_score, smaq/quantizer.py:154-184: scores =
+// (q @ E_inv^T) . centroids[codes] * norm * scale) with 2-bit group-32 values, decode layout,
+// bf16/fp16 queries, G <= 8.  Same partition, window, slots and merge as decode_v3_kernel.
+//  * Scores on the tensor cores (mma.m16n8k16, rows = 16 tokens, columns = 8 query heads,
+//    k = 16 dims).  The rotated query is split q = q_hi + q_lo (fp16) and so is every centroid
+//    value (c = c_hi + c_lo); three MMAs per k-step (q_hi c_hi + q_lo c_hi + q_hi c_lo) keep
+//    the products to ~2^-21 relative, i.e. fp32-class scores.
+//  * A operands come straight from the code bytes: one byte = two dims = one A register, looked
+//    up in two shared 256-entry tables of fp16 pairs (c_hi and c_lo), replicated per lane so
+//    every lookup is conflict-free.  The decode layout puts the 16 code bytes one lane needs
+//    for a token next to each other.
+//  * The norm, the softmax (reference maximum per head that only moves up) and P.V follow the
+//    block-VQ kernel.
+// =====================================================================================
+constexpr int SK_STAGE = CH * 64 + CH * 32 + CH * 8 + CH * 8 + CH * 2;  // codes | values | scales | zeros | norms
+constexpr int SK_V = CH * 64, SK_S = CH * 96, SK_Z = CH * 104, SK_N = CH * 112;
+
+struct SCfg {
+  static constexpr int WARPS = 16;
+  static constexpr int THREADS = WARPS * 32;
+  static constexpr int STAGES = 2;
+  static constexpr int TAB_BYTES = 2 * 256 * 32 * 4;                 // c_hi, c_lo tables x 32 lanes
+  static constexpr int Q_BYTES = 8 * 128 * 4;                       // fp32 query rows (rotation, window)
+  static constexpr int B_BYTES = 8 * 32 * 16;                       // B fragments [ks][lane]
+  static constexpr int SZ_BYTES = 2 * 4 * CH * 2;
+  static constexpr int PB_BYTES = 8 * 64;                           // p, fp16, [head][k-slot]
+  static constexpr int WARP_BYTES = STAGES * SK_STAGE + SZ_BYTES + PB_BYTES;
+  static constexpr int BAR_BYTES = WARPS * STAGES * 8;
+  static constexpr int MAX_FUSED_SEG = 1024;
+  static constexpr int PLAN_BYTES = (MAX_FUSED_SEG + 4) * 8 + 33 * 8 + 16 + MAX_FUSED_SEG * 4;
+  static constexpr int SMEM = TAB_BYTES + Q_BYTES + B_BYTES + WARPS * WARP_BYTES + BAR_BYTES + PLAN_BYTES;
+  static_assert(8 * (128 + 2) * 4 <= STAGES * SK_STAGE, "merge record must fit in a ring");
+  static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+template <bool FULL>
+__device__ __forceinline__ void sk_chunk(uint32_t st, uint32_t szs, uint32_t pb, uint32_t bfr, uint32_t tab_l,
+                                         const V3Lane& L, int nv, float (&acc)[8][4], float (&zacc)[4],
+                                         float (&mref)[2], float (&lsum)[2]) {
+  const int lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  // ---- value scales / zeros as fp16 in k-slot order (one token per lane)
+  {
+    uint2 s2 = lds64(st + SK_S + lane * 8);
+    uint2 z2 = lds64(st + SK_Z + lane * 8);
+    if (!FULL && lane >= nv) s2 = z2 = make_uint2(0u, 0u);
+    const uint32_t sp0 = pack_f16x2(bf16lo(s2.x), bf16hi(s2.x)), sp1 = pack_f16x2(bf16lo(s2.y), bf16hi(s2.y));
+    const uint32_t zp0 = pack_f16x2(bf16lo(z2.x), bf16hi(z2.x)), zp1 = pack_f16x2(bf16lo(z2.y), bf16hi(z2.y));
+    const uint32_t o = szs + L.sz_off;
+    sts16(o + 0, uint16_t(sp0)); sts16(o + 64, uint16_t(sp0 >> 16));
+    sts16(o + 128, uint16_t(sp1)); sts16(o + 192, uint16_t(sp1 >> 16));
+    sts16(o + 256, uint16_t(zp0)); sts16(o + 320, uint16_t(zp0 >> 16));
+    sts16(o + 384, uint16_t(zp1)); sts16(o + 448, uint16_t(zp1 >> 16));
+  }
+  // ---- scores: two 16-token tiles; thread holds tokens 16T + gid (+8), heads 2tig, 2tig+1
+  float d[2][4];
+  uint4 cr[2][2];  // code bytes of tokens 16T + gid and 16T + gid + 8 (16 contiguous bytes each)
+#pragma unroll
+  for (int T = 0; T < 2; ++T) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) cr[T][r] = lds128(st + (16 * T + gid + 8 * r) * 64 + 16 * tig);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) d[T][e] = 0.f;
+  }
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const uint4 bq = lds128(bfr + (ks * 32 + lane) * 16);  // b0 hi, b1 hi, b0 lo, b1 lo
+#pragma unroll
+    for (int T = 0; T < 2; ++T) {
+      uint32_t ah[4], al[4];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const uint32_t wv = (ks >> 1) == 0 ? cr[T][r].x : (ks >> 1) == 1 ? cr[T][r].y : (ks >> 1) == 2 ? cr[T][r].z : cr[T][r].w;
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {  // byte 2ks + h2 of the lane's 16: dims 16ks + 8h2 + 2tig, +1
+          const uint32_t by = __byte_perm(wv, 0, 0x4440 | uint32_t((2 * (ks & 1) + h2)));
+          const uint32_t off = tab_l + (by << 7);
+          ah[r + 2 * h2] = lds32(off);
+          al[r + 2 * h2] = lds32(off + 256 * 32 * 4);
+        }
+      }
+      mma_f16_16816(d[T], ah, bq.x, bq.y);   // q_hi . c_hi
+      mma_f16_16816(d[T], ah, bq.z, bq.w);   // q_lo . c_hi
+      mma_f16_16816(d[T], al, bq.x, bq.y);   // q_hi . c_lo
+    }
+  }
+  // times the token's norm; masked tokens -inf
+  float s[2][4];
+#pragma unroll
+  for (int T = 0; T < 2; ++T) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int t = 16 * T + gid + 8 * r;
+      const float nrm = __uint_as_float(uint32_t(*reinterpret_cast<const uint16_t*>(sm + st + SK_N + 2 * t)) << 16);
+      const bool ok = FULL || t < nv;
+      s[T][2 * r] = ok ? d[T][2 * r] * nrm : -INFINITY;
+      s[T][2 * r + 1] = ok ? d[T][2 * r + 1] * nrm : -INFINITY;
+    }
+  }
+  // ---- softmax for heads 2tig (c = 0) and 2tig + 1 (c = 1) over the warp's 32 tokens
+  bool grow = false;
+#pragma unroll
+  for (int T = 0; T < 2; ++T)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) grow |= s[T][e] > mref[e & 1];
+  if (__any_sync(0xffffffffu, grow)) {
+    float al2[2];
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      float mx = fmaxf(fmaxf(s[0][c], s[0][c + 2]), fmaxf(s[1][c], s[1][c + 2]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      const float mn = fmaxf(mref[c], mx);
+      al2[c] = fast_exp2(mref[c] - mn);
+      mref[c] = mn;
+      lsum[c] *= al2[c];
+    }
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      acc[m][0] *= al2[0]; acc[m][1] *= al2[1]; acc[m][2] *= al2[0]; acc[m][3] *= al2[1];
+    }
+    zacc[0] *= al2[0]; zacc[1] *= al2[1]; zacc[2] *= al2[0]; zacc[3] *= al2[1];
+  }
+  // p -> fp16 in the P.V B layout: row = head, k-slot of token t (see V3Lane::sz_off)
+#pragma unroll
+  for (int T = 0; T < 2; ++T) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int t = 16 * T + gid + 8 * r;
+      const int u = (t >> 2) & 3, v = t & 3;
+      const uint32_t slot = uint32_t(2 * (16 * T + 2 * v + (u & 1) + 8 * (u >> 1)));
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const float pv = fast_exp2(s[T][2 * r + c] - mref[c]);
+        lsum[c] += pv;
+        sts16(pb + (2 * tig + c) * 64 + slot, __half_as_ushort(__float2half_rn(pv)));
+      }
+    }
+  }
+  __syncwarp();
+  // ---- P.V: as the block-VQ kernel, all 8 head columns live
+#pragma unroll
+  for (int ks = 0; ks < 2; ++ks) {
+    const uint32_t p01 = lds32(pb + gid * 64 + ks * 32 + tig * 4);
+    const uint32_t p23 = lds32(pb + gid * 64 + ks * 32 + tig * 4 + 16);
+    const uint32_t sb = szs + ks * 32 + tig * 4;
+    uint32_t b0[4], b1[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      b0[j] = hmul2(p01, lds32(sb + j * 64));
+      b1[j] = hmul2(p23, lds32(sb + j * 64 + 16));
+    }
+    {
+      uint32_t az[4] = {0u, 0u, 0u, 0u};
+      if (gid < 4) {
+        az[0] = lds32(sb + 256 + gid * 64);
+        az[2] = lds32(sb + 256 + gid * 64 + 16);
+      }
+      mma_f16_16816(zacc, az, p01, p23);
+    }
+    const uint32_t vb = st + SK_V + (16 * ks + tig) * 32 + gid * 4;
+    const uint32_t w0 = lds32(vb), w1 = lds32(vb + 128), w2 = lds32(vb + 256), w3 = lds32(vb + 384);
+    const uint32_t u01 = __byte_perm(w0, w1, 0x5410), v01 = __byte_perm(w0, w1, 0x7632);
+    const uint32_t u23 = __byte_perm(w2, w3, 0x5410), v23 = __byte_perm(w2, w3, 0x7632);
+    const uint32_t x01[4] = {u01, u01 >> 8, v01, v01 >> 8};
+    const uint32_t x23[4] = {u23, u23 >> 8, v23, v23 >> 8};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const uint32_t m0 = 0x00030003u << (4 * hh), m1 = 0x00030003u << (4 * hh + 2);
+        const uint32_t a[4] = {x01[j] & m0, x01[j] & m1, x23[j] & m0, x23[j] & m1};
+        mma_f16_16816(acc[2 * j + hh], a, b0[j], b1[j]);
+      }
+    }
+  }
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(SCfg::THREADS, 1) decode_s_kernel(DecodeParams p) {
+  using C = SCfg;
+  constexpr int D = 128, GM = 8;
+  constexpr int ST = C::STAGES;
+  constexpr int WARPS = C::WARPS;
+  uint8_t* tab = sm;                                                   // [2][256][32] fp16 pairs
+  float* qs = reinterpret_cast<float*>(sm + C::TAB_BYTES);
+  uint8_t* bfrag = sm + C::TAB_BYTES + C::Q_BYTES;
+  uint8_t* wreg0 = bfrag + C::B_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(wreg0 + WARPS * C::WARP_BYTES);
+
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int G = p.G;
+  uint8_t* wreg = wreg0 + wid * C::WARP_BYTES;                       // ring | s,z | p
+  const uint32_t szs = uint32_t(wreg + ST * SK_STAGE - sm);
+  const uint32_t pbuf = szs + C::SZ_BYTES;
+  float* misc = reinterpret_cast<float*>(sm + pbuf);                  // zero terms after the loop
+  float* rec = reinterpret_cast<float*>(wreg);
+  uint64_t* wbar = bars + wid * ST;
+  if (lane == 0) {
+    for (int s = 0; s < ST; ++s) mbar_init(&wbar[s], 5);
+    fence_mbar_init();
+  }
+  uint32_t phase = 0;
+  bool failed = false;
+
+  int64_t* splan = reinterpret_cast<int64_t*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);
+  int* arrive_flag = reinterpret_cast<int*>(splan + C::MAX_FUSED_SEG + 4 + 33);
+  int* sntab = arrive_flag + 4;
+  const int64_t* plan = p.plan;
+  const int* ntab = nullptr;
+  if (p.fused) {
+    v3_plan(p, splan, splan + C::MAX_FUSED_SEG + 4, sntab);
+    plan = splan;
+    ntab = sntab;
+    for (int pair = blockIdx.x; pair < p.B * p.Hkv; pair += gridDim.x) {
+      int e = 0;
+      for (int k = 0; k < 2; ++k) {
+        int c0, c1;
+        v3_seg_ctas(p, plan, ntab, pair * 2 + k, c0, c1);
+        e += c1 - c0 + 1;
+      }
+      if (e == 0) v3_final_merge(p, plan, ntab, pair);
+    }
+  }
+  const int64_t total = plan[p.n_seg];
+  const int64_t per = plan[p.n_seg + 1];
+  const int c = blockIdx.x;
+  const int64_t lo = int64_t(c) * per, hi = min(lo + per, total);
+  if (lo >= hi) return;
+
+  V3Lane L;
+  {
+    const int ks = lane >> 4, u = (lane >> 2) & 3, v = lane & 3;
+    L.sz_off = uint32_t(2 * (16 * ks + 2 * v + (u & 1) + 8 * (u >> 1)));
+  }
+  // code byte -> (c_hi[lo nibble], c_hi[hi nibble]) and the c_lo pair, replicated per lane:
+  // entry (byte, lane) at byte * 128 + lane * 4
+  {
+    const int bits = p.nc == 8 ? 3 : 4;
+    const uint32_t mask = (1u << bits) - 1u;
+    for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) {
+      const int by = i >> 5;
+      const float c0v = __ldg(p.cent + (by & mask)), c1v = __ldg(p.cent + ((by >> bits) & mask));
+      const __half h0 = __float2half_rn(c0v), h1 = __float2half_rn(c1v);
+      const __half l0 = __float2half_rn(c0v - __half2float(h0)), l1 = __float2half_rn(c1v - __half2float(h1));
+      *reinterpret_cast<uint32_t*>(tab + i * 4) = uint32_t(__half_as_ushort(h0)) | (uint32_t(__half_as_ushort(h1)) << 16);
+      *reinterpret_cast<uint32_t*>(tab + 256 * 32 * 4 + i * 4) =
+          uint32_t(__half_as_ushort(l0)) | (uint32_t(__half_as_ushort(l1)) << 16);
+    }
+  }
+  const uint32_t tab_l = uint32_t(lane * 4);
+  const uint32_t ring_s = uint32_t(wreg - sm);
+  const uint32_t bfr = uint32_t(bfrag - sm);
+  __syncthreads();
+
+  int sa = 0, sb_ = p.n_seg - 1;
+  while (sa < sb_) {
+    const int mid = (sa + sb_) >> 1;
+    if (plan[mid + 1] > lo) sb_ = mid; else sa = mid + 1;
+  }
+  const float lscale = p.scale * kLog2e;
+  for (int s = sa; s < p.n_seg; ++s) {
+    const int64_t S = plan[s];
+    if (S >= hi) break;
+    const int n = v3_ntok(p, ntab, s);
+    if (n == 0) continue;
+    const int cs = seg_cost(s);
+    int64_t t0 = (lo <= S) ? 0 : (lo - S + cs - 1) / cs;
+    int64_t t1 = (hi - S + cs - 1) / cs;
+    if (t1 > n) t1 = n;
+    if (t0 >= t1) continue;
+    const int pair = s >> 1, b = pair / p.Hkv, h = pair - b * p.Hkv;
+    for (int i = threadIdx.x; i < 8 * D; i += blockDim.x) {
+      const int g = i / D, d = i - g * D;
+      qs[i] = g < G ? load_elem(p.q, p.q_dtype, b * p.q_sb + int64_t(h * G + g) * p.q_sh + d) : 0.f;
+    }
+    if (s & 1) {
+      __syncthreads();  // qs complete
+      const int ntok = int(t1 - t0);
+      WarpState<GM> ws;
+      ws.init();
+      for (int ch = wid; ch * 8 < ntok; ch += WARPS)
+        v3_window_chunk<GM>(p, qs, b, h, t0 + int64_t(ch) * 8, min(8, ntok - ch * 8), ws);
+#pragma unroll
+      for (int g = 0; g < GM; ++g) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) rec[g * D + lane * 4 + e] = g < G ? ws.acc[g][e] : 0.f;
+        if (lane == 0) {
+          rec[GM * D + g * 2] = g < G ? ws.m[g] : -INFINITY;
+          rec[GM * D + g * 2 + 1] = g < G ? ws.l[g] : 0.f;
+        }
+      }
+      __syncthreads();
+      v3_merge<GM, WARPS>(p, reinterpret_cast<const float*>(wreg0), C::WARP_BYTES / 4, c + s);
+      if (p.fused) v3_arrive(p, plan, ntab, s, arrive_flag);
+      continue;
+    }
+
+    // ---------------- compressed history
+    const int ntok = int(t1 - t0);
+    const int nchunks = (ntok + CH - 1) / CH;
+    const int mine = (wid < nchunks) ? (nchunks - 1 - wid) / WARPS + 1 : 0;
+    V3Src src;
+    {
+      const int k = lane < 5 ? lane : 0;
+      const uint8_t* base = k == 0 ? p.kcodes
+                            : k == 1 ? p.vdata
+                            : k == 2 ? static_cast<const uint8_t*>(p.vscales)
+                            : k == 3 ? static_cast<const uint8_t*>(p.vzeros)
+                                     : static_cast<const uint8_t*>(p.knorms);
+      src.row_bytes = k == 0 ? 64u : k == 1 ? 32u : k == 4 ? 2u : 8u;
+      src.dst_off = k == 0 ? 0u : k == 1 ? uint32_t(SK_V) : k == 2 ? uint32_t(SK_S) : k == 3 ? uint32_t(SK_Z) : uint32_t(SK_N);
+      src.base = p.bt ? base : base + ((int64_t(b) * p.Hkv + h) * p.page_size + t0) * src.row_bytes;
+    }
+    if (lane < 5) {
+      for (int i = 0; i < ST && i < mine; ++i) {
+        const int kc = wid + WARPS * i;
+        v3_issue(p, src, b, h, t0, min(CH, ntok - kc * CH), kc, wreg + i * SK_STAGE, &wbar[i]);
+      }
+    }
+    __syncthreads();  // qs complete
+    // rotated, scaled query q_r[g][j] = scale log2(e) sum_k q[g][k] E_inv[j][k], as fp16 hi + lo,
+    // in B-fragment order: entry (ks, lane) = {b0 hi, b1 hi, b0 lo, b1 lo} for head gid, dims
+    // 16 ks + 2 tig (+1) and 16 ks + 8 + 2 tig (+1)
+    {
+      for (int o = threadIdx.x; o < 8 * 32 * 4; o += blockDim.x) {
+        // o -> (ks, ln, word): each thread computes the four dims of one B word pair
+        const int ks = o >> 7, ln = (o >> 2) & 31, wsel = o & 3;
+        const int g = ln >> 2, tg = ln & 3;
+        const int dj = 16 * ks + 8 * (wsel & 1) + 2 * tg;  // first of the two dims of this word
+        uint32_t word = 0u;
+        if (g < G) {
+          float r2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float4* er = reinterpret_cast<const float4*>(p.E_inv + (dj + e) * D);
+            const float* qg = qs + g * D;
+            float a = 0.f;
+#pragma unroll 8
+            for (int k4 = 0; k4 < D / 4; ++k4) {
+              const float4 ev = __ldg(er + k4);
+              a = fmaf(qg[4 * k4], ev.x, a);
+              a = fmaf(qg[4 * k4 + 1], ev.y, a);
+              a = fmaf(qg[4 * k4 + 2], ev.z, a);
+              a = fmaf(qg[4 * k4 + 3], ev.w, a);
+            }
+            r2[e] = a * lscale;
+          }
+          if (wsel < 2) {
+            word = pack_f16x2(r2[0], r2[1]);
+          } else {
+            const float h0 = __half2float(__float2half_rn(r2[0])), h1 = __half2float(__float2half_rn(r2[1]));
+            word = pack_f16x2(r2[0] - h0, r2[1] - h1);
+          }
+        }
+        *reinterpret_cast<uint32_t*>(bfrag + (ks * 32 + ln) * 16 + wsel * 4) = word;
+      }
+    }
+    __syncthreads();  // B fragments complete
+
+    float acc[8][4];
+#pragma unroll
+    for (int m = 0; m < 8; ++m)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[m][e] = 0.f;
+    float zacc[4] = {0.f, 0.f, 0.f, 0.f};
+    float mref[2] = {-INFINITY, -INFINITY}, lsum[2] = {0.f, 0.f};
+    for (int i = 0; i < mine; ++i) {
+      const int stg = i % ST;
+      uint8_t* stage = wreg + stg * SK_STAGE;
+      if (!failed && !mbar_wait(&wbar[stg], (phase >> stg) & 1u)) failed = true;
+      phase ^= 1u << stg;
+      const int nv = min(CH, ntok - (wid + WARPS * i) * CH);
+      if (nv == CH)
+        sk_chunk<true>(ring_s + stg * SK_STAGE, szs, pbuf, bfr, tab_l, L, nv, acc, zacc, mref, lsum);
+      else
+        sk_chunk<false>(ring_s + stg * SK_STAGE, szs, pbuf, bfr, tab_l, L, nv, acc, zacc, mref, lsum);
+      if (lane < 5 && i + ST < mine) {
+        const int kc = wid + WARPS * (i + ST);
+        v3_issue(p, src, b, h, t0, min(CH, ntok - kc * CH), kc, stage, &wbar[stg]);
+      }
+    }
+    // ---- warp epilogue: heads 2tig, 2tig+1 -> (m, l); zero terms; value sums -> record
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      float l = lsum[cc];
+      l += __shfl_xor_sync(0xffffffffu, l, 4);
+      l += __shfl_xor_sync(0xffffffffu, l, 8);
+      l += __shfl_xor_sync(0xffffffffu, l, 16);
+      if (gid == 0) {
+        const int g = 2 * tig + cc;
+        rec[GM * D + g * 2] = (mine && mref[cc] != -INFINITY) ? mref[cc] * kLn2 : -INFINITY;
+        rec[GM * D + g * 2 + 1] = l;
+      }
+    }
+    __syncwarp();  // p buffer reads done before the zero terms reuse it
+    if (gid < 4) {
+      misc[(2 * tig) * 4 + gid] = zacc[0];
+      misc[(2 * tig + 1) * 4 + gid] = zacc[1];
+    }
+    __syncwarp();
+    {
+      const int ga = 2 * tig, gb = 2 * tig + 1;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float za = misc[ga * 4 + j], zb = misc[gb * 4 + j];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int d0 = 32 * j + 4 * gid + 2 * hh;
+          const float s0 = hh ? 1048576.0f : 16777216.0f;
+          const float s1 = hh ? 262144.0f : 4194304.0f;
+          rec[ga * D + d0] = fmaf(acc[2 * j + hh][0], s0, za);
+          rec[ga * D + d0 + 1] = fmaf(acc[2 * j + hh][2], s1, za);
+          rec[gb * D + d0] = fmaf(acc[2 * j + hh][1], s0, zb);
+          rec[gb * D + d0 + 1] = fmaf(acc[2 * j + hh][3], s1, zb);
+        }
+      }
+    }
+    __syncthreads();
+    v3_merge<GM, WARPS>(p, reinterpret_cast<const float*>(wreg0), C::WARP_BYTES / 4, c + s);
+    if (p.fused) v3_arrive(p, plan, ntab, s, arrive_flag);
+  }
+  if (failed && lane == 0) atomicExch(reinterpret_cast<int*>(p.plan + p.n_seg + 2), 1);
+}
+
+bool decode_s_eligible(const DecodeParams& p, int key_bits, int value_bits) {
+  return (key_bits == 3 || key_bits == 4) && value_bits == 2 && p.D == 128 && p.gs == 32 && p.G <= 8 &&
+         p.layout == SMAQ_LAYOUT_DECODE && p.kv_dtype == SMAQ_BF16 && p.page_size % 16 == 0 &&
+         (p.q_dtype == SMAQ_BF16 || p.q_dtype == SMAQ_F16) && p.n_seg <= SCfg::MAX_FUSED_SEG && p.E_inv != nullptr;
+}
+
+int launch_decode_s(DecodeParams& p, int grid_req, cudaStream_t s, int* grid_out, bool query_only) {
+  auto kern = decode_s_kernel;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SCfg::SMEM);
+  if (e != cudaSuccess) return cuda_status(e, "decode_s attr");
+  const int grid = grid_req > 0 ? grid_req : num_sms();
+  *grid_out = grid;
+  if (query_only) return SMAQ_OK;
+  kern<<<grid, SCfg::THREADS, SCfg::SMEM, s>>>(p);
+  return cuda_status(cudaGetLastError(), "decode_s_kernel");
+}
+
 bool decode_v2_eligible(const DecodeParams& p, int key_format, int value_bits, int q_dtype) {
   (void)q_dtype;
   return key_format == SMAQ_KEYS_BVQ && value_bits == 2 && p.D == 128 && p.gs == 32 && p.G <= 8 &&

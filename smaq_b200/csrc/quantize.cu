@@ -223,7 +223,7 @@ __global__ void __launch_bounds__(SQ_WARPS * 32) scalar_key_kernel(
     const typename DT::T* __restrict__ k, int64_t n_tokens, int n_heads, int64_t st, int64_t sh,
     const RowMap rm,
     const float* __restrict__ E, const float* __restrict__ bnd, uint8_t* __restrict__ codes,
-    typename DT::T* __restrict__ norms) {
+    typename DT::T* __restrict__ norms, int layout) {
   constexpr int D = 32 * EPL;
   constexpr int NB = (1 << BITS) - 1;
   constexpr int VPB = (8 / BITS) > 0 ? 8 / BITS : 1;
@@ -331,7 +331,11 @@ __global__ void __launch_bounds__(SQ_WARPS * 32) scalar_key_kernel(
         }
       } else {                        // 3- and 4-bit: two codes per byte at shifts 0 and BITS
 #pragma unroll
-        for (int e = 0; e < EPL; e += 2) dst[(lane * EPL + e) / 2] = uint8_t(c[e] | (c[e + 1] << BITS));
+        for (int e = 0; e < EPL; e += 2) {
+          const int pb = (lane * EPL + e) / 2;
+          // decode layout (3/4-bit, head_dim 128): reference byte p at 16 (p % 4) + p / 4
+          dst[layout == SMAQ_LAYOUT_DECODE ? 16 * (pb & 3) + (pb >> 2) : pb] = uint8_t(c[e] | (c[e + 1] << BITS));
+        }
       }
       if (lane == 0) norms[row] = from_f<DT>(nrm[rr]);
     }
@@ -549,7 +553,7 @@ static int launch_scalar_t(const smaq_append_args& a, cudaStream_t s) {
   using T = typename DT::T;
   kern<<<grid, SQ_WARPS * 32, sm, s>>>(static_cast<const T*>(a.k), a.n_tokens, a.n_heads, a.k_stride_t,
                                        a.k_stride_h, make_rowmap(a), a.E,
-                                       a.boundaries, a.key_codes, static_cast<T*>(a.key_norms));
+                                       a.boundaries, a.key_codes, static_cast<T*>(a.key_norms), a.layout);
   return cuda_status(cudaGetLastError(), "scalar_key_kernel");
 }
 
@@ -629,8 +633,10 @@ static int validate_append(const smaq_append_args& a) {
   if (a.layout != SMAQ_LAYOUT_REFERENCE && a.layout != SMAQ_LAYOUT_DECODE)
     return fail(SMAQ_ERR_INVALID, "append: unknown layout %d", a.layout);
   if (a.layout == SMAQ_LAYOUT_DECODE) {
-    if (a.head_dim != 128 || (a.v && a.value_bits != 2) || (a.k && a.key_format == SMAQ_KEYS_BVQ && a.block_dim != 8))
-      return fail(SMAQ_ERR_UNSUPPORTED, "decode layout needs head_dim 128, 2-bit values, 8-dim VQ blocks");
+    if (a.head_dim != 128 || (a.v && a.value_bits != 2) || (a.k && a.key_format == SMAQ_KEYS_BVQ && a.block_dim != 8) ||
+        (a.k && a.key_format == SMAQ_KEYS_SCALAR && a.key_bits != 3 && a.key_bits != 4))
+      return fail(SMAQ_ERR_UNSUPPORTED,
+                  "decode layout needs head_dim 128, 2-bit values, 8-dim VQ blocks, 3/4-bit scalar keys");
     if (a.page_size % 16) return fail(SMAQ_ERR_INVALID, "decode layout needs page_size %% 16 == 0");
   }
   if (a.v) {

@@ -262,7 +262,7 @@ template <int BITS>
 __global__ void __launch_bounds__(TR_THREADS, 1) tc_scalar_key_kernel(
     const __grid_constant__ CUtensorMap kmap, int64_t n_tokens, int n_heads, const RowMap rm,
     const float* __restrict__ E, const float* __restrict__ bnd, uint8_t* __restrict__ codes,
-    __nv_bfloat16* __restrict__ norms) {
+    __nv_bfloat16* __restrict__ norms, int layout) {
   constexpr int NB = (1 << BITS) - 1;
   constexpr int VPB = BITS == 2 ? 4 : 2;      // codes per byte (3-bit packs two per byte)
   constexpr int PD = TR_D / VPB;              // bytes per code row
@@ -483,9 +483,23 @@ __global__ void __launch_bounds__(TR_THREADS, 1) tc_scalar_key_kernel(
       int64_t tok;
       int h;
       rm.token_head(r, tok, h);
-      uint4* dst = reinterpret_cast<uint4*>(codes + rm.row(tok, h) * PD + half * (PD / 2));
+      uint8_t* crow = codes + rm.row(tok, h) * PD;
+      if (BITS != 2 && layout == SMAQ_LAYOUT_DECODE) {
+        // decode layout: reference byte p at 16 (p % 4) + p / 4, i.e. byte t of this half's
+        // word i goes to 16 t + 8 half + i
 #pragma unroll
-      for (int k = 0; k < PD / 32; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+        for (int t = 0; t < 4; ++t) {
+          const uint32_t sel = uint32_t(t) | (uint32_t(t + 4) << 4);
+          const uint32_t lo = __byte_perm(__byte_perm(w[0], w[1], sel), __byte_perm(w[2], w[3], sel), 0x5410);
+          const uint32_t hi = __byte_perm(__byte_perm(w[4 % (PD / 8)], w[5 % (PD / 8)], sel),
+                                          __byte_perm(w[6 % (PD / 8)], w[7 % (PD / 8)], sel), 0x5410);
+          *reinterpret_cast<uint2*>(crow + 16 * t + 8 * half) = make_uint2(lo, hi);
+        }
+      } else {
+        uint4* dst = reinterpret_cast<uint4*>(crow + half * (PD / 2));
+#pragma unroll
+        for (int k = 0; k < PD / 32; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+      }
     }
   }
   if (failed) atomicOr(&g_tc_rotate_fault, 1u);
@@ -532,7 +546,7 @@ static int launch_bits(const smaq_append_args& a, const CUtensorMap& map, cudaSt
   const int64_t tiles = (a.n_tokens + tok_per_tile - 1) / tok_per_tile;
   const int grid = int(tiles < num_sms() ? tiles : num_sms());
   kern<<<grid, TR_THREADS, TR_SMEM, s>>>(map, a.n_tokens, a.n_heads, make_rowmap(a), a.E,
-                                         a.boundaries, a.key_codes, static_cast<__nv_bfloat16*>(a.key_norms));
+                                         a.boundaries, a.key_codes, static_cast<__nv_bfloat16*>(a.key_norms), a.layout);
   return cuda_status(cudaGetLastError(), "tc_scalar_key_kernel");
 }
 

@@ -302,6 +302,14 @@ def bvq_to_reference(idx: torch.Tensor) -> torch.Tensor:
     return idx[..., pos]
 
 
+_SPERM = [16 * (k % 4) + k // 4 for k in range(64)]         # 3/4-bit scalar code byte k at _SPERM[k]
+
+
+def scalar_codes_to_reference(codes: torch.Tensor) -> torch.Tensor:
+    """Decode-layout 3/4-bit scalar key code rows ``(..., 64)`` -> reference byte order."""
+    return codes[..., _SPERM]
+
+
 def fp16_codebook(decoded_centroids: torch.Tensor) -> Optional[torch.Tensor]:
     """fp16 copy of a decoded codebook if it is exactly fp16-valued (enables the tensor-core
     decode kernel), else None."""

@@ -113,6 +113,8 @@ def run_case(cuda, kind, bits, B, Hkv, G, hist, recent, page_size, dtype, seed, 
         vdata_t = ops.values_to_reference(vdata_t)
         if kind == "bvq":
             codes_t = ops.bvq_to_reference(codes_t)
+        else:
+            codes_t = ops.scalar_codes_to_reference(codes_t)
     codes, norms = tn(codes_t), tn(st["norms"])
     vdata, vs, vz = tn(vdata_t), tn(st["vs"]), tn(st["vz"])
     bt = tn(st["bt"])
@@ -202,3 +204,38 @@ def test_decode_layout_bytes_are_permuted_reference_bytes(cuda):
     assert torch.equal(out[1][2], out[0][2]) and torch.equal(out[1][3], out[0][3])
     ref_idx = ops.quantize_keys_bvq(k, Eb, C).reshape(64, 2, 16).transpose(0, 1)
     assert torch.equal(out[0][0], ref_idx)
+
+
+@pytest.mark.parametrize("bits", [3, 4])
+@pytest.mark.parametrize("G", [1, 4, 7, 8])
+def test_fast_scalar_decode_paged(cuda, bits, G):
+    """Scalar-key fast path (decode layout, split-fp16 tensor-core scores) against the oracle."""
+    run_case(cuda, "scalar", bits, B=5, Hkv=2, G=G, hist=[1000, 15, 16, 333, 2048], recent=[64, 3, 0, 128, 1],
+             page_size=16, dtype="bfloat16", seed=41, layout=1)
+
+
+@pytest.mark.parametrize("num_ctas", [1, 7, 300])
+def test_fast_scalar_partition_invariance(cuda, num_ctas):
+    run_case(cuda, "scalar", 4, B=3, Hkv=2, G=7, hist=[3000, 100, 17], recent=[64, 0, 9], page_size=16,
+             dtype="bfloat16", seed=43, num_ctas=num_ctas, layout=1)
+
+
+@pytest.mark.parametrize("bits", [3, 4])
+def test_scalar_decode_layout_bytes(cuda, bits):
+    """Decode-layout scalar code rows (SIMT and tensor-core append kernels) hold the reference
+    bytes permuted (bit-exact), norms identical."""
+    import torch
+    from smaq_b200 import ops
+    from smaq_b200._lib import SMAQ_KEYS_SCALAR
+    qz = scalar_tables(bits, cuda)
+    for dt, H in ((torch.bfloat16, 2), (torch.float32, 2), (torch.bfloat16, 3)):
+        k = torch.from_numpy(syn.keys((256, H), D, seed=51)).to(cuda).to(dt)
+        out = {}
+        for lay in (0, 1):
+            codes = torch.zeros((H, 256, 64), dtype=torch.uint8, device=cuda)
+            norms = torch.zeros((H, 256), dtype=dt, device=cuda)
+            ops.append(k, None, n_heads=H, page_size=256, key_format=SMAQ_KEYS_SCALAR, key_bits=bits, E=qz.E,
+                       boundaries=qz.decision_boundaries, key_codes=codes, key_norms=norms, layout=lay)
+            out[lay] = (codes, norms)
+        assert torch.equal(ops.scalar_codes_to_reference(out[1][0]), out[0][0])
+        assert torch.equal(out[1][1], out[0][1])
