@@ -1015,8 +1015,8 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
 //    value (c = c_hi + c_lo); three MMAs per k-step (q_hi c_hi + q_lo c_hi + q_hi c_lo) keep
 //    the products to ~2^-21 relative, i.e. fp32-class scores.
 //  * A operands come straight from the code bytes: one byte = two dims = one A register, looked
-//    up in two shared 256-entry tables of fp16 pairs (c_hi and c_lo), replicated per lane so
-//    every lookup is conflict-free.  The decode layout puts the 16 code bytes one lane needs
+//    up in a shared 256-entry table of (c_hi pair, c_lo pair), replicated per lane so every
+//    lookup is conflict-free.  The decode layout puts the 16 code bytes one lane needs
 //    for a token next to each other.
 //  * The norm, the softmax (reference maximum per head that only moves up) and P.V follow the
 //    block-VQ kernel.
@@ -1063,29 +1063,27 @@ __device__ __forceinline__ void sk_chunk(uint32_t st, uint32_t szs, uint32_t pb,
   }
   // ---- scores: two 16-token tiles; thread holds tokens 16T + gid (+8), heads 2tig, 2tig+1
   float d[2][4];
-  uint4 cr[2][2];  // code bytes of tokens 16T + gid and 16T + gid + 8 (16 contiguous bytes each)
 #pragma unroll
   for (int T = 0; T < 2; ++T) {
-#pragma unroll
-    for (int r = 0; r < 2; ++r) cr[T][r] = lds128(st + (16 * T + gid + 8 * r) * 64 + 16 * tig);
+    // code bytes of tokens 16T + gid and 16T + gid + 8 (the lane's 16 contiguous bytes each)
+    const uint4 c0 = lds128(st + (16 * T + gid) * 64 + 16 * tig);
+    const uint4 c1 = lds128(st + (16 * T + gid + 8) * 64 + 16 * tig);
 #pragma unroll
     for (int e = 0; e < 4; ++e) d[T][e] = 0.f;
-  }
 #pragma unroll
-  for (int ks = 0; ks < 8; ++ks) {
-    const uint4 bq = lds128(bfr + (ks * 32 + lane) * 16);  // b0 hi, b1 hi, b0 lo, b1 lo
-#pragma unroll
-    for (int T = 0; T < 2; ++T) {
+    for (int ks = 0; ks < 8; ++ks) {
+      const uint4 bq = lds128(bfr + (ks * 32 + lane) * 16);  // b0 hi, b1 hi, b0 lo, b1 lo
       uint32_t ah[4], al[4];
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
-        const uint32_t wv = (ks >> 1) == 0 ? cr[T][r].x : (ks >> 1) == 1 ? cr[T][r].y : (ks >> 1) == 2 ? cr[T][r].z : cr[T][r].w;
+        const uint4& cw = r ? c1 : c0;
+        const uint32_t wv = (ks >> 1) == 0 ? cw.x : (ks >> 1) == 1 ? cw.y : (ks >> 1) == 2 ? cw.z : cw.w;
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {  // byte 2ks + h2 of the lane's 16: dims 16ks + 8h2 + 2tig, +1
-          const uint32_t by = __byte_perm(wv, 0, 0x4440 | uint32_t((2 * (ks & 1) + h2)));
-          const uint32_t off = tab_l + (by << 7);
-          ah[r + 2 * h2] = lds32(off);
-          al[r + 2 * h2] = lds32(off + 256 * 32 * 4);
+          const uint32_t b256 = __byte_perm(wv, 0, 0x4404 | (uint32_t(2 * (ks & 1) + h2) << 4));  // byte * 256
+          const uint2 e2 = lds64(b256 | tab_l);   // (c_hi pair, c_lo pair)
+          ah[r + 2 * h2] = e2.x;
+          al[r + 2 * h2] = e2.y;
         }
       }
       mma_f16_16816(d[T], ah, bq.x, bq.y);   // q_hi . c_hi
@@ -1192,7 +1190,7 @@ __global__ void __launch_bounds__(SCfg::THREADS, 1) decode_s_kernel(DecodeParams
   constexpr int D = 128, GM = 8;
   constexpr int ST = C::STAGES;
   constexpr int WARPS = C::WARPS;
-  uint8_t* tab = sm;                                                   // [2][256][32] fp16 pairs
+  uint8_t* tab = sm;                                                   // [256][32] (hi, lo) fp16 pairs
   float* qs = reinterpret_cast<float*>(sm + C::TAB_BYTES);
   uint8_t* bfrag = sm + C::TAB_BYTES + C::Q_BYTES;
   uint8_t* wreg0 = bfrag + C::B_BYTES;
@@ -1244,8 +1242,8 @@ __global__ void __launch_bounds__(SCfg::THREADS, 1) decode_s_kernel(DecodeParams
     const int ks = lane >> 4, u = (lane >> 2) & 3, v = lane & 3;
     L.sz_off = uint32_t(2 * (16 * ks + 2 * v + (u & 1) + 8 * (u >> 1)));
   }
-  // code byte -> (c_hi[lo nibble], c_hi[hi nibble]) and the c_lo pair, replicated per lane:
-  // entry (byte, lane) at byte * 128 + lane * 4
+  // code byte -> (c_hi[lo nibble], c_hi[hi nibble]) | (c_lo pair), replicated per lane so a
+  // warp's 32 lookups hit 32 distinct bank pairs: entry (byte, lane) at byte * 256 + lane * 8
   {
     const int bits = p.nc == 8 ? 3 : 4;
     const uint32_t mask = (1u << bits) - 1u;
@@ -1254,12 +1252,12 @@ __global__ void __launch_bounds__(SCfg::THREADS, 1) decode_s_kernel(DecodeParams
       const float c0v = __ldg(p.cent + (by & mask)), c1v = __ldg(p.cent + ((by >> bits) & mask));
       const __half h0 = __float2half_rn(c0v), h1 = __float2half_rn(c1v);
       const __half l0 = __float2half_rn(c0v - __half2float(h0)), l1 = __float2half_rn(c1v - __half2float(h1));
-      *reinterpret_cast<uint32_t*>(tab + i * 4) = uint32_t(__half_as_ushort(h0)) | (uint32_t(__half_as_ushort(h1)) << 16);
-      *reinterpret_cast<uint32_t*>(tab + 256 * 32 * 4 + i * 4) =
-          uint32_t(__half_as_ushort(l0)) | (uint32_t(__half_as_ushort(l1)) << 16);
+      *reinterpret_cast<uint2*>(tab + i * 8) =
+          make_uint2(uint32_t(__half_as_ushort(h0)) | (uint32_t(__half_as_ushort(h1)) << 16),
+                     uint32_t(__half_as_ushort(l0)) | (uint32_t(__half_as_ushort(l1)) << 16));
     }
   }
-  const uint32_t tab_l = uint32_t(lane * 4);
+  const uint32_t tab_l = uint32_t(lane * 8);
   const uint32_t ring_s = uint32_t(wreg - sm);
   const uint32_t bfr = uint32_t(bfrag - sm);
   __syncthreads();
