@@ -322,184 +322,6 @@ __global__ void decode_merge_kernel(DecodeParams p, void* out, int64_t o_sb, int
   }
 }
 
-// Exact recent window + merge, one CTA per (sequence, kv head): used with the tensor-core
-// history kernel, whose stream-K partition then covers only compressed history.  The window is
-// attended in fp32 exactly like the reference's _exact_scores/_apply_weights (score.py:99-124)
-// and combined with the history partial slots under one softmax.
-constexpr int FIN_THREADS = 512, FIN_CHUNK = 128, FIN_PARTS = FIN_THREADS / 128;
-__device__ __forceinline__ float fin_bf16(uint32_t w, int hi) { return __uint_as_float(hi ? (w & 0xffff0000u) : (w << 16)); }
-
-__global__ void __launch_bounds__(FIN_THREADS) decode_finish_kernel(DecodeParams p, void* out, int64_t o_sb,
-                                                                     int64_t o_sh, float* partial_out) {
-  constexpr int D = 128;
-  __shared__ __align__(16) float qs[8 * D];
-  __shared__ float sc[8][FIN_CHUNK];
-  __shared__ float mrec[8], lrec[8], arec[8];
-  __shared__ float half_acc[FIN_PARTS][8][D];
-  const int pair = blockIdx.x;
-  const int b = pair / p.Hkv, h = pair - b * p.Hkv;
-  const int G = p.G;
-  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  for (int i = tid; i < G * D; i += blockDim.x)
-    qs[i] = load_elem(p.q, p.q_dtype, b * p.q_sb + int64_t(h * G + i / D) * p.q_sh + (i % D));
-  if (tid < 8) {
-    mrec[tid] = -INFINITY;
-    lrec[tid] = 0.f;
-  }
-  const int W = p.recent_len ? p.recent_len[b] : 0;
-  const bool bf = p.r_dtype == SMAQ_BF16;
-  const int d = tid & (D - 1), part = tid >> 7;   // P.V: dimension d, token quarter `part`
-  float accr[8];
-#pragma unroll
-  for (int g = 0; g < 8; ++g) accr[g] = 0.f;
-  __syncthreads();
-  for (int t0 = 0; t0 < W; t0 += FIN_CHUNK) {
-    const int n = min(FIN_CHUNK, W - t0);
-    {  // scores: warp w takes tokens w, w+8, ...; lane holds dims [4 lane, 4 lane + 4) of q
-      float qr[8][4];
-#pragma unroll
-      for (int g = 0; g < 8; ++g)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) qr[g][e] = g < G ? qs[g * D + lane * 4 + e] : 0.f;
-      for (int tb = wid; tb < n; tb += 16 * 8) {
-        float kv[8][4];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {  // 8 key rows in flight
-          const int t = tb + u * 16;
-          const int64_t rb = b * p.r_sb + int64_t(t0 + (t < n ? t : 0)) * p.r_st + h * p.r_sh + lane * 4;
-          if (bf) {
-            const uint2 w = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p.rk) + rb));
-            kv[u][0] = fin_bf16(w.x, 0); kv[u][1] = fin_bf16(w.x, 1); kv[u][2] = fin_bf16(w.y, 0); kv[u][3] = fin_bf16(w.y, 1);
-          } else {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) kv[u][e] = load_elem(p.rk, p.r_dtype, rb + e);
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int t = tb + u * 16;
-#pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            if (g >= G) break;
-            float a = qr[g][0] * kv[u][0];
-            a = fmaf(qr[g][1], kv[u][1], a);
-            a = fmaf(qr[g][2], kv[u][2], a);
-            a = fmaf(qr[g][3], kv[u][3], a);
-            a = warp_sum(a);
-            if (lane == 0 && t < n) sc[g][t] = a * p.scale;
-          }
-        }
-      }
-    }
-    __syncthreads();
-    if (wid < G) {  // warp g: chunk max, rescale factor, p and running sum
-      const int g = wid;
-      float mx = -INFINITY;
-      for (int t = lane; t < n; t += 32) mx = fmaxf(mx, sc[g][t]);
-      mx = warp_max(mx);
-      const float mn = fmaxf(mrec[g], mx);
-      float ls = 0.f;
-      for (int t = lane; t < n; t += 32) {
-        const float pv = expf(sc[g][t] - mn);
-        sc[g][t] = pv;
-        ls += pv;
-      }
-      ls = warp_sum(ls);
-      if (lane == 0) {
-        const float al = expf(mrec[g] - mn);
-        arec[g] = al;
-        lrec[g] = lrec[g] * al + ls;
-        mrec[g] = mn;
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int g = 0; g < 8; ++g)
-      if (g < G) accr[g] *= arec[g];
-    const int qn = (n + FIN_PARTS - 1) / FIN_PARTS, tb = part * qn, te = min(n, tb + qn);
-    const int64_t vb = b * p.r_sb + h * p.r_sh + d;
-    if (bf && qn <= 32) {  // the whole quarter in flight at once
-      float v[32];
-#pragma unroll
-      for (int u = 0; u < 32; ++u)
-        v[u] = tb + u < te ? __bfloat162float(static_cast<const __nv_bfloat16*>(p.rv)[vb + int64_t(t0 + tb + u) * p.r_st]) : 0.f;
-#pragma unroll
-      for (int u = 0; u < 32; ++u)
-        if (tb + u < te) {
-#pragma unroll
-          for (int g = 0; g < 8; ++g)
-            if (g < G) accr[g] = fmaf(sc[g][tb + u], v[u], accr[g]);
-        }
-    } else {
-      for (int t = tb; t < te; ++t) {
-        const float v = load_elem(p.rv, p.r_dtype, vb + int64_t(t0 + t) * p.r_st);
-#pragma unroll
-        for (int g = 0; g < 8; ++g)
-          if (g < G) accr[g] = fmaf(sc[g][t], v, accr[g]);
-      }
-    }
-    __syncthreads();
-  }
-  // combine the token quarters: half_acc[0][g][d] ends with the window sum of every head
-#pragma unroll
-  for (int g = 0; g < 8; ++g)
-    if (g < G) half_acc[part][g][d] = accr[g];
-  __syncthreads();
-  if (part == 0) {
-#pragma unroll
-    for (int g = 0; g < 8; ++g)
-      if (g < G) half_acc[0][g][d] = (half_acc[0][g][d] + half_acc[1][g][d]) + (half_acc[2][g][d] + half_acc[3][g][d]);
-  }
-  __syncthreads();
-  const int64_t per = p.plan[p.n_seg + 1];
-  const int slot_f = G * (D + 2);
-  const int s = pair * 2;
-  const int nh = seg_tokens(p, s);
-  const int64_t S = p.plan[s];
-  const int c0 = int(S / per);
-  const int c1 = nh ? int((S + int64_t(nh - 1)) / per) : c0 - 1;
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const int idx = threadIdx.x + k * FIN_THREADS;
-    if (idx >= G * D) continue;
-    const int g = idx / D, d = idx % D;
-    float M = W ? mrec[g] : -INFINITY;
-    for (int c = c0; c <= c1; ++c) M = fmaxf(M, p.slots[int64_t(c + s) * slot_f + G * D + g * 2]);
-    float L = 0.f, ah = 0.f, ar = 0.f;
-    if (W) {
-      const float f = expf(mrec[g] - M);
-      ar = half_acc[0][g][d] * f;
-      L = lrec[g] * f;
-    }
-    for (int c = c0; c <= c1; ++c) {
-      const float* sl = p.slots + int64_t(c + s) * slot_f;
-      const float f = expf(sl[G * D + g * 2] - M);
-      ah += sl[g * D + d] * f;
-      L += sl[G * D + g * 2 + 1] * f;
-    }
-    const int hq = h * G + g;
-    if (partial_out) {
-      float* po = partial_out + (int64_t(b) * p.Hq + hq) * (2 * D + 2);
-      po[d] = ah;
-      po[D + d] = ar;
-      if (d == 0) {
-        po[2 * D] = M;
-        po[2 * D + 1] = L;
-      }
-    }
-    if (out) {
-      float oh = 0.f, orr = 0.f;
-      if (L > 0.f) {
-        oh = ah / L;
-        orr = ar / L;
-      }
-      const float o = round_dtype(round_dtype(oh, p.q_dtype) + round_dtype(orr, p.q_dtype), p.q_dtype);
-      store_elem(out, p.q_dtype, b * o_sb + hq * o_sh + d, o);
-    }
-  }
-}
-
-// R partial sets [R][B][Hq][2D+2] -> output
 __global__ void merge_partials_kernel(const float* __restrict__ parts, int R, int B, int Hq, int D,
                                       void* out, int out_dtype, int64_t o_sb, int64_t o_sh) {
   const int bh = blockIdx.x;
@@ -675,7 +497,6 @@ extern "C" int smaq_decode(const smaq_decode_args* args, void* stream) {
   p.n_seg = 2 * a.batch * a.n_kv_heads;
   p.layout = a.layout;
   p.cent16 = a.key_format == SMAQ_KEYS_BVQ ? static_cast<const uint16_t*>(a.centroids_f16) : nullptr;
-  p.recent_in_merge = 0;  // every kernel attends the exact window itself
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int grid = 0;
   int st = dispatch_decode(p, kb, a.value_bits, a.num_ctas, s, &grid, true);
@@ -707,11 +528,6 @@ extern "C" int smaq_decode(const smaq_decode_args* args, void* stream) {
   if (st) return st;
   st = dispatch_decode(p, kb, a.value_bits, grid, s, &grid, false);
   if (st) return st;
-  if (p.recent_in_merge) {
-    decode_finish_kernel<<<a.batch * a.n_kv_heads, FIN_THREADS, 0, s>>>(p, a.out, a.o_stride_b, a.o_stride_h,
-                                                                        a.partial_out);
-    return cuda_status(cudaGetLastError(), "decode_finish_kernel");
-  }
   decode_merge_kernel<<<a.batch * a.n_kv_heads, 256, 0, s>>>(p, a.out, a.o_stride_b, a.o_stride_h, a.partial_out);
   return cuda_status(cudaGetLastError(), "decode_merge_kernel");
 }

@@ -42,7 +42,6 @@ struct DecodeParams {
   int grid;
   int layout;
   const uint16_t* cent16;  // bvq: fp16 copy of the decoded centroids (exact), or null
-  int recent_in_merge;     // 1: the exact window is attended by the merge kernel, not the main one
   // single-launch mode of the tensor-core kernel: the partition is computed in every CTA and
   // the last CTA to finish a (sequence, kv head) pair merges its slots into the outputs
   int fused;
@@ -59,7 +58,7 @@ __device__ __forceinline__ int seg_tokens(const DecodeParams& p, int s) {
     const int tot = p.hist_total ? p.hist_total[b] : p.hist_len[b];
     return tot >= p.min_hist ? p.hist_len[b] : 0;
   }
-  return (p.recent_len && !p.recent_in_merge) ? p.recent_len[b] : 0;
+  return p.recent_len ? p.recent_len[b] : 0;
 }
 __device__ __forceinline__ int seg_cost(int s) { return (s & 1) ? RECENT_COST : 1; }
 // Segment cost padded to a multiple of 16 units so that every CTA slice and every history
