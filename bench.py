@@ -56,6 +56,7 @@ def parse():
     ap.add_argument("--hkv", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="decode", choices=["decode", "append", "longctx", "paged"])
+    ap.add_argument("--paged-layers", type=int, default=28, help="layers of the paged workload (profiling only)")
     return ap.parse_args()
 
 
@@ -539,6 +540,7 @@ def run_paged(a, rank: int, world: int):
     dev = torch.device("cuda", local)
     D = 128
     lens = paged_lengths()
+    n_layers = a.paged_layers
     quant = SMAQQuantizer(D, bits=PG_BITS, device=dev)
     quant.fit(torch.from_numpy(syn.calibration_queries(512, D)).to(dev))
     U_np, outl = syn.basis(D)
@@ -550,7 +552,7 @@ def run_paged(a, rank: int, world: int):
     rng = np.random.default_rng(40 + rank)
     bf = torch.bfloat16
     layers = []
-    for li in range(PG_LAYERS):
+    for li in range(n_layers):
         gen = torch.Generator(device=dev).manual_seed(1000 * (rank + 1) + li)
         perm = rng.permutation(n_pages)
         bt = np.zeros((PG_B, maxp), np.int32)
@@ -634,18 +636,20 @@ def run_paged(a, rank: int, world: int):
         peak = float(json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))["hbm_gbs"])
     except Exception:
         peak = 6650.0
-    achieved = bpl * PG_LAYERS / (ms * 1e-3) / 1e9
-    line = {"metric": METRIC, "value": PG_B / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": a.steps,
-            "warmup": max(3, a.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+    achieved = bpl * n_layers / (ms * 1e-3) / 1e9
+    # tokens/s of a full 28-layer step (ms scaled when fewer layers were built for profiling)
+    ms_full = ms * PG_LAYERS / n_layers
+    line = {"metric": METRIC, "value": PG_B / (ms_full * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": a.steps,
+            "warmup": max(3, a.warmup), "ms_per_step": ms_full, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32-accum/bf16-io", "data": "synthetic", "config": paged_config(),
             "hbm_gbs": achieved,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": None, "kernel": "smaq_decode (scalar keys, paged) per step",
                          "algorithmic_bytes_per_launch": bpl},
-            "e2e": {"value": PG_B / (e2e_ms * 1e-3), "unit": "tokens/s",
+            "e2e": {"value": PG_B / (e2e_ms * PG_LAYERS / n_layers * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in hq),
                     "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in ho)},
-            "gpu_launches": PG_LAYERS * a.steps, "clocks": ck}
+            "gpu_launches": n_layers * a.steps, "clocks": ck}
     if not a.no_cpu_baseline:
         line["cpu_baseline"] = paged_cpu_sample()
     if rank == 0:
@@ -797,11 +801,11 @@ def main():
             "hbm_gbs": world * bpl * a.layers / (ms * 1e-3) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s",
                          "frac": achieved / peak_gbs, "traffic": traffic, "peak_source": peak_src,
-                         "kernel": "smaq_decode (plan+decode+merge) per layer",
+                         "kernel": "smaq_decode per layer (one decode_v3_kernel launch)",
                          "algorithmic_bytes_per_launch": bpl},
             "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "gpu_launches": 3 * a.layers * a.steps,
+            "gpu_launches": a.layers * a.steps,
             "clocks": ck,
         }
         if world == 1 and not a.no_cpu_baseline:
