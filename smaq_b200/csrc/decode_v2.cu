@@ -317,13 +317,17 @@ __device__ __forceinline__ void v3_chunk_lut(uint32_t st, uint32_t szs, uint32_t
   if (X.swp4) { const uint32_t a = n0, b = n2; n0 = n1; n1 = a; n2 = n3; n3 = b; }
   const uint32_t r[4] = {__byte_perm(n0, 0, X.sel), __byte_perm(n1, 0, X.sel), __byte_perm(n2, 0, X.sel),
                          __byte_perm(n3, 0, X.sel)};
-  float s[4] = {0.f, 0.f, 0.f, 0.f};
+  // heads (0, 1) and (2, 3) accumulate as packed fp32 pairs (one add.f32x2 per pair)
+  uint64_t s01 = 0ull, s23 = 0ull;
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     const uint32_t c256 = __byte_perm(r[j >> 2], 0, 0x4404 | ((j & 3) << 4));  // code * 256
-    const float4 e = *reinterpret_cast<const float4*>(sm + (c256 | (X.xl ^ uint32_t(j << 4))));
-    s[0] += e.x; s[1] += e.y; s[2] += e.z; s[3] += e.w;
+    const ulonglong2 e = *reinterpret_cast<const ulonglong2*>(sm + (c256 | (X.xl ^ uint32_t(j << 4))));
+    asm("add.rn.f32x2 %0, %0, %1;" : "+l"(s01) : "l"(e.x));
+    asm("add.rn.f32x2 %0, %0, %1;" : "+l"(s23) : "l"(e.y));
   }
+  float s[4] = {__uint_as_float(uint32_t(s01)), __uint_as_float(uint32_t(s01 >> 32)),
+                __uint_as_float(uint32_t(s23)), __uint_as_float(uint32_t(s23 >> 32))};
   if (!FULL && lane >= nv) s[0] = s[1] = s[2] = s[3] = -INFINITY;
   // ---- softmax: p = exp2(s - mref); the reference maximum only moves up
   const bool grow = (s[0] > mref[0]) | (s[1] > mref[1]) | (s[2] > mref[2]) | (s[3] > mref[3]);
