@@ -205,6 +205,20 @@ int smaq_merge_partials(const float* partials, int n_parts, int batch, int n_q_h
                         void* out, int out_dtype, int64_t o_stride_b, int64_t o_stride_h,
                         void* stream);
 
+/* Failure detection.  Every device-side wait (mbarrier, cross-CTA counter) polls a bounded
+ * number of times; one that runs out records an error word and the kernel returns instead of
+ * hanging, so the context stays usable.  These calls synchronise `stream` and read that word.
+ *   smaq_decode_status: the word of the smaq_decode call that used `workspace` for a
+ *     (batch, n_kv_heads) shape (NULL = the smaq_decode_noalloc scratch of the current device).
+ *   smaq_append_status: the key kernel's word; reading clears it.
+ * Both return SMAQ_OK, or SMAQ_ERR_DEVICE with a message for smaq_last_error().
+ *   smaq_selftest_wait_timeout: launches one warp that waits on an mbarrier nothing arrives at,
+ *     polling `spin_limit` times, and returns SMAQ_ERR_DEVICE once the wait has run out and the
+ *     kernel has returned (the failure path, exercised without any device fault). */
+int smaq_decode_status(const void* workspace, int batch, int n_kv_heads, void* stream);
+int smaq_append_status(void* stream);
+int smaq_selftest_wait_timeout(unsigned int spin_limit, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

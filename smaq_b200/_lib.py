@@ -22,6 +22,7 @@ EXPORTS = (
     "smaq_abi_version", "smaq_last_error", "smaq_append", "smaq_quantize_keys_scalar",
     "smaq_quantize_values", "smaq_quantize_keys_bvq", "smaq_decode_workspace_size", "smaq_decode",
     "smaq_merge_partials", "smaq_decode_noalloc", "smaq_decode_noalloc_max_workspace",
+    "smaq_decode_status", "smaq_append_status", "smaq_selftest_wait_timeout",
 )
 
 vp = C.c_void_p
@@ -89,6 +90,12 @@ def load() -> C.CDLL:
     lib.smaq_decode_noalloc.argtypes = [C.POINTER(DecodeArgs), vp]
     lib.smaq_decode_noalloc.restype = i32
     lib.smaq_decode_noalloc_max_workspace.restype = C.c_size_t
+    lib.smaq_decode_status.argtypes = [vp, i32, i32, vp]
+    lib.smaq_decode_status.restype = i32
+    lib.smaq_append_status.argtypes = [vp]
+    lib.smaq_append_status.restype = i32
+    lib.smaq_selftest_wait_timeout.argtypes = [C.c_uint, vp]
+    lib.smaq_selftest_wait_timeout.restype = i32
     _lib = lib
     return lib
 

@@ -21,6 +21,7 @@
 
 #include "common.cuh"
 #include "decode_common.cuh"
+#include "ptx.cuh"
 
 namespace smaq {
 
@@ -540,4 +541,58 @@ extern "C" int smaq_merge_partials(const float* partials, int n_parts, int batch
   merge_partials_kernel<<<batch * n_q_heads, 128, 0, static_cast<cudaStream_t>(stream)>>>(
       partials, n_parts, batch, n_q_heads, head_dim, out, out_dtype, o_stride_b, o_stride_h);
   return cuda_status(cudaGetLastError(), "merge_partials_kernel");
+}
+
+// ---------------------------------------------------------------- device status
+namespace smaq {
+__global__ void selftest_wait_kernel(uint32_t limit, int* status) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);  // one arrival expected, none ever comes
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const bool done = mbar_wait(&bar, 0, limit);
+  if (threadIdx.x == 0) *status = done ? 0 : 1;
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_arrive_expect_tx(&bar, 0);  // complete the phase before the CTA exits
+}
+__device__ int g_selftest_status;
+}  // namespace smaq
+
+int smaq_noalloc_scratch(void** out);  // decode_noalloc.cu
+
+extern "C" int smaq_decode_status(const void* workspace, int batch, int n_kv_heads, void* stream) {
+  if (batch <= 0 || n_kv_heads <= 0) return smaq::fail(SMAQ_ERR_INVALID, "decode status: bad sizes");
+  const int n_seg = 2 * batch * n_kv_heads;
+  const void* ws = workspace;
+  if (!ws) {  // the no-allocation entry point's scratch on the current device
+    void* p = nullptr;
+    const int st = smaq_noalloc_scratch(&p);
+    if (st) return st;
+    ws = p;
+  }
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return smaq::cuda_status(e, "decode status: stream");
+  int word = 0;
+  e = cudaMemcpy(&word, static_cast<const int64_t*>(ws) + n_seg + 2, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return smaq::cuda_status(e, "decode status: read");
+  if (word) return smaq::fail(SMAQ_ERR_DEVICE, "decode: a bounded device wait ran out (stream data never arrived)");
+  return SMAQ_OK;
+}
+
+extern "C" int smaq_selftest_wait_timeout(unsigned int spin_limit, void* stream) {
+  int* st = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&st), smaq::g_selftest_status);
+  if (e != cudaSuccess) return smaq::cuda_status(e, "selftest: symbol");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  smaq::selftest_wait_kernel<<<1, 32, 0, s>>>(spin_limit, st);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return smaq::cuda_status(e, "selftest: kernel");
+  int word = -1;
+  e = cudaMemcpy(&word, st, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return smaq::cuda_status(e, "selftest: read");
+  if (word) return smaq::fail(SMAQ_ERR_DEVICE, "selftest: the wait ran out after %u polls and returned", spin_limit);
+  return SMAQ_OK;
 }

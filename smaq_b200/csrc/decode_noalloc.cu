@@ -38,6 +38,9 @@ int scratch_address(void** out) {
 
 extern "C" size_t smaq_decode_noalloc_max_workspace(void) { return kNoAllocScratchBytes; }
 
+// Scratch address of the current device (used by smaq_decode_status for no-allocation calls).
+int smaq_noalloc_scratch(void** out) { return scratch_address(out); }
+
 extern "C" int smaq_decode_noalloc(const smaq_decode_args* args, void* stream) {
   if (!args) return smaq::fail(SMAQ_ERR_INVALID, "smaq_decode_noalloc: null args");
   const size_t need = smaq_decode_workspace_size(args->batch, args->n_q_heads, args->n_kv_heads,

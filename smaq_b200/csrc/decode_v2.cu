@@ -691,6 +691,9 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
   if (threadIdx.x == 0) atomicAdd(&g_v3_prof[15], 1ull);
 #endif
   if (p.fused) {
+    // device error word: cleared by CTA 0 at start; a bounded wait that runs out (seconds later)
+    // sets it, and smaq_decode_status reports it
+    if (blockIdx.x == 0 && threadIdx.x == 0) *reinterpret_cast<volatile int*>(p.plan + p.n_seg + 2) = 0;
     v3_plan(p, splan, splan + C::MAX_FUSED_SEG + 4, sntab);
     plan = splan;
     ntab = sntab;
@@ -1222,6 +1225,9 @@ __global__ void __launch_bounds__(SCfg::THREADS, 1) decode_s_kernel(DecodeParams
   const int64_t* plan = p.plan;
   const int* ntab = nullptr;
   if (p.fused) {
+    // device error word: cleared by CTA 0 at start; a bounded wait that runs out (seconds later)
+    // sets it, and smaq_decode_status reports it
+    if (blockIdx.x == 0 && threadIdx.x == 0) *reinterpret_cast<volatile int*>(p.plan + p.n_seg + 2) = 0;
     v3_plan(p, splan, splan + C::MAX_FUSED_SEG + 4, sntab);
     plan = splan;
     ntab = sntab;

@@ -570,3 +570,14 @@ int launch_scalar_keys_tc(const smaq_append_args& a, cudaStream_t s) {
 }
 
 }  // namespace smaq
+
+extern "C" int smaq_append_status(void* stream) {
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return smaq::cuda_status(e, "append status: stream");
+  unsigned int word = 0, zero = 0;
+  e = cudaMemcpyFromSymbol(&word, smaq::g_tc_rotate_fault, sizeof(word));
+  if (e == cudaSuccess && word) e = cudaMemcpyToSymbol(smaq::g_tc_rotate_fault, &zero, sizeof(zero));
+  if (e != cudaSuccess) return smaq::cuda_status(e, "append status: read");
+  if (word) return smaq::fail(SMAQ_ERR_DEVICE, "append: a bounded device wait in the key kernel ran out");
+  return SMAQ_OK;
+}

@@ -17,10 +17,16 @@ contexts.  Units of work are (sequence, KV head) pairs, which are independent.
   the kernel receives as ``hist_total``.
 
 Rank ``r`` of a plan sits at head group ``r // seq_splits`` and split ``r % seq_splits``.
+
+Failure handling: the exchange is the only point where a rank waits on another.  Give
+``split_groups`` a ``timeout``; a peer that died or never reaches the exchange then ends the
+all-gather with an error, which ``sharded_decode`` re-raises as ``PeerFailure`` naming the
+split group, between decode steps and with no kernel of this rank in flight.
 """
 
 from __future__ import annotations
 
+import datetime
 import math
 from dataclasses import dataclass
 from typing import Callable, Optional, Sequence
@@ -28,6 +34,10 @@ from typing import Callable, Optional, Sequence
 import torch
 
 PARTIAL_EXTRA = 2  # (m, l) after acc_hist[D] and acc_recent[D]
+
+
+class PeerFailure(RuntimeError):
+    """A rank of this rank's split group failed to join the partials exchange."""
 
 
 @dataclass(frozen=True)
@@ -81,14 +91,16 @@ def make_plan(world: int, n_kv_heads: int) -> ShardPlan:
     return ShardPlan(world, n_kv_heads, hg, world // hg)
 
 
-def split_groups(plan: ShardPlan, backend: Optional[str] = None):
+def split_groups(plan: ShardPlan, backend: Optional[str] = None, timeout: Optional[float] = None):
     """One process group per head group, over its sequence-split ranks (``None`` entries when
-    there is no split).  Every rank must call this, in the same order."""
+    there is no split).  Every rank must call this, in the same order.  ``timeout`` (seconds)
+    bounds each exchange: a peer that does not arrive within it fails the collective."""
     import torch.distributed as dist
+    kw = {} if timeout is None else {"timeout": datetime.timedelta(seconds=timeout)}
     groups = []
     for hg in range(plan.head_groups):
         ranks = [hg * plan.seq_splits + s for s in range(plan.seq_splits)]
-        groups.append(dist.new_group(ranks, backend=backend) if plan.seq_splits > 1 else None)
+        groups.append(dist.new_group(ranks, backend=backend, **kw) if plan.seq_splits > 1 else None)
     return groups
 
 
@@ -121,5 +133,8 @@ def sharded_decode(plan: ShardPlan, rank: int, groups: Sequence, decode_fn: Call
     if plan.seq_splits == 1:
         return decode_fn(partial=False)
     part = decode_fn(partial=True)
-    gathered = gather_partials(part, groups[hg], plan.seq_splits)
+    try:
+        gathered = gather_partials(part, groups[hg], plan.seq_splits)
+    except Exception as e:  # the backend's timeout / closed-connection error
+        raise PeerFailure(f"rank {rank}: partials exchange with ranks {plan.split_peers(rank)} failed: {e}") from e
     return combine(gathered, out_dtype, merge_fn)

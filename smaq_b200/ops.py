@@ -285,6 +285,26 @@ def merge_partials(partials: torch.Tensor, out_dtype: torch.dtype) -> torch.Tens
     return out
 
 
+# --------------------------------------------------------------------- failure detection
+def decode_status(batch: int, n_kv_heads: int, workspace: Optional[torch.Tensor] = None) -> None:
+    """Raise if a bounded device wait of the last ``decode`` that used ``workspace`` (``None``:
+    the no-allocation scratch) ran out.  Synchronises the current stream."""
+    lib = _lib.load()
+    _lib.check(lib.smaq_decode_status(None if workspace is None else workspace.data_ptr(), batch, n_kv_heads,
+                                      _stream()), "smaq_decode_status")
+
+
+def append_status() -> None:
+    """Raise if a bounded device wait of the key kernel ran out since the last check (clears it)."""
+    _lib.check(_lib.load().smaq_append_status(_stream()), "smaq_append_status")
+
+
+def selftest_wait_timeout(spin_limit: int = 1 << 12) -> int:
+    """Run a kernel whose mbarrier wait can never complete with a ``spin_limit`` poll bound;
+    returns the library status (``5`` = SMAQ_ERR_DEVICE when the timeout path works)."""
+    return int(_lib.load().smaq_selftest_wait_timeout(spin_limit, _stream()))
+
+
 # --------------------------------------------------------------------- decode-layout byte order
 # (SMAQ_LAYOUT_DECODE, include/smaq_b200.h): same bits as the reference, permuted inside rows.
 _VPERM = [4 * (k % 8) + k // 8 for k in range(32)]          # reference byte k lives at _VPERM[k]

@@ -47,3 +47,10 @@ def test_cpu_tensors_raise():
     from smaq_b200 import ops
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         ops.quantize_values(torch.zeros(4, 128))
+
+
+def test_status_calls_validate_without_a_gpu():
+    from smaq_b200 import _lib
+    lib = _lib.load()
+    assert lib.smaq_decode_status(None, 0, 2, None) == 1
+    assert b"bad sizes" in lib.smaq_last_error()

@@ -104,3 +104,55 @@ def test_sharded_decode_matches_reference_gloo(tmp_path, world, Hkv, G):
     for r in range(world):
         w = float(open(f"{res}.{r}").read())
         assert w <= 2e-3, (r, w)
+
+
+def _failure_worker(rank, world, port, mode, result_path):
+    """Rank 1 fails on the host before the partials exchange (``exit``: the process ends;
+    ``stall``: it stays alive but never joins); rank 0 must get a PeerFailure within the
+    split group's timeout instead of waiting forever."""
+    import time
+    import torch
+    import torch.distributed as dist
+    from smaq_b200 import distributed as sd
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    plan = sd.make_plan(world, 1)
+    groups = sd.split_groups(plan, timeout=3.0)
+    if rank == 1:
+        if mode == "exit":
+            os._exit(0)
+        time.sleep(20.0)
+        os._exit(0)
+    t0 = time.monotonic()
+    outcome = "completed"
+    try:
+        sd.sharded_decode(plan, rank, groups, lambda partial: torch.zeros((1, 4, 2 * D + 2)), torch.float32,
+                          lambda parts, dt: parts[0, :, :, :D])
+    except sd.PeerFailure as e:
+        outcome = "PeerFailure:" + str(e).splitlines()[0][:200]
+    with open(result_path, "w") as fh:
+        fh.write(f"{time.monotonic() - t0:.3f}\n{outcome}\n")
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["exit", "stall"])
+def test_peer_failure_is_detected_gloo(tmp_path, mode):
+    import torch.multiprocessing as mp
+    port = 31000 + (os.getpid() % 1000) + (0 if mode == "exit" else 3)
+    res = str(tmp_path / "outcome")
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_failure_worker, args=(r, 2, port, mode, res)) for r in range(2)]
+    for p in procs:
+        p.start()
+    procs[0].join(60)
+    alive = procs[0].is_alive()
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+        p.join(5)
+    assert not alive, "rank 0 hung in the exchange"
+    elapsed, outcome = open(res).read().splitlines()
+    assert outcome.startswith("PeerFailure:"), outcome
+    assert "ranks [0, 1]" in outcome
+    assert float(elapsed) < 30.0

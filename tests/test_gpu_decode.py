@@ -71,7 +71,8 @@ def build_paged(dev, kind, bits, B, Hkv, hist, page_size, dtype, seed):
     return st, raw
 
 
-def run_case(cuda, kind, bits, B, Hkv, G, hist, recent, page_size, dtype, seed, num_ctas=0, layout=0):
+def run_case(cuda, kind, bits, B, Hkv, G, hist, recent, page_size, dtype, seed, num_ctas=0, layout=0,
+             entry="smaq_decode"):
     import torch
     from smaq_b200 import ops
     from smaq_b200._lib import SMAQ_KEYS_BVQ, SMAQ_KEYS_SCALAR
@@ -105,7 +106,7 @@ def run_case(cuda, kind, bits, B, Hkv, G, hist, recent, page_size, dtype, seed, 
         assert kw["centroids_f16"] is not None
     out = ops.decode(q, n_kv_heads=Hkv, key_codes=st["codes"], v_data=st["vdata"], v_scales=st["vs"],
                      v_zeros=st["vz"], hist_len=hl, page_size=page_size, block_table=st["bt"],
-                     recent_k=rk, recent_v=rv, recent_len=rl, num_ctas=num_ctas, layout=layout, **kw)
+                     recent_k=rk, recent_v=rv, recent_len=rl, num_ctas=num_ctas, layout=layout, entry=entry, **kw)
     got = tn(out)
     # oracle per sequence, from the GPU-written rows (isolates decode from quantize parity)
     codes_t, vdata_t = st["codes"], st["vdata"]
