@@ -55,6 +55,10 @@ def parse():
     ap.add_argument("--hq", type=int, default=32)
     ap.add_argument("--hkv", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ctas", type=int, default=0, help="decode grid size (0: one CTA per SM)")
+    ap.add_argument("--no-overlap", dest="overlap", action="store_false",
+                    help="plain stream ordering between layer launches (default: each layer's launch overlaps "
+                         "the previous one's end; no layer writes another layer's history rows or the lengths)")
     ap.add_argument("--workload", default="decode", choices=["decode", "append", "longctx", "paged"])
     ap.add_argument("--paged-layers", type=int, default=28, help="layers of the paged workload (profiling only)")
     return ap.parse_args()
@@ -201,7 +205,22 @@ def decode_layer(a, L, vq, hl, rl, ws, q=None, out=None):
                       centroids=vq.decoded_centroids, key_codes=L["codes"], v_data=L["vdata"], v_scales=L["vs"],
                       v_zeros=L["vz"], hist_len=hl, page_size=a.ctx, recent_k=L["rk"], recent_v=L["rv"],
                       recent_len=rl, out=L["out"] if out is None else out, workspace=ws, layout=SMAQ_LAYOUT_DECODE,
-                      centroids_f16=vq.cb16)
+                      centroids_f16=vq.cb16, num_ctas=getattr(a, "ctas", 0), overlap_prior=getattr(a, "overlap", False))
+
+
+def stack_io(layers):
+    """Put every layer's query rows in one device buffer and its outputs in another (each layer
+    keeps views), with pinned host mirrors, so an end-to-end step moves all queries host->device
+    in one copy and all outputs device->host in one copy."""
+    import torch
+    Q = torch.stack([L["q"] for L in layers])
+    O = torch.stack([L["out"] for L in layers])
+    for i, L in enumerate(layers):
+        L["q"], L["out"] = Q[i], O[i]
+    hQ = torch.empty_like(Q, device="cpu").pin_memory()
+    hQ.copy_(Q.cpu())
+    hO = torch.empty_like(O, device="cpu").pin_memory()
+    return Q, O, hQ, hO
 
 
 # ----------------------------------------------------------------------------- CPU baseline
@@ -611,17 +630,12 @@ def run_paged(a, rank: int, world: int):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / a.steps
     ck = clocks.stop()
-    hq = [torch.empty_like(L["q"], device="cpu").pin_memory() for L in layers]
-    for h, L in zip(hq, layers):
-        h.copy_(L["q"].cpu())
-    ho = [torch.empty_like(L["out"], device="cpu").pin_memory() for L in layers]
-    dq = [torch.empty_like(L["q"]) for L in layers]
+    Q, O, hQ, hO = stack_io(layers)
 
     def e2e_step():
-        for i, L in enumerate(layers):
-            dq[i].copy_(hq[i], non_blocking=True)
-            dec(L, dq[i])
-            ho[i].copy_(L["out"], non_blocking=True)
+        Q.copy_(hQ, non_blocking=True)
+        step()
+        hO.copy_(O, non_blocking=True)
 
     e2e_step()
     torch.cuda.synchronize()
@@ -647,8 +661,8 @@ def run_paged(a, rank: int, world: int):
                          "traffic": None, "kernel": "smaq_decode (scalar keys, paged) per step",
                          "algorithmic_bytes_per_launch": bpl},
             "e2e": {"value": PG_B / (e2e_ms * PG_LAYERS / n_layers * 1e-3), "unit": "tokens/s",
-                    "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in hq),
-                    "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in ho)},
+                    "h2d_bytes_per_step": hQ.numel() * hQ.element_size(),
+                    "d2h_bytes_per_step": hO.numel() * hO.element_size()},
             "gpu_launches": n_layers * a.steps, "clocks": ck}
     if not a.no_cpu_baseline:
         line["cpu_baseline"] = paged_cpu_sample()
@@ -712,7 +726,7 @@ def main():
     hl = torch.full((a.batch,), a.ctx, dtype=torch.int32, device=dev)
     rl = torch.full((a.batch,), a.window, dtype=torch.int32, device=dev)
     from smaq_b200 import ops
-    ws = torch.empty(ops.decode_workspace_bytes(a.batch, a.hq, a.hkv, 128), dtype=torch.uint8, device=dev)
+    ws = torch.empty(ops.decode_workspace_bytes(a.batch, a.hq, a.hkv, 128, a.ctas), dtype=torch.uint8, device=dev)
 
     def step():
         for L in layers:
@@ -749,17 +763,12 @@ def main():
         torch.cuda.synchronize()
     layer_ms = statistics.mean(s0.elapsed_time(s1) for s0, s1 in evs)
     # end to end through the public API with host buffers: H2D queries, decode, D2H outputs
-    hq = [torch.empty_like(L["q"], device="cpu").pin_memory() for L in layers]
-    for h, L in zip(hq, layers):
-        h.copy_(L["q"].cpu())
-    ho = [torch.empty_like(L["out"], device="cpu").pin_memory() for L in layers]
-    dq = [torch.empty_like(L["q"]) for L in layers]
+    Q, O, hQ, hO = stack_io(layers)
 
     def e2e_step():
-        for i, L in enumerate(layers):
-            dq[i].copy_(hq[i], non_blocking=True)
-            decode_layer(a, L, vq, hl, rl, ws, q=dq[i])
-            ho[i].copy_(L["out"], non_blocking=True)
+        Q.copy_(hQ, non_blocking=True)
+        step()
+        hO.copy_(O, non_blocking=True)
 
     for _ in range(2):
         e2e_step()
@@ -788,8 +797,8 @@ def main():
     # DRAM bytes per launch from one ncu capture of this workload (profiles/decode_bvq_cfg1_kernel.md)
     default_shape = (a.batch, a.ctx, a.window, a.hq, a.hkv) == (16, 32768, 128, 32, 8)
     traffic = 284.2e6 if default_shape else None
-    h2d = sum(t.numel() * t.element_size() for t in hq)
-    d2h = sum(t.numel() * t.element_size() for t in ho)
+    h2d = hQ.numel() * hQ.element_size()
+    d2h = hO.numel() * hO.element_size()
     if rank == 0:
         strong = a.workload == "longctx"
         tokens = a.batch if strong else a.batch * world

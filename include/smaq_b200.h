@@ -54,7 +54,7 @@
 extern "C" {
 #endif
 
-#define SMAQ_ABI_VERSION 1
+#define SMAQ_ABI_VERSION 2
 
 /* element types */
 enum { SMAQ_F32 = 0, SMAQ_BF16 = 1, SMAQ_F16 = 2 };
@@ -179,6 +179,13 @@ typedef struct smaq_decode_args {
    * they equal `centroids` exactly (an fp16-valued codebook); with SMAQ_LAYOUT_DECODE rows,
    * bf16/fp16 queries, 2-bit values and group 32 this selects the tensor-core kernel. */
   const void* centroids_f16;
+  /* Nonzero: launch the single-launch kernels with programmatic dependent launch, so that their
+   * partition and first history copies overlap the end of the previous kernel on the stream.
+   * The caller promises that kernel writes none of: key_codes / key_norms / v_data / v_scales /
+   * v_zeros rows, block_table, hist_len, hist_total, recent_len.  Queries, the window, outputs
+   * and the workspace are read or written only after that kernel has completed.  Ignored by the
+   * multi-launch path.  Zero gives plain stream ordering. */
+  int overlap_prior;
 } smaq_decode_args;
 
 /* Bytes of workspace smaq_decode needs for these shapes (host-only computation). */

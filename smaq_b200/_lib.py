@@ -54,7 +54,7 @@ class DecodeArgs(C.Structure):
         ("r_stride_b", i64), ("r_stride_t", i64), ("r_stride_h", i64), ("recent_len", vp),
         ("out", vp), ("o_stride_b", i64), ("o_stride_h", i64), ("partial_out", vp),
         ("workspace", vp), ("workspace_bytes", C.c_size_t), ("num_ctas", i32), ("layout", i32),
-        ("centroids_f16", vp),
+        ("centroids_f16", vp), ("overlap_prior", i32),
     ]
 
 
@@ -66,11 +66,12 @@ def load() -> C.CDLL:
     global _lib
     if _lib is not None:
         return _lib
-    if not os.path.exists(LIB_PATH):
+    path = os.environ.get("SMAQ_B200_LIB", LIB_PATH)  # an alternate build of the same library
+    if not os.path.exists(path):
         raise RuntimeError(
-            f"smaq_b200 CUDA library not found at {LIB_PATH}; build it with "
+            f"smaq_b200 CUDA library not found at {path}; build it with "
             "`python -m smaq_b200.build` (there is no CPU fallback)")
-    lib = C.CDLL(LIB_PATH)
+    lib = C.CDLL(path)
     lib.smaq_abi_version.restype = i32
     lib.smaq_last_error.restype = C.c_char_p
     lib.smaq_append.argtypes = [C.POINTER(AppendArgs), vp]

@@ -517,6 +517,7 @@ extern "C" int smaq_decode(const smaq_decode_args* args, void* stream) {
     uint32_t e = ++epochs;
     if (e == 0) e = ++epochs;
     p.fused = 1;
+    p.pdl = a.overlap_prior ? 1 : 0;
     p.epoch = e;
     p.out = a.out;
     p.o_sb = a.o_stride_b;

@@ -45,6 +45,7 @@ struct DecodeParams {
   // single-launch mode of the tensor-core kernel: the partition is computed in every CTA and
   // the last CTA to finish a (sequence, kv head) pair merges its slots into the outputs
   int fused;
+  int pdl;  // overlapped launch (smaq_decode_args.overlap_prior, single-launch kernels only)
   uint32_t epoch;          // nonzero, different for consecutive calls (tags pair_cnt values)
   uint64_t* pair_cnt;      // [B * Hkv] (epoch << 32 | slots written), reset by the merging CTA
   void* out;

@@ -98,6 +98,21 @@ struct V3Src {
   uint32_t dst_off;     // offset of the stream inside a stage
 };
 
+// This lane's stream (lane & 3: indices, value codes, scales, zeros) of the history segment of
+// (sequence b, kv head h) that starts at token t0.
+__device__ __forceinline__ V3Src v3_src(const DecodeParams& p, int b, int h, int64_t t0) {
+  V3Src src;
+  const int k = threadIdx.x & 3;
+  const uint8_t* base = k == 0 ? p.kcodes
+                        : k == 1 ? p.vdata
+                        : k == 2 ? static_cast<const uint8_t*>(p.vscales)
+                                 : static_cast<const uint8_t*>(p.vzeros);
+  src.row_bytes = k == 0 ? 16u : k == 1 ? 32u : 8u;
+  src.dst_off = k == 0 ? uint32_t(ST_IDX) : k == 1 ? uint32_t(ST_V) : k == 2 ? uint32_t(ST_S) : uint32_t(ST_Z);
+  src.base = p.bt ? base : base + ((int64_t(b) * p.Hkv + h) * p.page_size + t0) * src.row_bytes;
+  return src;
+}
+
 // Lanes 0..3 each copy one stream of chunk `kc` (tokens t0 + 32kc ..) into `stage`; the
 // mbarrier was initialised with 4 arrivals.  Paged stores split the copy at page boundaries.
 __device__ __forceinline__ void v3_issue(const DecodeParams& p, const V3Src& src, int b, int h, int64_t t0,
@@ -688,15 +703,63 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
   const int* ntab = nullptr;
 #ifdef SMAQ_PROF
   long long prof_t = clock64();
+  const long long prof_t0 = prof_t;
   if (threadIdx.x == 0) atomicAdd(&g_v3_prof[15], 1ull);
 #endif
+  if (p.fused) {
+    // overlapped launch: the next launch on the stream may be scheduled now; its CTAs take an SM
+    // only when one of ours has exited
+    if (p.pdl) pdl_launch_dependents();
+    v3_plan(p, splan, splan + C::MAX_FUSED_SEG + 4, sntab);
+    plan = splan;
+    ntab = sntab;
+  }
+  const int64_t total = plan[p.n_seg];
+  const int64_t per = plan[p.n_seg + 1];
+  const int c = blockIdx.x;
+  const int64_t lo = int64_t(c) * per, hi = min(lo + per, total);
+  int sa = 0;
+  if (lo < hi) {
+    int sb_ = p.n_seg - 1;
+    while (sa < sb_) {
+      const int mid = (sa + sb_) >> 1;
+      if (plan[mid + 1] > lo) sb_ = mid; else sa = mid + 1;
+    }
+  }
+  // Overlapped launch: the first history chunks of this CTA are requested before waiting for
+  // the previous launch on the stream (the caller promises that launch writes neither the
+  // history rows nor the lengths); queries, the window, outputs and the workspace only after.
+  int pre_s = -1;
+  if (p.pdl) {
+    if (lo < hi) {
+      for (int s = sa; s < p.n_seg && plan[s] < hi; ++s) {
+        const int n = v3_ntok(p, ntab, s);
+        if (n == 0) continue;
+        int64_t t0 = (lo <= plan[s]) ? 0 : (lo - plan[s] + seg_cost(s) - 1) / seg_cost(s);
+        int64_t t1 = (hi - plan[s] + seg_cost(s) - 1) / seg_cost(s);
+        if (t1 > n) t1 = n;
+        if (t0 >= t1) continue;
+        if (!(s & 1)) {
+          const int pair = s >> 1, b = pair / p.Hkv, h = pair - b * p.Hkv;
+          const int ntok = int(t1 - t0), nchunks = (ntok + CH - 1) / CH;
+          const int mine = (wid < nchunks) ? (nchunks - 1 - wid) / WARPS + 1 : 0;
+          const V3Src src = v3_src(p, b, h, t0);
+          if (lane < 4)
+            for (int i = 0; i < ST && i < mine; ++i) {
+              const int kc = wid + WARPS * i;
+              v3_issue(p, src, b, h, t0, min(CH, ntok - kc * CH), kc, wreg + i * STAGE_BYTES, &wbar[i]);
+            }
+          pre_s = s;
+        }
+        break;
+      }
+    }
+    pdl_wait();
+  }
   if (p.fused) {
     // device error word: cleared by CTA 0 at start; a bounded wait that runs out (seconds later)
     // sets it, and smaq_decode_status reports it
     if (blockIdx.x == 0 && threadIdx.x == 0) *reinterpret_cast<volatile int*>(p.plan + p.n_seg + 2) = 0;
-    v3_plan(p, splan, splan + C::MAX_FUSED_SEG + 4, sntab);
-    plan = splan;
-    ntab = sntab;
     // pairs nobody attends (no usable history, no window): zero output, empty partials
     for (int pair = blockIdx.x; pair < p.B * p.Hkv; pair += gridDim.x) {
       int e = 0;
@@ -708,10 +771,6 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
       if (e == 0) v3_final_merge(p, plan, ntab, pair);
     }
   }
-  const int64_t total = plan[p.n_seg];
-  const int64_t per = plan[p.n_seg + 1];
-  const int c = blockIdx.x;
-  const int64_t lo = int64_t(c) * per, hi = min(lo + per, total);
   V3_PROF(0);
   if (lo >= hi) return;
 
@@ -735,11 +794,6 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
   const uint32_t ring_s = uint32_t(wreg - sm);
   __syncthreads();
 
-  int sa = 0, sb_ = p.n_seg - 1;
-  while (sa < sb_) {
-    const int mid = (sa + sb_) >> 1;
-    if (plan[mid + 1] > lo) sb_ = mid; else sa = mid + 1;
-  }
   // warm L2 with what this CTA reads outside its bulk-copied streams (the streams of the whole
   // step do not fit in L2, so these lines would otherwise come from HBM at full load latency):
   // the score-table codebook, and the exact window rows of its window segments
@@ -823,18 +877,8 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
     const int ntok = int(t1 - t0);
     const int nchunks = (ntok + CH - 1) / CH;
     const int mine = (wid < nchunks) ? (nchunks - 1 - wid) / WARPS + 1 : 0;
-    V3Src src;
-    {
-      const int k = lane & 3;
-      const uint8_t* base = k == 0 ? p.kcodes
-                            : k == 1 ? p.vdata
-                            : k == 2 ? static_cast<const uint8_t*>(p.vscales)
-                                     : static_cast<const uint8_t*>(p.vzeros);
-      src.row_bytes = k == 0 ? 16u : k == 1 ? 32u : 8u;
-      src.dst_off = k == 0 ? uint32_t(ST_IDX) : k == 1 ? uint32_t(ST_V) : k == 2 ? uint32_t(ST_S) : uint32_t(ST_Z);
-      src.base = p.bt ? base : base + ((int64_t(b) * p.Hkv + h) * p.page_size + t0) * src.row_bytes;
-    }
-    if (lane < 4) {
+    const V3Src src = v3_src(p, b, h, t0);
+    if (lane < 4 && s != pre_s) {  // (pre_s: already issued before the dependency wait)
       for (int i = 0; i < ST && i < mine; ++i) {
         const int kc = wid + WARPS * i;
         v3_issue(p, src, b, h, t0, min(CH, ntok - kc * CH), kc, wreg + i * STAGE_BYTES, &wbar[i]);
@@ -1010,6 +1054,13 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
     if (p.fused) v3_arrive(p, plan, ntab, s, arrive_flag);
     V3_PROF(6);
   }
+#ifdef SMAQ_PROF
+  if (threadIdx.x == 0) {  // whole-CTA time: sum (7) and maximum (14) over CTAs
+    const unsigned long long tot = (unsigned long long)(clock64() - prof_t0);
+    atomicAdd(&g_v3_prof[7], tot);
+    atomicMax(&g_v3_prof[14], tot);
+  }
+#endif
   if (failed && lane == 0) atomicExch(reinterpret_cast<int*>(p.plan + p.n_seg + 2), 1);
 }
 
@@ -1475,8 +1526,22 @@ static int launch_v3_t(DecodeParams& p, int grid_req, cudaStream_t s, int* grid_
   const int grid = grid_req > 0 ? grid_req : num_sms();
   *grid_out = grid;
   if (query_only) return SMAQ_OK;
-  kern<<<grid, V3Cfg<GM>::THREADS, sm, s>>>(p, p.cent16);
-  return cuda_status(cudaGetLastError(), "decode_v3_kernel");
+  if (!p.pdl) {
+    kern<<<grid, V3Cfg<GM>::THREADS, sm, s>>>(p, p.cent16);
+    return cuda_status(cudaGetLastError(), "decode_v3_kernel");
+  }
+  // programmatic dependent launch: may start while the previous kernel on `s` finishes
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(V3Cfg<GM>::THREADS);
+  cfg.dynamicSmemBytes = sm;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, p, p.cent16), "decode_v3_kernel (overlapped)");
 }
 
 int decode_v2_max_fused_segments() { return V3Cfg<4>::MAX_FUSED_SEG; }

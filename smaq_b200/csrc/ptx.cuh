@@ -57,6 +57,12 @@ __device__ __forceinline__ void l2_prefetch(const void* src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
+// Programmatic dependent launch (sm_90+): wait until the previous grid on the stream has
+// completed and its memory is visible; allow the next grid on the stream to be scheduled.
+// Both are no-ops for a launch without the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // D[16x8] += A[16x16] * B[16x8], fp16 inputs, fp32 accumulate.
 __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm(

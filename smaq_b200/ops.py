@@ -183,12 +183,16 @@ def decode(q: torch.Tensor, *, n_kv_heads: int, key_format: int, key_codes: torc
            scale: Optional[float] = None, min_history: int = MIN_HISTORY, out: Optional[torch.Tensor] = None,
            partial_out: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
            num_ctas: int = 0, want_out: bool = True, layout: int = SMAQ_LAYOUT_REFERENCE,
-           centroids_f16: Optional[torch.Tensor] = None, entry: str = "smaq_decode") -> Optional[torch.Tensor]:
+           centroids_f16: Optional[torch.Tensor] = None, entry: str = "smaq_decode",
+           overlap_prior: bool = False) -> Optional[torch.Tensor]:
     """Batched hybrid decode attention.
 
     ``q``: ``[B, Hq, D]``.  History streams are store rows ``[pages, Hkv, page_size, ...]``;
     ``recent_k/v``: ``[B, W, Hkv, D]`` (stride 0 on B allowed).  Returns ``out [B, Hq, D]`` in
     the query dtype (reference rounding), and/or fills ``partial_out [B, Hq, 2D+2]``.
+    ``overlap_prior``: overlap the launch with the end of the previous kernel on the stream
+    (programmatic dependent launch); only when that kernel writes none of the history rows,
+    block table or lengths (``smaq_decode_args.overlap_prior``).
     """
     _cuda(q, key_codes, v_data, hist_len, recent_k, block_table)
     lib = _lib.load()
@@ -259,6 +263,7 @@ def decode(q: torch.Tensor, *, n_kv_heads: int, key_format: int, key_codes: torc
         a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel()
     a.num_ctas = num_ctas
     a.layout = layout
+    a.overlap_prior = 1 if overlap_prior else 0
     if centroids_f16 is not None:
         c16 = centroids_f16.to(torch.float16).contiguous()
         keep.append(c16)

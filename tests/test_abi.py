@@ -20,7 +20,7 @@ def test_library_exports_header_symbols():
     missing = [s for s in decl if not hasattr(lib, s)]
     assert not missing, missing
     assert set(decl) == set(_lib.EXPORTS)
-    assert lib.smaq_abi_version() == 1
+    assert lib.smaq_abi_version() == 2
 
 
 def test_invalid_arguments_are_reported_without_a_gpu():

@@ -240,3 +240,45 @@ def test_scalar_decode_layout_bytes(cuda, bits):
             out[lay] = (codes, norms)
         assert torch.equal(ops.scalar_codes_to_reference(out[1][0]), out[0][0])
         assert torch.equal(out[1][1], out[0][1])
+
+
+def test_overlapped_launches_match_plain(cuda):
+    """overlap_prior (programmatic dependent launch): back-to-back launches sharing one workspace,
+    each right after a kernel that rewrites its queries, give exactly the plain launches' outputs."""
+    import torch
+    from smaq_b200 import ops
+    from smaq_b200._lib import SMAQ_KEYS_BVQ
+    B, Hkv, G, page_size = 5, 2, 4, 16
+    hist, recent = [1000, 15, 16, 333, 2048], [64, 3, 0, 128, 1]
+    st, raw = build_paged(cuda, "bvq", 0, B, Hkv, hist, page_size, "bfloat16", 41)
+    Eb, C, dec = random_codebook(cuda)
+    for k, v, slots in raw:
+        ops.append(k, v, n_heads=Hkv, slots=slots, page_size=page_size, key_format=SMAQ_KEYS_BVQ,
+                   E_blocks=Eb, centroids=C, key_codes=st["codes"], v_data=st["vdata"], v_scales=st["vs"],
+                   v_zeros=st["vz"], layout=1)
+    c16 = ops.fp16_codebook(dec)
+    bf = torch.bfloat16
+    rk = torch.from_numpy(syn.keys((B, 128, Hkv), D, seed=42)).to(cuda).to(bf)
+    rv = torch.from_numpy(syn.values((B, 128, Hkv), D, seed=43)).to(cuda).to(bf)
+    hl = torch.tensor(hist, dtype=torch.int32, device=cuda)
+    rl = torch.tensor(recent, dtype=torch.int32, device=cuda)
+    n = 6
+    src = [torch.from_numpy(syn.queries((B, Hkv * G), D, seed=50 + i)).to(cuda).to(bf) for i in range(n)]
+    ws = torch.empty(ops.decode_workspace_bytes(B, Hkv * G, Hkv, D), dtype=torch.uint8, device=cuda)
+
+    def run(overlap):
+        q = torch.zeros_like(src[0])
+        outs = []
+        for i in range(n):
+            q.copy_(src[i])  # the kernel right before each launch writes its queries
+            outs.append(ops.decode(q, n_kv_heads=Hkv, key_format=SMAQ_KEYS_BVQ, centroids=dec, key_codes=st["codes"],
+                                   v_data=st["vdata"], v_scales=st["vs"], v_zeros=st["vz"], hist_len=hl,
+                                   page_size=page_size, block_table=st["bt"], recent_k=rk, recent_v=rv,
+                                   recent_len=rl, workspace=ws, layout=1, centroids_f16=c16, overlap_prior=overlap))
+        torch.cuda.synchronize()
+        return outs
+
+    plain, over = run(False), run(True)
+    for a, b in zip(plain, over):
+        assert torch.equal(a, b)
+    ops.decode_status(B, Hkv, ws)  # raises if a device wait ran out
