@@ -510,7 +510,7 @@ extern "C" int smaq_decode(const smaq_decode_args* args, void* stream) {
   p.slots = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + plan_bytes(p.n_seg));
   p.grid = grid;
   if ((kb == 0 && decode_v2_eligible(p, SMAQ_KEYS_BVQ, a.value_bits, p.q_dtype) &&
-       p.n_seg <= decode_v2_max_fused_segments()) ||
+       p.n_seg <= decode_v2_max_fused_segments(p.G)) ||
       (kb != 0 && decode_s_eligible(p, kb, a.value_bits))) {
     // one launch: partition, history, window and the per-pair merge in the tensor-core kernel
     static std::atomic<uint32_t> epochs{0};

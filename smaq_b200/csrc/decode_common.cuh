@@ -157,7 +157,7 @@ __device__ void cta_flush(const DecodeParams& p, WarpState<GM>& st, float* red, 
 // Fast path (block-VQ keys, decode layout, 2-bit values, head_dim 128): see decode_v2.cu.
 bool decode_v2_eligible(const DecodeParams& p, int key_format, int value_bits, int q_dtype);
 int launch_decode_v2(DecodeParams& p, int grid_req, cudaStream_t s, int* grid_out, bool query_only);
-int decode_v2_max_fused_segments();
+int decode_v2_max_fused_segments(int G);
 // Scalar 3/4-bit keys, decode layout: tensor-core kernel (decode_v2.cu); always single-launch.
 bool decode_s_eligible(const DecodeParams& p, int key_bits, int value_bits);
 int launch_decode_s(DecodeParams& p, int grid_req, cudaStream_t s, int* grid_out, bool query_only);

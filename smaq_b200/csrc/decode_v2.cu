@@ -53,25 +53,33 @@ constexpr int ST_IDX = 0, ST_V = CH * 16, ST_S = CH * 48, ST_Z = CH * 56, STAGE_
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
-template <int GM>
-struct V3Cfg {
 #ifndef SMAQ_V3_WARPS
 #define SMAQ_V3_WARPS 16
 #define SMAQ_V3_STAGES 3
 #endif
-  static constexpr int WARPS = SMAQ_V3_WARPS;
+// G <= 4 (score lookup table): warps per CTA, ring stages, CTAs per SM, partition-table size
+#ifndef SMAQ_V3_LUT_WARPS
+#define SMAQ_V3_LUT_WARPS 16
+#define SMAQ_V3_LUT_STAGES 3
+#define SMAQ_V3_LUT_CTAS 1
+#define SMAQ_V3_LUT_SEG 2048
+#endif
+template <int GM>
+struct V3Cfg {
+  static constexpr int WARPS = GM == 4 ? SMAQ_V3_LUT_WARPS : SMAQ_V3_WARPS;
   static constexpr int THREADS = WARPS * 32;
-  static constexpr int STAGES = SMAQ_V3_STAGES;
+  static constexpr int STAGES = GM == 4 ? SMAQ_V3_LUT_STAGES : SMAQ_V3_STAGES;
+  static constexpr int CTAS = GM == 4 ? SMAQ_V3_LUT_CTAS : 1;    // resident CTAs per SM
   static constexpr int CB_BYTES = 256 * 16 * 16;                 // fp16 codebook [c][block'][8]
-  static constexpr int Q_BYTES = 8 * 128 * 4;
+  static constexpr int Q_BYTES = GM * 128 * 4;                   // fp32 query rows
   static constexpr int SZ_BYTES = 2 * 4 * CH * 2;                // fp16 scales | zeros [j][ks][slot]
   static constexpr int WARP_BYTES = STAGES * STAGE_BYTES + SZ_BYTES + 256;  // ring | s,z | misc
   static constexpr int BAR_BYTES = WARPS * STAGES * 8;
-  static constexpr int MAX_FUSED_SEG = 2048;                     // in-kernel partition table
+  static constexpr int MAX_FUSED_SEG = GM == 4 ? SMAQ_V3_LUT_SEG : 2048;  // in-kernel partition table
   static constexpr int PLAN_BYTES = (MAX_FUSED_SEG + 4) * 8 + 33 * 8 + 16 + MAX_FUSED_SEG * 4;  // table | scan | flag | tokens
   static constexpr int SMEM = CB_BYTES + Q_BYTES + WARPS * WARP_BYTES + BAR_BYTES + PLAN_BYTES;
   static_assert(GM * (128 + 2) * 4 <= STAGES * STAGE_BYTES, "merge record must fit in a ring");
-  static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(SMEM <= (CTAS == 1 ? 232448 : 233472 / CTAS - 1024), "shared memory budget");
 };
 
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
@@ -669,7 +677,7 @@ __device__ void v3_arrive(const DecodeParams& p, const int64_t* plan, const int*
 }
 
 template <int GM>
-__global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(DecodeParams p,
+__global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3_kernel(DecodeParams p,
                                                                           const uint16_t* __restrict__ cb16) {
   using C = V3Cfg<GM>;
   constexpr int D = 128;
@@ -839,7 +847,7 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, 1) decode_v3_kernel(Decode
     if (t1 > n) t1 = n;
     if (t0 >= t1) continue;
     const int pair = s >> 1, b = pair / p.Hkv, h = pair - b * p.Hkv;
-    for (int i = threadIdx.x; i < 8 * D; i += blockDim.x) {
+    for (int i = threadIdx.x; i < GM * D; i += blockDim.x) {
       const int g = i / D, d = i - g * D;
       qs[i] = g < G ? load_elem(p.q, p.q_dtype, b * p.q_sb + int64_t(h * G + g) * p.q_sh + d) : 0.f;
     }
@@ -1523,7 +1531,7 @@ static int launch_v3_t(DecodeParams& p, int grid_req, cudaStream_t s, int* grid_
   const int sm = V3Cfg<GM>::SMEM;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
   if (e != cudaSuccess) return cuda_status(e, "decode_v3 attr");
-  const int grid = grid_req > 0 ? grid_req : num_sms();
+  const int grid = grid_req > 0 ? grid_req : num_sms() * V3Cfg<GM>::CTAS;
   *grid_out = grid;
   if (query_only) return SMAQ_OK;
   if (!p.pdl) {
@@ -1544,7 +1552,7 @@ static int launch_v3_t(DecodeParams& p, int grid_req, cudaStream_t s, int* grid_
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, p, p.cent16), "decode_v3_kernel (overlapped)");
 }
 
-int decode_v2_max_fused_segments() { return V3Cfg<4>::MAX_FUSED_SEG; }
+int decode_v2_max_fused_segments(int G) { return G <= 4 ? V3Cfg<4>::MAX_FUSED_SEG : V3Cfg<8>::MAX_FUSED_SEG; }
 
 #ifdef SMAQ_PROF
 extern "C" int smaq_debug_v3_prof(unsigned long long* out8, int reset) {
