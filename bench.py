@@ -610,7 +610,7 @@ def run_paged(a, rank: int, world: int):
                    E_inv=quant.E_inv, centroids=quant.centroids, key_norms=L["norms"], key_codes=L["codes"],
                    v_data=L["vdata"], v_scales=L["vs"], v_zeros=L["vz"], hist_len=hl, page_size=PG_PAGE,
                    block_table=L["bt"], recent_k=L["rk"], recent_v=L["rv"], recent_len=rl, out=L["out"], workspace=ws,
-                   layout=SMAQ_LAYOUT_DECODE)
+                   layout=SMAQ_LAYOUT_DECODE, overlap_prior=a.overlap)
 
     def step():
         for L in layers:

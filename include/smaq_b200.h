@@ -182,7 +182,8 @@ typedef struct smaq_decode_args {
   /* Nonzero: launch the single-launch kernels with programmatic dependent launch, so that their
    * partition and first history copies overlap the end of the previous kernel on the stream.
    * The caller promises that kernel writes none of: key_codes / key_norms / v_data / v_scales /
-   * v_zeros rows, block_table, hist_len, hist_total, recent_len.  Queries, the window, outputs
+   * v_zeros rows, block_table, hist_len, hist_total, recent_len, and the codebooks (centroids,
+   * centroids_f16, E_inv).  Queries, the window, outputs
    * and the workspace are read or written only after that kernel has completed.  Ignored by the
    * multi-launch path.  Zero gives plain stream ordering. */
   int overlap_prior;

@@ -33,10 +33,13 @@
 namespace smaq {
 
 #ifndef SMAQ_ABL
-#define SMAQ_ABL 0  // profiling builds only: bit 1 skips P.V, 2 skips score MMAs, 4 skips staging
+#define SMAQ_ABL 0  // profiling builds only: bit 1 skips P.V, 2 skips score MMAs, 4 skips staging;
+                    // lookup-table path: 32 skips P.V, 64 score lookups, 128 scale staging, 256 softmax
 #endif
 #ifdef SMAQ_PROF  // profiling builds only: per-phase clock totals of thread 0 of every CTA
-__device__ unsigned long long g_v3_prof[16];
+// [0..13] phase totals, [7] whole-CTA total, [14] whole-CTA maximum, [15] CTA count,
+// [19] cycles thread 0 spends in chunk waits, [20] chunk waits whose data had not landed, [21] chunk waits
+__device__ unsigned long long g_v3_prof[32];
 #define V3_PROF(k)                                                \
   do {                                                            \
     if (threadIdx.x == 0) {                                       \
@@ -319,7 +322,7 @@ __device__ __forceinline__ void v3_chunk_lut(uint32_t st, uint32_t szs, uint32_t
   const int lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
   // ---- the chunk's value scales and zeros as fp16, in MMA k-slot order (one token per lane)
-  {
+  if (!(SMAQ_ABL & 128)) {
     uint2 s2 = lds64(st + ST_S + lane * 8);
     uint2 z2 = lds64(st + ST_Z + lane * 8);
     if (!FULL && lane >= nv) s2 = z2 = make_uint2(0u, 0u);  // rows past the end may hold anything
@@ -342,8 +345,9 @@ __device__ __forceinline__ void v3_chunk_lut(uint32_t st, uint32_t szs, uint32_t
                          __byte_perm(n3, 0, X.sel)};
   // heads (0, 1) and (2, 3) accumulate as packed fp32 pairs (one add.f32x2 per pair)
   uint64_t s01 = 0ull, s23 = 0ull;
+  if (SMAQ_ABL & 64) { s01 = r[0] | (uint64_t(r[1]) << 32); s23 = r[2] | (uint64_t(r[3]) << 32); }
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
+  for (int j = 0; j < ((SMAQ_ABL & 64) ? 0 : 16); ++j) {
     const uint32_t c256 = __byte_perm(r[j >> 2], 0, 0x4404 | ((j & 3) << 4));  // code * 256
     const ulonglong2 e = *reinterpret_cast<const ulonglong2*>(sm + (c256 | (X.xl ^ uint32_t(j << 4))));
     asm("add.rn.f32x2 %0, %0, %1;" : "+l"(s01) : "l"(e.x));
@@ -354,7 +358,7 @@ __device__ __forceinline__ void v3_chunk_lut(uint32_t st, uint32_t szs, uint32_t
   if (!FULL && lane >= nv) s[0] = s[1] = s[2] = s[3] = -INFINITY;
   // ---- softmax: p = exp2(s - mref); the reference maximum only moves up
   const bool grow = (s[0] > mref[0]) | (s[1] > mref[1]) | (s[2] > mref[2]) | (s[3] > mref[3]);
-  if (__any_sync(0xffffffffu, grow)) {
+  if (!(SMAQ_ABL & 256) && __any_sync(0xffffffffu, grow)) {
     float al[4];
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
@@ -375,14 +379,14 @@ __device__ __forceinline__ void v3_chunk_lut(uint32_t st, uint32_t szs, uint32_t
   // p in fp16, k-slot order per head (the B operand layout of the P.V MMA)
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
-    const float pg = fast_exp2(s[g] - mref[g]);  // 0 for masked tokens
+    const float pg = (SMAQ_ABL & 256) ? s[g] : fast_exp2(s[g] - mref[g]);  // 0 for masked tokens
     lsum[g] += pg;
     sts16(pb + g * 64 + L.sz_off, __half_as_ushort(__float2half_rn(pg)));
   }
   __syncwarp();  // p, fp16 scales / zeros visible to the warp
   // ---- P.V: k-step ks covers tokens 16ks + tig + 4u (u = 0..3)
 #pragma unroll
-  for (int ks = 0; ks < 2; ++ks) {
+  for (int ks = 0; ks < ((SMAQ_ABL & 32) ? 0 : 2); ++ks) {
     const uint32_t p01 = gid < 4 ? lds32(pb + gid * 64 + ks * 32 + tig * 4) : 0u;        // k-slots 2tig, 2tig+1
     const uint32_t p23 = gid < 4 ? lds32(pb + gid * 64 + ks * 32 + tig * 4 + 16) : 0u;   // k-slots 2tig+8, 2tig+9
     const uint32_t sb = szs + ks * 32 + tig * 4;
@@ -986,7 +990,17 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3
     for (int i = 0; i < mine; ++i) {
       const int stg = i % ST;
       uint8_t* stage = wreg + stg * STAGE_BYTES;
+#ifdef SMAQ_PROF
+      const long long w0_ = clock64();
+      if (threadIdx.x == 0 && !mbar_test(&wbar[stg], (phase >> stg) & 1u)) atomicAdd(&g_v3_prof[20], 1ull);
+#endif
       if (!failed && !mbar_wait(&wbar[stg], (phase >> stg) & 1u)) failed = true;
+#ifdef SMAQ_PROF
+      if (threadIdx.x == 0) {
+        atomicAdd(&g_v3_prof[19], (unsigned long long)(clock64() - w0_));
+        atomicAdd(&g_v3_prof[21], 1ull);
+      }
+#endif
       phase ^= 1u << stg;
       const int nv = min(CH, ntok - (wid + WARPS * i) * CH);
       if constexpr (GM == 4) {
@@ -1284,12 +1298,34 @@ __global__ void __launch_bounds__(SCfg::THREADS, 1) decode_s_kernel(DecodeParams
   const int64_t* plan = p.plan;
   const int* ntab = nullptr;
   if (p.fused) {
-    // device error word: cleared by CTA 0 at start; a bounded wait that runs out (seconds later)
-    // sets it, and smaq_decode_status reports it
-    if (blockIdx.x == 0 && threadIdx.x == 0) *reinterpret_cast<volatile int*>(p.plan + p.n_seg + 2) = 0;
+    // overlapped launch: the next launch on the stream may be scheduled now
+    if (p.pdl) pdl_launch_dependents();
     v3_plan(p, splan, splan + C::MAX_FUSED_SEG + 4, sntab);
     plan = splan;
     ntab = sntab;
+  }
+  // code byte -> (c_hi[lo nibble], c_hi[hi nibble]) | (c_lo pair), replicated per lane so a
+  // warp's 32 lookups hit 32 distinct bank pairs: entry (byte, lane) at byte * 256 + lane * 8
+  {
+    const int bits = p.nc == 8 ? 3 : 4;
+    const uint32_t mask = (1u << bits) - 1u;
+    for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) {
+      const int by = i >> 5;
+      const float c0v = __ldg(p.cent + (by & mask)), c1v = __ldg(p.cent + ((by >> bits) & mask));
+      const __half h0 = __float2half_rn(c0v), h1 = __float2half_rn(c1v);
+      const __half l0 = __float2half_rn(c0v - __half2float(h0)), l1 = __float2half_rn(c1v - __half2float(h1));
+      *reinterpret_cast<uint2*>(tab + i * 8) =
+          make_uint2(uint32_t(__half_as_ushort(h0)) | (uint32_t(__half_as_ushort(h1)) << 16),
+                     uint32_t(__half_as_ushort(l0)) | (uint32_t(__half_as_ushort(l1)) << 16));
+    }
+  }
+  // overlapped launch: partition and code table above overlap the previous kernel's end;
+  // everything below may read its outputs
+  if (p.pdl) pdl_wait();
+  if (p.fused) {
+    // device error word: cleared by CTA 0 at start; a bounded wait that runs out (seconds later)
+    // sets it, and smaq_decode_status reports it
+    if (blockIdx.x == 0 && threadIdx.x == 0) *reinterpret_cast<volatile int*>(p.plan + p.n_seg + 2) = 0;
     for (int pair = blockIdx.x; pair < p.B * p.Hkv; pair += gridDim.x) {
       int e = 0;
       for (int k = 0; k < 2; ++k) {
@@ -1310,21 +1346,6 @@ __global__ void __launch_bounds__(SCfg::THREADS, 1) decode_s_kernel(DecodeParams
   {
     const int ks = lane >> 4, u = (lane >> 2) & 3, v = lane & 3;
     L.sz_off = uint32_t(2 * (16 * ks + 2 * v + (u & 1) + 8 * (u >> 1)));
-  }
-  // code byte -> (c_hi[lo nibble], c_hi[hi nibble]) | (c_lo pair), replicated per lane so a
-  // warp's 32 lookups hit 32 distinct bank pairs: entry (byte, lane) at byte * 256 + lane * 8
-  {
-    const int bits = p.nc == 8 ? 3 : 4;
-    const uint32_t mask = (1u << bits) - 1u;
-    for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) {
-      const int by = i >> 5;
-      const float c0v = __ldg(p.cent + (by & mask)), c1v = __ldg(p.cent + ((by >> bits) & mask));
-      const __half h0 = __float2half_rn(c0v), h1 = __float2half_rn(c1v);
-      const __half l0 = __float2half_rn(c0v - __half2float(h0)), l1 = __float2half_rn(c1v - __half2float(h1));
-      *reinterpret_cast<uint2*>(tab + i * 8) =
-          make_uint2(uint32_t(__half_as_ushort(h0)) | (uint32_t(__half_as_ushort(h1)) << 16),
-                     uint32_t(__half_as_ushort(l0)) | (uint32_t(__half_as_ushort(l1)) << 16));
-    }
   }
   const uint32_t tab_l = uint32_t(lane * 8);
   const uint32_t ring_s = uint32_t(wreg - sm);
@@ -1514,8 +1535,22 @@ int launch_decode_s(DecodeParams& p, int grid_req, cudaStream_t s, int* grid_out
   const int grid = grid_req > 0 ? grid_req : num_sms();
   *grid_out = grid;
   if (query_only) return SMAQ_OK;
-  kern<<<grid, SCfg::THREADS, SCfg::SMEM, s>>>(p);
-  return cuda_status(cudaGetLastError(), "decode_s_kernel");
+  if (!p.pdl) {
+    kern<<<grid, SCfg::THREADS, SCfg::SMEM, s>>>(p);
+    return cuda_status(cudaGetLastError(), "decode_s_kernel");
+  }
+  // programmatic dependent launch: may start while the previous kernel on `s` finishes
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(SCfg::THREADS);
+  cfg.dynamicSmemBytes = SCfg::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, p), "decode_s_kernel (overlapped)");
 }
 
 bool decode_v2_eligible(const DecodeParams& p, int key_format, int value_bits, int q_dtype) {
@@ -1555,11 +1590,13 @@ static int launch_v3_t(DecodeParams& p, int grid_req, cudaStream_t s, int* grid_
 int decode_v2_max_fused_segments(int G) { return G <= 4 ? V3Cfg<4>::MAX_FUSED_SEG : V3Cfg<8>::MAX_FUSED_SEG; }
 
 #ifdef SMAQ_PROF
-extern "C" int smaq_debug_v3_prof(unsigned long long* out8, int reset) {
+// Profiling builds only: copy the 32 counters of g_v3_prof to `out` (room for 32), then
+// optionally clear them.
+extern "C" int smaq_debug_v3_prof(unsigned long long* out, int reset) {
   cudaDeviceSynchronize();
-  cudaMemcpyFromSymbol(out8, g_v3_prof, sizeof(unsigned long long) * 16);
+  cudaMemcpyFromSymbol(out, g_v3_prof, sizeof(unsigned long long) * 32);
   if (reset) {
-    unsigned long long z[16] = {};
+    unsigned long long z[32] = {};
     cudaMemcpyToSymbol(g_v3_prof, z, sizeof(z));
   }
   return 0;

@@ -192,7 +192,7 @@ def decode(q: torch.Tensor, *, n_kv_heads: int, key_format: int, key_codes: torc
     the query dtype (reference rounding), and/or fills ``partial_out [B, Hq, 2D+2]``.
     ``overlap_prior``: overlap the launch with the end of the previous kernel on the stream
     (programmatic dependent launch); only when that kernel writes none of the history rows,
-    block table or lengths (``smaq_decode_args.overlap_prior``).
+    block table, lengths or codebooks (``smaq_decode_args.overlap_prior``).
     """
     _cuda(q, key_codes, v_data, hist_len, recent_k, block_table)
     lib = _lib.load()

@@ -242,21 +242,32 @@ def test_scalar_decode_layout_bytes(cuda, bits):
         assert torch.equal(out[1][1], out[0][1])
 
 
-def test_overlapped_launches_match_plain(cuda):
+@pytest.mark.parametrize("kind", ["bvq", "scalar"])
+def test_overlapped_launches_match_plain(cuda, kind):
     """overlap_prior (programmatic dependent launch): back-to-back launches sharing one workspace,
     each right after a kernel that rewrites its queries, give exactly the plain launches' outputs."""
     import torch
     from smaq_b200 import ops
-    from smaq_b200._lib import SMAQ_KEYS_BVQ
+    from smaq_b200._lib import SMAQ_KEYS_BVQ, SMAQ_KEYS_SCALAR
     B, Hkv, G, page_size = 5, 2, 4, 16
     hist, recent = [1000, 15, 16, 333, 2048], [64, 3, 0, 128, 1]
-    st, raw = build_paged(cuda, "bvq", 0, B, Hkv, hist, page_size, "bfloat16", 41)
-    Eb, C, dec = random_codebook(cuda)
-    for k, v, slots in raw:
-        ops.append(k, v, n_heads=Hkv, slots=slots, page_size=page_size, key_format=SMAQ_KEYS_BVQ,
-                   E_blocks=Eb, centroids=C, key_codes=st["codes"], v_data=st["vdata"], v_scales=st["vs"],
-                   v_zeros=st["vz"], layout=1)
-    c16 = ops.fp16_codebook(dec)
+    bits = 4 if kind == "scalar" else 0
+    st, raw = build_paged(cuda, kind, bits, B, Hkv, hist, page_size, "bfloat16", 41)
+    if kind == "scalar":
+        qz = scalar_tables(bits, cuda)
+        for k, v, slots in raw:
+            ops.append(k, v, n_heads=Hkv, slots=slots, page_size=page_size, key_format=SMAQ_KEYS_SCALAR,
+                       key_bits=bits, E=qz.E, boundaries=qz.decision_boundaries, key_codes=st["codes"],
+                       key_norms=st["norms"], v_data=st["vdata"], v_scales=st["vs"], v_zeros=st["vz"], layout=1)
+        kw = dict(key_format=SMAQ_KEYS_SCALAR, key_bits=bits, E_inv=qz.E_inv, centroids=qz.centroids,
+                  key_norms=st["norms"])
+    else:
+        Eb, C, dec = random_codebook(cuda)
+        for k, v, slots in raw:
+            ops.append(k, v, n_heads=Hkv, slots=slots, page_size=page_size, key_format=SMAQ_KEYS_BVQ,
+                       E_blocks=Eb, centroids=C, key_codes=st["codes"], v_data=st["vdata"], v_scales=st["vs"],
+                       v_zeros=st["vz"], layout=1)
+        kw = dict(key_format=SMAQ_KEYS_BVQ, centroids=dec, centroids_f16=ops.fp16_codebook(dec))
     bf = torch.bfloat16
     rk = torch.from_numpy(syn.keys((B, 128, Hkv), D, seed=42)).to(cuda).to(bf)
     rv = torch.from_numpy(syn.values((B, 128, Hkv), D, seed=43)).to(cuda).to(bf)
@@ -271,10 +282,10 @@ def test_overlapped_launches_match_plain(cuda):
         outs = []
         for i in range(n):
             q.copy_(src[i])  # the kernel right before each launch writes its queries
-            outs.append(ops.decode(q, n_kv_heads=Hkv, key_format=SMAQ_KEYS_BVQ, centroids=dec, key_codes=st["codes"],
-                                   v_data=st["vdata"], v_scales=st["vs"], v_zeros=st["vz"], hist_len=hl,
-                                   page_size=page_size, block_table=st["bt"], recent_k=rk, recent_v=rv,
-                                   recent_len=rl, workspace=ws, layout=1, centroids_f16=c16, overlap_prior=overlap))
+            outs.append(ops.decode(q, n_kv_heads=Hkv, key_codes=st["codes"], v_data=st["vdata"], v_scales=st["vs"],
+                                   v_zeros=st["vz"], hist_len=hl, page_size=page_size, block_table=st["bt"],
+                                   recent_k=rk, recent_v=rv, recent_len=rl, workspace=ws, layout=1,
+                                   overlap_prior=overlap, **kw))
         torch.cuda.synchronize()
         return outs
 
