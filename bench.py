@@ -793,7 +793,10 @@ def main():
         peak_src = "measured"
     except Exception:
         peak_gbs = 6650.0
-    achieved = bpl / (layer_ms * 1e-3) / 1e9
+    # average launch duration over the timed region: one decode launch per layer and nothing
+    # else in a step (consecutive launches overlap when --no-overlap is not given)
+    launch_ms = ms / a.layers
+    achieved = bpl / (launch_ms * 1e-3) / 1e9
     # DRAM bytes per launch from one ncu capture of this workload (profiles/decode_bvq_cfg1_kernel.md)
     default_shape = (a.batch, a.ctx, a.window, a.hq, a.hkv) == (16, 32768, 128, 32, 8)
     traffic = 284.2e6 if default_shape else None
@@ -811,7 +814,9 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s",
                          "frac": achieved / peak_gbs, "traffic": traffic, "peak_source": peak_src,
                          "kernel": "smaq_decode per layer (one decode_v3_kernel launch)",
-                         "algorithmic_bytes_per_launch": bpl},
+                         "algorithmic_bytes_per_launch": bpl, "launch_us": launch_ms * 1e3,
+                         "launch_us_isolated": layer_ms * 1e3,
+                         "launch_time": "timed region / launches; isolated = one launch between two events"},
             "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": a.layers * a.steps,
