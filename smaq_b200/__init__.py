@@ -1,7 +1,7 @@
 """smaq_b200: B200-native (sm_100a) implementation of SMAQ's compressed-KV hot path.
 
 The modules mirror the reference package ``smaq`` (gauravsaini/smaq) for the hot path:
-``quantizer``, ``block_vq``, ``kv_cache``, ``store``, ``score``, ``capture``, ``strategies``,
+``quantizer``, ``weighted_scalar``, ``block_vq``, ``kv_cache``, ``store``, ``score``, ``capture``, ``strategies``,
 ``core``, ``calibration``, ``vllm_attn_backend`` / ``integration.vllm``.  Compute runs in
 ``libsmaq_b200.so`` (C ABI in ``include/smaq_b200.h``); there is no CPU fallback.
 
@@ -16,8 +16,8 @@ import sys
 
 __version__ = "0.1.0"
 
-_MIRRORED = ("ssf", "core", "calibration", "quantizer", "block_vq", "kv_cache", "strategies", "store",
-             "score", "capture", "backends")
+_MIRRORED = ("ssf", "core", "calibration", "quantizer", "weighted_scalar", "block_vq", "kv_cache", "strategies",
+             "store", "score", "capture", "backends")
 
 
 def install_as_smaq() -> None:
@@ -40,7 +40,9 @@ def __getattr__(name):
         "compute_hybrid_attention": "score", "KVCaptureEngine": "capture", "RingBuffer": "capture",
         "SMAQFullMetricScalarStrategy": "strategies", "SMAQBlockVQStrategy": "strategies",
         "IdentityMetricStrategy": "strategies", "SMAQFullMetricStrategy": "strategies",
-        "SMAQDiagonalMetricState": "strategies", "IdentityCalibrationProvider": "calibration",
+        "SMAQDiagonalMetricState": "strategies", "IdentityScalarStrategy": "strategies",
+        "SMAQDiagonalMetricStrategy": "strategies", "RotationAdapter": "weighted_scalar",
+        "SMAQWeightedRotationQuantizer": "weighted_scalar", "IdentityCalibrationProvider": "calibration",
         "StaticCalibrationProvider": "calibration", "TorchHybridAttentionBackend": "backends",
         "AttentionBackend": "core", "CacheBackend": "core", "CacheCapabilities": "core",
         "CalibrationProvider": "core", "LayoutInfo": "core", "MetricStrategy": "core",

@@ -24,7 +24,7 @@ from smaq_b200.calibration import IdentityCalibrationProvider
 from smaq_b200.core import CacheCapabilities, CalibrationProvider
 from smaq_b200.kv_cache import ValueQuantized
 from smaq_b200.quantizer import SMAQQuantized
-from smaq_b200.strategies import SMAQBlockVQStrategy, SMAQFullMetricScalarStrategy
+from smaq_b200.strategies import IdentityScalarStrategy, SMAQBlockVQStrategy, SMAQFullMetricScalarStrategy
 
 
 class FlatCache(NamedTuple):
@@ -36,13 +36,14 @@ class FlatCache(NamedTuple):
 
 
 def key_format_of(strategy) -> int:
-    if isinstance(strategy, SMAQFullMetricScalarStrategy):
+    if isinstance(strategy, IdentityScalarStrategy):
         return SMAQ_KEYS_SCALAR
     if isinstance(strategy, SMAQBlockVQStrategy):
         return SMAQ_KEYS_BVQ
     raise NotImplementedError(
-        f"key strategy {type(strategy).__name__} has no sm_100a kernel (supported: "
-        "SMAQFullMetricScalarStrategy, SMAQBlockVQStrategy)")
+        f"key strategy {type(strategy).__name__} has no sm_100a kernel (supported: the scalar strategies "
+        "IdentityScalarStrategy / SMAQFullMetricScalarStrategy / SMAQDiagonalMetricStrategy, and "
+        "SMAQBlockVQStrategy)")
 
 
 class CompressedKVStore:

@@ -1,9 +1,12 @@
 """Key quantization strategies on the hot path (same classes as smaq/strategies.py).
 
-Only the two strategies the decode kernels serve are provided:
-``SMAQFullMetricScalarStrategy`` (scalar codes, the reference's default key strategy) and
-``SMAQBlockVQStrategy``.  The RotationAdapter-based strategies of the reference (identity /
-diagonal metric, exact shadow) are outside this package's scope.
+Scalar-code strategies (``IdentityScalarStrategy`` and its subclasses
+``SMAQFullMetricScalarStrategy`` and ``SMAQDiagonalMetricStrategy``) share the
+``SMAQQuantized`` format.  Their quantizers expose ``E`` / ``E_inv`` / ``centroids`` /
+``decision_boundaries``, so the scalar-key append and decode kernels serve all three.
+``SMAQBlockVQStrategy`` is served by the block-VQ kernels.  The reference's
+``ExactShadowStrategy`` keeps the history's keys unquantized and scores them with a dense
+matmul: it is a validation mode outside the compressed path and is not provided.
 """
 
 from __future__ import annotations
@@ -16,6 +19,7 @@ from smaq_b200.block_vq import BlockVQQuantized, SMAQBlockVQ
 from smaq_b200.core import MetricStrategy, QuantizationStrategy
 from smaq_b200.quantizer import SMAQQuantized, SMAQQuantizer
 from smaq_b200.ssf import build_smaq_metric
+from smaq_b200.weighted_scalar import RotationAdapter
 
 
 def _dev(device):
@@ -77,25 +81,17 @@ class SMAQDiagonalMetricState(MetricStrategy):
         return {"Sigma_q": self.sigma_q}
 
 
-class SMAQFullMetricScalarStrategy(QuantizationStrategy):
-    """Scalar metric-aware key codes (smaq/strategies.py:100-168)."""
+class IdentityScalarStrategy(QuantizationStrategy):
+    """Scalar codes with no metric: identity rotation, unit scales, midpoint codebook
+    (smaq/strategies.py:100-138)."""
 
-    name = "smaq_full_metric_scalar"
-    metric_name = "smaq_full_metric"
+    name = "identity_scalar"
+    metric_name = "identity"
     quantization_name = "scalar"
 
-    def __init__(self, dim: int, bits: int = 3, Sigma_q: torch.Tensor | None = None,
-                 device: torch.device | None = None, dtype: torch.dtype = torch.float32):
-        self.quantizer = SMAQQuantizer(dim=dim, bits=bits, Sigma_q=Sigma_q, device=device, dtype=dtype)
+    def __init__(self, dim: int, bits: int = 3, device: torch.device | None = None):
+        self.quantizer = RotationAdapter(dim=dim, bits=bits, coord_scales=torch.ones(dim), device=device)
         self.bits = bits
-
-    @property
-    def supports_kernel(self) -> bool:
-        return True
-
-    def fit(self, calibration_queries: Any, calibration_keys: Any | None = None) -> "SMAQFullMetricScalarStrategy":
-        self.quantizer.fit(calibration_queries)
-        return self
 
     def quantize(self, keys: Any) -> Any:
         return self.quantizer.quantize(keys)
@@ -104,8 +100,7 @@ class SMAQFullMetricScalarStrategy(QuantizationStrategy):
         return self.quantizer.dequantize(quantized)
 
     def attention_score(self, query: Any, quantized: Any, scale: float | None = None, **kwargs: Any) -> Any:
-        return self.quantizer.attention_score(query, quantized, scale=scale,
-                                              use_kernel=kwargs.get("use_kernel", False))
+        return self.quantizer.attention_score(query, quantized, scale=scale)
 
     def flatten_quantized(self, quantized: SMAQQuantized) -> SMAQQuantized:
         ix, nm = quantized.indices, quantized.norms
@@ -123,6 +118,44 @@ class SMAQFullMetricScalarStrategy(QuantizationStrategy):
     def memory_bytes(self, quantized: SMAQQuantized) -> int:
         # the reference's accounting: one byte per packed code byte, two per norm
         return quantized.indices.nelement() + quantized.norms.nelement() * 2
+
+
+class SMAQFullMetricScalarStrategy(IdentityScalarStrategy):
+    """Scalar metric-aware key codes (smaq/strategies.py:141-166)."""
+
+    name = "smaq_full_metric_scalar"
+    metric_name = "smaq_full_metric"
+
+    def __init__(self, dim: int, bits: int = 3, Sigma_q: torch.Tensor | None = None,
+                 device: torch.device | None = None, dtype: torch.dtype = torch.float32):
+        self.quantizer = SMAQQuantizer(dim=dim, bits=bits, Sigma_q=Sigma_q, device=device, dtype=dtype)
+        self.bits = bits
+
+    @property
+    def supports_kernel(self) -> bool:
+        return True
+
+    def fit(self, calibration_queries: Any, calibration_keys: Any | None = None) -> "SMAQFullMetricScalarStrategy":
+        self.quantizer.fit(calibration_queries)
+        return self
+
+    def attention_score(self, query: Any, quantized: Any, scale: float | None = None, **kwargs: Any) -> Any:
+        return self.quantizer.attention_score(query, quantized, scale=scale,
+                                              use_kernel=kwargs.get("use_kernel", False))
+
+
+class SMAQDiagonalMetricStrategy(IdentityScalarStrategy):
+    """Diagonal approximation of the SMAQ metric in a rotation basis (smaq/strategies.py:169-192)."""
+
+    name = "smaq_diagonal_metric"
+    metric_name = "smaq_diagonal_metric"
+
+    def __init__(self, dim: int, bits: int = 3, Sigma_q: torch.Tensor | None = None,
+                 rotation: torch.Tensor | None = None, device: torch.device | None = None,
+                 dtype: torch.dtype = torch.float32):
+        self.quantizer = RotationAdapter(dim=dim, bits=bits, Sigma_q=Sigma_q, rotation=rotation, device=device,
+                                         dtype=dtype)
+        self.bits = bits
 
 
 class SMAQBlockVQStrategy(QuantizationStrategy):

@@ -7,7 +7,8 @@ Usage::
 ``PATH`` is a checkout of gauravsaini/smaq (the package directory ``smaq/``
 must sit directly under it).  The reference is pure Python on PyTorch; it is
 imported here, fed the seeded synthetic inputs of ``smaq_b200.synthetic``, and
-its outputs are written to ``tests/golden/*.npz``.  bf16/fp16 tensors are
+its outputs are written to ``tests/golden/golden.npz`` and, for the rotation adapter
+(smaq/weighted_scalar.py), ``tests/golden/golden_rotation.npz``.  bf16/fp16 tensors are
 stored as float32 arrays holding exactly representable values.  The GPU box
 never runs this script; the tests only read the ``.npz`` files it wrote.
 """
@@ -34,12 +35,101 @@ def t2n(t):
     return t.detach().cpu().numpy()
 
 
+def rotation_goldens(out):
+    """RotationAdapter (smaq/weighted_scalar.py) and its strategies: scales, codebooks, codes,
+    norms, scores, calibration choice and a hybrid decode through the store."""
+    import torch
+    from smaq.weighted_scalar import (RotationAdapter, build_block_diagonal_metric_scales,
+                                      build_rotated_diagonal_metric_scales)
+    from smaq.strategies import SMAQDiagonalMetricStrategy
+    from smaq.store import CompressedKVStore
+    from smaq.score import compute_hybrid_attention
+    D = 128
+    cpu = torch.device("cpu")
+    calq = torch.from_numpy(syn.calibration_queries(512, D))
+    sig = (calq.T @ calq) / calq.shape[0]
+    R = torch.linalg.qr(torch.from_numpy(np.random.default_rng(61).standard_normal((D, D)).astype(np.float32)))[0]
+    out["ra_sigma"] = t2n(sig)
+    out["ra_rotation"] = t2n(R)
+    out["ra_scales_rot"] = t2n(build_rotated_diagonal_metric_scales(sig, rotation=R))
+    out["ra_scales_norot"] = t2n(build_rotated_diagonal_metric_scales(sig))
+    out["ra_scales_block2"] = t2n(build_block_diagonal_metric_scales(sig, block_size=2))
+    out["ra_scales_block3"] = t2n(build_block_diagonal_metric_scales(sig, block_size=3))
+    DT = {"fp32": torch.float32, "bf16": torch.bfloat16}
+    kq = syn.keys((48, 4), D, seed=62).reshape(192, D)
+    kq[0] = 0.0
+    qq = syn.queries((6,), D, seed=63)
+    cases = {
+        "identity3": dict(bits=3, coord_scales=torch.ones(D)),
+        "diag4": dict(bits=4, Sigma_q=sig),
+        "rot3": dict(bits=3, Sigma_q=sig, rotation=R),
+        "block2": dict(bits=2, coord_scales=build_block_diagonal_metric_scales(sig, block_size=2)),
+    }
+    for dn, dt in DT.items():
+        out[f"ra_{dn}_k"] = t2n(torch.from_numpy(kq).to(dt))
+        out[f"ra_{dn}_q"] = t2n(torch.from_numpy(qq).to(dt))
+    for tag, kw in cases.items():
+        ad = RotationAdapter(D, device=cpu, **kw)
+        p = f"ra_{tag}_"
+        for name in ("coord_scales", "inv_coord_scales", "centroids", "decision_boundaries"):
+            out[p + name] = t2n(getattr(ad, name))
+        out[p + "bits"] = np.array(kw["bits"], np.int64)
+        out[p + "rotated"] = np.array("rotation" in kw)
+        for dn, dt in DT.items():
+            qk = ad.quantize(torch.from_numpy(kq).to(dt))
+            out[p + dn + "_indices"] = t2n(qk.indices)
+            out[p + dn + "_norms"] = t2n(qk.norms)
+            if dn == "fp32":
+                out[p + dn + "_dequant"] = t2n(ad.dequantize(qk))
+            qt = torch.from_numpy(qq).to(dt)
+            out[p + dn + "_scores"] = t2n(ad.attention_score(qt, qk, scale=D ** -0.5))
+    # calibration: c and rotation-or-identity by held-out logit MSE
+    calk = torch.from_numpy(syn.keys((512,), D, seed=64))
+    _, res = RotationAdapter.fit(D, 3, calq, calk, rotation=R, c_values=[1.0, 5.0, 20.0], device=cpu)
+    out["ra_fit_best"] = np.array([res["best_c"], float(res["best_use_rotation"])], np.float64)
+    out["ra_fit_lmse"] = np.array([r["lmse"] for r in res["all_results"]], np.float64)
+    # hybrid decode through a store keyed by the diagonal-metric strategy (bf16, GQA 4)
+    strat = SMAQDiagonalMetricStrategy(D, bits=4, Sigma_q=sig, rotation=R, device=cpu)
+    Hq, Hkv, nh, nr = 16, 4, 200, 40
+    hk = torch.from_numpy(syn.keys((nh, Hkv), D, seed=65)).to(torch.bfloat16)
+    hv = torch.from_numpy(syn.values((nh, Hkv), D, seed=66)).to(torch.bfloat16)
+    rk = torch.from_numpy(syn.keys((nr, Hkv), D, seed=67)).to(torch.bfloat16)
+    rv = torch.from_numpy(syn.values((nr, Hkv), D, seed=68)).to(torch.bfloat16)
+    q = torch.from_numpy(syn.queries((1, Hq), D, seed=69)).to(torch.bfloat16)
+    store = CompressedKVStore(D, Hkv, key_bits=4, device=cpu, key_strategy=strat)
+    store.append_chunk(hk[:70], hv[:70])
+    store.append_chunk(hk[70:], hv[70:])
+    o = compute_hybrid_attention(q, store, rk, rv, Hq)
+    flat = store.get_flat_cache()
+    p = "ra_hy_"
+    for name, t in (("hist_k", hk), ("recent_k", rk), ("recent_v", rv), ("q", q), ("out", o),
+                    ("key_indices", flat.key_q.indices), ("key_norms", flat.key_q.norms),
+                    ("v_data", flat.value_q.data), ("v_scales", flat.value_q.scales),
+                    ("v_zeros", flat.value_q.zeros), ("coord_scales", strat.quantizer.coord_scales),
+                    ("centroids", strat.quantizer.centroids),
+                    ("decision_boundaries", strat.quantizer.decision_boundaries)):
+        out[p + name] = t2n(t)
+    out[p + "meta"] = np.array([Hq, Hkv, nh, nr], np.int64)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SMAQ_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", choices=["all", "rotation"], default="all",
+                    help="rotation: write only golden_rotation.npz")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     import torch
+    if args.only in ("all", "rotation"):
+        import smaq  # the reference package
+        assert "reference" in smaq.__file__ or args.reference in smaq.__file__, smaq.__file__
+        rot = {}
+        rotation_goldens(rot)
+        path = os.path.join(HERE, "golden_rotation.npz")
+        np.savez_compressed(path, **rot)
+        print("wrote", path, os.path.getsize(path) // 1024, "KiB,", len(rot), "arrays")
+        if args.only == "rotation":
+            return
     torch.set_num_threads(os.cpu_count() or 1)
     import smaq  # the reference package
     from smaq.quantizer import SMAQQuantizer
