@@ -12,6 +12,7 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "ptx.cuh"
 #include "tc_rotate.cuh"
 
 namespace smaq {
@@ -134,7 +135,8 @@ __device__ __forceinline__ uint32_t bf2_pack(float lo, float hi) {
 
 __global__ void __launch_bounds__(256) value_bf16_g32_kernel(
     const __nv_bfloat16* __restrict__ v, int64_t n_tokens, int n_heads, int64_t st, int64_t sh, const RowMap rm,
-    uint8_t* __restrict__ data, __nv_bfloat16* __restrict__ scales, __nv_bfloat16* __restrict__ zeros, int layout) {
+    uint8_t* __restrict__ data, __nv_bfloat16* __restrict__ scales, __nv_bfloat16* __restrict__ zeros, int layout,
+    int after_keys) {
   const int64_t gid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t n_rows = n_tokens * n_heads;
   const int64_t r = gid >> 2;
@@ -203,6 +205,9 @@ __global__ void __launch_bounds__(256) value_bf16_g32_kernel(
     lo = __byte_perm(c01, c23, 0x6420);  // byte 2g of sources 0..3
     hi = __byte_perm(c01, c23, 0x7531);  // byte 2g + 1 of sources 0..3
   }
+  // launched overlapped with the key kernel of the same append: the last block waits for that
+  // grid, so this grid completes (and the stream moves on) only after both
+  if (after_keys && blockIdx.x == gridDim.x - 1) pdl_wait();
   if (!live) return;  // after the shuffles: whole rows are live or not, warps stay converged
   const int64_t row = rm.row(t, h);
   reinterpret_cast<uint2*>(data + row * 32)[g] = make_uint2(lo, hi);
@@ -518,19 +523,35 @@ static int launch_values_t(const smaq_append_args& a, cudaStream_t s) {
   return cuda_status(cudaGetLastError(), "value_quant_kernel");
 }
 
+// after_keys: the key kernel of the same append was launched just before on `s`; the fast bf16
+// value kernel then starts as its programmatic dependent and runs beside it (the key kernel
+// leaves room for one 128-thread block per SM).
 template <class DT>
-static int launch_values_d(const smaq_append_args& a, cudaStream_t s) {
+static int launch_values_d(const smaq_append_args& a, cudaStream_t s, int after_keys) {
   if constexpr (std::is_same<DT, BF16>::value) {
     if (a.head_dim == 128 && a.group_size == 32 && a.value_bits == 2 &&
         reinterpret_cast<uintptr_t>(a.v) % 16 == 0 && a.v_stride_t % 8 == 0 && a.v_stride_h % 8 == 0 &&
         reinterpret_cast<uintptr_t>(a.v_data) % 8 == 0) {
+      // 128-thread blocks: beside the key kernel (18 warps at 96 registers, 5/5/4/4 per SM
+      // sub-partition) only two sub-partitions have room, three 40-register warps each
       const int64_t threads = a.n_tokens * a.n_heads * 4;
-      const int64_t blocks = (threads + 255) / 256;
-      if (blocks > 0)
-        value_bf16_g32_kernel<<<unsigned(blocks), 256, 0, s>>>(
-            static_cast<const __nv_bfloat16*>(a.v), a.n_tokens, a.n_heads, a.v_stride_t, a.v_stride_h, make_rowmap(a),
-            a.v_data, static_cast<__nv_bfloat16*>(a.v_scales), static_cast<__nv_bfloat16*>(a.v_zeros), a.layout);
-      return cuda_status(cudaGetLastError(), "value_bf16_g32_kernel");
+      const int64_t blocks = (threads + 127) / 128;
+      if (blocks <= 0) return SMAQ_OK;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(unsigned(blocks));
+      cfg.blockDim = dim3(128);
+      cfg.stream = s;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = after_keys ? 1 : 0;
+      return cuda_status(
+          cudaLaunchKernelEx(&cfg, value_bf16_g32_kernel, static_cast<const __nv_bfloat16*>(a.v), a.n_tokens,
+                             a.n_heads, a.v_stride_t, a.v_stride_h, make_rowmap(a), a.v_data,
+                             static_cast<__nv_bfloat16*>(a.v_scales), static_cast<__nv_bfloat16*>(a.v_zeros),
+                             a.layout, after_keys),
+          "value_bf16_g32_kernel");
     }
   }
   switch (a.head_dim) {
@@ -607,17 +628,17 @@ static int launch_bvq_d(const smaq_append_args& a, cudaStream_t s) {
 }
 
 template <template <class> class F>
-static int by_dtype(int dtype, const smaq_append_args& a, cudaStream_t s) {
+static int by_dtype(int dtype, const smaq_append_args& a, cudaStream_t s, int after_keys = 0) {
   switch (dtype) {
-    case SMAQ_F32: return F<F32>::run(a, s);
-    case SMAQ_BF16: return F<BF16>::run(a, s);
-    case SMAQ_F16: return F<F16>::run(a, s);
+    case SMAQ_F32: return F<F32>::run(a, s, after_keys);
+    case SMAQ_BF16: return F<BF16>::run(a, s, after_keys);
+    case SMAQ_F16: return F<F16>::run(a, s, after_keys);
   }
   return fail(SMAQ_ERR_INVALID, "unknown dtype %d", dtype);
 }
-template <class DT> struct RunValues { static int run(const smaq_append_args& a, cudaStream_t s) { return launch_values_d<DT>(a, s); } };
-template <class DT> struct RunScalar { static int run(const smaq_append_args& a, cudaStream_t s) { return launch_scalar_d<DT>(a, s); } };
-template <class DT> struct RunBvq { static int run(const smaq_append_args& a, cudaStream_t s) { return launch_bvq_d<DT>(a, s); } };
+template <class DT> struct RunValues { static int run(const smaq_append_args& a, cudaStream_t s, int after_keys) { return launch_values_d<DT>(a, s, after_keys); } };
+template <class DT> struct RunScalar { static int run(const smaq_append_args& a, cudaStream_t s, int) { return launch_scalar_d<DT>(a, s); } };
+template <class DT> struct RunBvq { static int run(const smaq_append_args& a, cudaStream_t s, int) { return launch_bvq_d<DT>(a, s); } };
 
 static size_t dsize(int dtype) { return dtype == SMAQ_F32 ? 4 : 2; }
 
@@ -681,16 +702,15 @@ extern "C" int smaq_append(const smaq_append_args* args, void* stream) {
   if (st) return st;
   if (a.n_tokens == 0) return SMAQ_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (a.v) {
-    st = by_dtype<RunValues>(a.dtype, a, s);
-    if (st) return st;
-  }
+  // keys first: the value kernel may then run beside the (compute-bound) key kernel
   if (a.k) {
     if (a.key_format == SMAQ_KEYS_SCALAR)
       st = by_dtype<RunScalar>(a.dtype, a, s);
     else
       st = by_dtype<RunBvq>(a.dtype, a, s);
+    if (st) return st;
   }
+  if (a.v) st = by_dtype<RunValues>(a.dtype, a, s, a.k ? 1 : 0);
   return st;
 }
 

@@ -277,6 +277,8 @@ __global__ void __launch_bounds__(TR_THREADS, 1) tc_scalar_key_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n_rows = n_tokens * n_heads;
   const int tok_per_tile = TR_ROWS / n_heads;
+  // the append's value kernel (launched next, as a programmatic dependent) may start beside us
+  pdl_launch_dependents();
   const int64_t n_tiles = (n_tokens + tok_per_tile - 1) / tok_per_tile;
 
   // ---- E = E_hi + E_mid + E_lo in bf16 (each the bf16 rounding of what the previous ones
