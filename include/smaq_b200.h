@@ -76,6 +76,9 @@ enum {
 };
 
 int smaq_abi_version(void);
+/* No counterpart in the reference.  sizeof(smaq_append_args) for which = 0, sizeof(smaq_decode_args)
+ * for which = 1, else 0: a binding compares its own mirror of the structs with these. */
+size_t smaq_args_size(int which);
 const char* smaq_last_error(void);
 
 /* ------------------------------------------------------------------ append */

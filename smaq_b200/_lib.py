@@ -19,7 +19,7 @@ STATUS = {0: "OK", 1: "INVALID", 2: "UNSUPPORTED", 3: "CUDA", 4: "WORKSPACE", 5:
 
 # every symbol include/smaq_b200.h declares (checked by the CPU test suite)
 EXPORTS = (
-    "smaq_abi_version", "smaq_last_error", "smaq_append", "smaq_quantize_keys_scalar",
+    "smaq_abi_version", "smaq_args_size", "smaq_last_error", "smaq_append", "smaq_quantize_keys_scalar",
     "smaq_quantize_values", "smaq_quantize_keys_bvq", "smaq_decode_workspace_size", "smaq_decode",
     "smaq_merge_partials", "smaq_decode_noalloc", "smaq_decode_noalloc_max_workspace",
     "smaq_decode_status", "smaq_append_status", "smaq_selftest_wait_timeout",
@@ -73,6 +73,12 @@ def load() -> C.CDLL:
             "`python -m smaq_b200.build` (there is no CPU fallback)")
     lib = C.CDLL(path)
     lib.smaq_abi_version.restype = i32
+    lib.smaq_args_size.argtypes = [i32]
+    lib.smaq_args_size.restype = C.c_size_t
+    for which, mirror in ((0, AppendArgs), (1, DecodeArgs)):
+        if lib.smaq_args_size(which) != C.sizeof(mirror):
+            raise RuntimeError(f"{path}: {mirror.__name__} is {C.sizeof(mirror)} bytes here but "
+                               f"{lib.smaq_args_size(which)} in the library (stale build or ABI mismatch)")
     lib.smaq_last_error.restype = C.c_char_p
     lib.smaq_append.argtypes = [C.POINTER(AppendArgs), vp]
     lib.smaq_append.restype = i32

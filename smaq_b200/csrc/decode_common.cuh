@@ -6,8 +6,13 @@ namespace smaq {
 
 constexpr int DEC_WARPS = 8;
 constexpr int DEC_THREADS = DEC_WARPS * 32;
-constexpr int RECENT_COST = 8;
-constexpr int DEC_MAX_CTAS_PER_SM = 8;  // grid cap when the caller lets the library choose  // exact bf16 K+V token = 512 B vs 48-114 B for a compressed token
+// Partition weight of one exact-window token in units of one compressed token-head (an exact
+// bf16 K+V token is 512 B against 48-114 B for a compressed one)
+#ifndef SMAQ_RECENT_COST
+#define SMAQ_RECENT_COST 8
+#endif
+constexpr int RECENT_COST = SMAQ_RECENT_COST;
+constexpr int DEC_MAX_CTAS_PER_SM = 8;  // grid cap when the caller lets the library choose
 
 struct DecodeParams {
   const void* q;

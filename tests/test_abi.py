@@ -23,6 +23,15 @@ def test_library_exports_header_symbols():
     assert lib.smaq_abi_version() == 2
 
 
+def test_struct_mirrors_match_the_library():
+    import ctypes
+    from smaq_b200 import _lib
+    lib = _lib.load()  # also raises on a mismatch
+    assert lib.smaq_args_size(0) == ctypes.sizeof(_lib.AppendArgs)
+    assert lib.smaq_args_size(1) == ctypes.sizeof(_lib.DecodeArgs)
+    assert lib.smaq_args_size(2) == 0
+
+
 def test_invalid_arguments_are_reported_without_a_gpu():
     """Argument validation runs on the host and fails with a message, before any CUDA call."""
     import ctypes
