@@ -114,10 +114,13 @@ def rotation_goldens(out):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("SMAQ_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("SMAQ_REFERENCE"),
+                    help="checkout of gauravsaini/smaq (or set SMAQ_REFERENCE)")
     ap.add_argument("--only", choices=["all", "rotation"], default="all",
                     help="rotation: write only golden_rotation.npz")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference PATH (or SMAQ_REFERENCE) is required")
     sys.path.insert(0, args.reference)
     import torch
     if args.only in ("all", "rotation"):
@@ -188,6 +191,9 @@ def main():
     calk = syn.keys((4096,), D, seed=11)
     vq = SMAQBlockVQ(D, device=torch.device("cpu"))
     vq.fit(torch.from_numpy(calk), torch.from_numpy(syn.calibration_queries(4096, D, seed=12)))
+    # the fitted tables as the reference's k-means produced them (before any rounding)
+    for name in ("E_blocks", "E_inv_blocks", "centroids", "decoded_centroids"):
+        out["bvq_fit_" + name] = t2n(getattr(vq, name)).copy()
     # fp16 codebook: reference buffers rounded to fp16-representable values
     for name in ("E_blocks", "E_inv_blocks", "centroids", "decoded_centroids"):
         getattr(vq, name).copy_(getattr(vq, name).half().float())
@@ -266,6 +272,8 @@ def main():
     bstrat.quantizer = vq
     run_case("bvq_bf16", bstrat, 32, 8, 400, 128, torch.bfloat16, torch.bfloat16, torch.bfloat16, 400)
     run_case("bvq_fp32", bstrat, 8, 2, 150, 10, torch.float32, torch.float32, torch.float32, 410)
+    # bf16 block VQ with the raw history kept (fits the fixture): replayed through the store
+    run_case("bvq_bf16_store", bstrat, 16, 4, 300, 64, torch.bfloat16, torch.bfloat16, torch.bfloat16, 420)
 
     # ---------------- capture engine flush pattern (RingBuffer, F13) ---------
     store = CompressedKVStore(D, 2, key_bits=3, device=torch.device("cpu"))
