@@ -197,6 +197,14 @@ size_t smaq_decode_workspace_size(int batch, int n_q_heads, int n_kv_heads, int 
                                   int num_ctas);
 int smaq_decode(const smaq_decode_args* args, void* stream);
 
+/* No counterpart in the reference (it has one implementation).  The kernel path smaq_decode
+ * takes for these arguments, without launching anything: SMAQ_PATH_FUSED_BVQ (one launch,
+ * block-VQ keys, tensor-core scores and P.V), SMAQ_PATH_FUSED_SCALAR (one launch, 3/4-bit
+ * scalar keys, tensor-core scores and P.V) or SMAQ_PATH_GENERAL (partition, SIMT decode and
+ * merge launches: every other supported format); a negative status for invalid arguments. */
+enum { SMAQ_PATH_GENERAL = 0, SMAQ_PATH_FUSED_BVQ = 1, SMAQ_PATH_FUSED_SCALAR = 2 };
+int smaq_decode_kernel_path(const smaq_decode_args* args);
+
 /* No counterpart in the reference.  smaq_decode without a caller workspace, for callers that
  * cannot allocate device memory (all device memory owned by another allocator or pool, or a
  * host that reaches the GPU only through this ABI).  Scratch comes from a fixed 8 MiB array in

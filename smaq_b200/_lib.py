@@ -21,6 +21,7 @@ STATUS = {0: "OK", 1: "INVALID", 2: "UNSUPPORTED", 3: "CUDA", 4: "WORKSPACE", 5:
 EXPORTS = (
     "smaq_abi_version", "smaq_args_size", "smaq_last_error", "smaq_append", "smaq_quantize_keys_scalar",
     "smaq_quantize_values", "smaq_quantize_keys_bvq", "smaq_decode_workspace_size", "smaq_decode",
+    "smaq_decode_kernel_path",
     "smaq_merge_partials", "smaq_decode_noalloc", "smaq_decode_noalloc_max_workspace",
     "smaq_decode_status", "smaq_append_status", "smaq_selftest_wait_timeout",
 )
@@ -66,7 +67,7 @@ def load() -> C.CDLL:
     global _lib
     if _lib is not None:
         return _lib
-    path = os.environ.get("SMAQ_B200_LIB", LIB_PATH)  # an alternate build of the same library
+    path = LIB_PATH
     if not os.path.exists(path):
         raise RuntimeError(
             f"smaq_b200 CUDA library not found at {path}; build it with "
@@ -92,6 +93,8 @@ def load() -> C.CDLL:
     lib.smaq_decode_workspace_size.restype = C.c_size_t
     lib.smaq_decode.argtypes = [C.POINTER(DecodeArgs), vp]
     lib.smaq_decode.restype = i32
+    lib.smaq_decode_kernel_path.argtypes = [C.POINTER(DecodeArgs)]
+    lib.smaq_decode_kernel_path.restype = i32
     lib.smaq_merge_partials.argtypes = [vp, i32, i32, i32, i32, vp, i32, i64, i64, vp]
     lib.smaq_merge_partials.restype = i32
     lib.smaq_decode_noalloc.argtypes = [C.POINTER(DecodeArgs), vp]

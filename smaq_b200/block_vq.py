@@ -85,6 +85,16 @@ class SMAQBlockVQ(nn.Module):
         self.register_buffer("centroids", z.clone())
         self.register_buffer("decoded_centroids", z.clone())
         self._fitted = False
+        self._cb16 = (None, None)
+
+    def fp16_codebook(self) -> Optional[torch.Tensor]:
+        """The decoded centroids as fp16 when they are exactly fp16-valued (then the decode runs
+        the tensor-core kernel), else None.  Recomputed only when the table changed."""
+        t = self.decoded_centroids
+        key = (t.data_ptr(), t._version, t.device)
+        if self._cb16[0] != key:
+            self._cb16 = (key, ops.fp16_codebook(t) if t.is_cuda else None)
+        return self._cb16[1]
 
     @property
     def bits_per_dim(self) -> float:

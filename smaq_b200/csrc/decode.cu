@@ -191,16 +191,22 @@ __global__ void __launch_bounds__(DEC_THREADS) decode_kernel(DecodeParams p) {
 #pragma unroll
             for (int g = 0; g < GM; ++g) a[g] = 0.f;
             const uint8_t* crow = p.kcodes + row * PD;
+            uint4 wrow[PD / 16];
+#pragma unroll
+            for (int q4 = 0; q4 < PD / 16; ++q4) wrow[q4] = __ldg(reinterpret_cast<const uint4*>(crow + q4 * 16));
+            const uint8_t* rowb = reinterpret_cast<const uint8_t*>(wrow);
+            // SMAQ_LAYOUT_DECODE (3/4-bit, 64-byte rows): reference byte pb sits at 16 (pb % 4) + pb / 4
+            const bool perm = PD == 64 && p.layout == SMAQ_LAYOUT_DECODE;
 #pragma unroll
             for (int q4 = 0; q4 < PD / 16; ++q4) {
-              const uint4 w = __ldg(reinterpret_cast<const uint4*>(crow + q4 * 16));
-              const uint8_t* by = reinterpret_cast<const uint8_t*>(&w);
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
+                const int pb = q4 * 16 + j;
+                const uint32_t byv = perm ? rowb[(16 * (pb & 3) + (pb >> 2)) & (PD - 1)] : rowb[pb];
 #pragma unroll
                 for (int v = 0; v < VPB; ++v) {
                   const int d = (q4 * 16 + j) * VPB + v;
-                  const float cv = cent[(by[j] >> (v * KB)) & MASK];
+                  const float cv = cent[(byv >> (v * KB)) & MASK];
 #pragma unroll
                   for (int g = 0; g < GM; ++g) {
                     if (g >= G) break;
@@ -430,7 +436,9 @@ extern "C" size_t smaq_decode_workspace_size(int batch, int n_q_heads, int n_kv_
   return plan_bytes(n_seg) + sizeof(float) * size_t(grid + n_seg) * G * (head_dim + 2);
 }
 
-extern "C" int smaq_decode(const smaq_decode_args* args, void* stream) {
+namespace smaq {
+// Validate the arguments and fill the kernel parameters (no CUDA call).
+static int decode_params(const smaq_decode_args* args, DecodeParams& p, int& kb) {
   if (!args) return fail(SMAQ_ERR_INVALID, "decode: null args");
   const smaq_decode_args& a = *args;
   if (a.batch <= 0 || a.n_q_heads <= 0 || a.n_kv_heads <= 0 || a.n_q_heads % a.n_kv_heads)
@@ -440,7 +448,7 @@ extern "C" int smaq_decode(const smaq_decode_args* args, void* stream) {
   if (!a.out && !a.partial_out) return fail(SMAQ_ERR_INVALID, "decode: no output");
   if (!a.q || !a.hist_len) return fail(SMAQ_ERR_INVALID, "decode: null query or hist_len");
   if (a.page_size <= 0) return fail(SMAQ_ERR_INVALID, "decode: page_size must be > 0");
-  int kb = 0;
+  kb = 0;
   if (a.key_format == SMAQ_KEYS_SCALAR) {
     if (a.key_bits < 2 || a.key_bits > 4) return fail(SMAQ_ERR_UNSUPPORTED, "decode: key bits %d", a.key_bits);
     if (!a.E_inv || !a.centroids || !a.key_codes || !a.key_norms)
@@ -461,7 +469,7 @@ extern "C" int smaq_decode(const smaq_decode_args* args, void* stream) {
   if ((reinterpret_cast<uintptr_t>(a.key_codes) & 15) || (reinterpret_cast<uintptr_t>(a.v_data) & 3))
     return fail(SMAQ_ERR_INVALID, "decode: key codes must be 16-byte aligned");
 
-  DecodeParams p = {};
+  p = DecodeParams{};
   p.q = a.q;
   p.q_dtype = a.q_dtype;
   p.q_sb = a.q_stride_b;
@@ -498,9 +506,35 @@ extern "C" int smaq_decode(const smaq_decode_args* args, void* stream) {
   p.n_seg = 2 * a.batch * a.n_kv_heads;
   p.layout = a.layout;
   p.cent16 = a.key_format == SMAQ_KEYS_BVQ ? static_cast<const uint16_t*>(a.centroids_f16) : nullptr;
+  return SMAQ_OK;
+}
+
+// Which kernel path smaq_decode takes for these arguments (see smaq_decode_kernel_path).
+static int decode_path(const DecodeParams& p, int kb, int value_bits) {
+  if (kb == 0 && decode_v2_eligible(p, SMAQ_KEYS_BVQ, value_bits, p.q_dtype) &&
+      p.n_seg <= decode_v2_max_fused_segments(p.G))
+    return SMAQ_PATH_FUSED_BVQ;
+  if (kb != 0 && decode_s_eligible(p, kb, value_bits)) return SMAQ_PATH_FUSED_SCALAR;
+  return SMAQ_PATH_GENERAL;
+}
+}  // namespace smaq
+
+extern "C" int smaq_decode_kernel_path(const smaq_decode_args* args) {
+  DecodeParams p;
+  int kb = 0;
+  const int st = decode_params(args, p, kb);
+  return st ? -st : decode_path(p, kb, args->value_bits);
+}
+
+extern "C" int smaq_decode(const smaq_decode_args* args, void* stream) {
+  DecodeParams p;
+  int kb = 0;
+  int st = decode_params(args, p, kb);
+  if (st) return st;
+  const smaq_decode_args& a = *args;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int grid = 0;
-  int st = dispatch_decode(p, kb, a.value_bits, a.num_ctas, s, &grid, true);
+  st = dispatch_decode(p, kb, a.value_bits, a.num_ctas, s, &grid, true);
   if (st) return st;
   const size_t need = plan_bytes(p.n_seg) + sizeof(float) * size_t(grid + p.n_seg) * p.G * (p.D + 2);
   if (!a.workspace || a.workspace_bytes < need)
@@ -509,9 +543,7 @@ extern "C" int smaq_decode(const smaq_decode_args* args, void* stream) {
   p.pair_cnt = reinterpret_cast<uint64_t*>(static_cast<char*>(a.workspace) + plan_table_bytes(p.n_seg));
   p.slots = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + plan_bytes(p.n_seg));
   p.grid = grid;
-  if ((kb == 0 && decode_v2_eligible(p, SMAQ_KEYS_BVQ, a.value_bits, p.q_dtype) &&
-       p.n_seg <= decode_v2_max_fused_segments(p.G)) ||
-      (kb != 0 && decode_s_eligible(p, kb, a.value_bits))) {
+  if (decode_path(p, kb, a.value_bits) != SMAQ_PATH_GENERAL) {
     // one launch: partition, history, window and the per-pair merge in the tensor-core kernel
     static std::atomic<uint32_t> epochs{0};
     uint32_t e = ++epochs;

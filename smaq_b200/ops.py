@@ -20,6 +20,7 @@ from smaq_b200._lib import (SMAQ_BF16, SMAQ_F16, SMAQ_F32, SMAQ_KEYS_BVQ, SMAQ_K
 _DT = {torch.float32: SMAQ_F32, torch.bfloat16: SMAQ_BF16, torch.float16: SMAQ_F16}
 
 MIN_HISTORY = 16
+PATH_GENERAL, PATH_FUSED_BVQ, PATH_FUSED_SCALAR = 0, 1, 2   # smaq_decode_kernel_path
 
 
 def dtype_code(dt: torch.dtype) -> int:
@@ -184,7 +185,7 @@ def decode(q: torch.Tensor, *, n_kv_heads: int, key_format: int, key_codes: torc
            partial_out: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
            num_ctas: int = 0, want_out: bool = True, layout: int = SMAQ_LAYOUT_REFERENCE,
            centroids_f16: Optional[torch.Tensor] = None, entry: str = "smaq_decode",
-           overlap_prior: bool = False) -> Optional[torch.Tensor]:
+           overlap_prior: bool = False, query_path: bool = False):
     """Batched hybrid decode attention.
 
     ``q``: ``[B, Hq, D]``.  History streams are store rows ``[pages, Hkv, page_size, ...]``;
@@ -193,6 +194,8 @@ def decode(q: torch.Tensor, *, n_kv_heads: int, key_format: int, key_codes: torc
     ``overlap_prior``: overlap the launch with the end of the previous kernel on the stream
     (programmatic dependent launch); only when that kernel writes none of the history rows,
     block table, lengths or codebooks (``smaq_decode_args.overlap_prior``).
+    ``query_path``: launch nothing and return the kernel path these arguments select
+    (``PATH_FUSED_BVQ``, ``PATH_FUSED_SCALAR`` or ``PATH_GENERAL``, smaq_decode_kernel_path).
     """
     _cuda(q, key_codes, v_data, hist_len, recent_k, block_table)
     lib = _lib.load()
@@ -201,7 +204,7 @@ def decode(q: torch.Tensor, *, n_kv_heads: int, key_format: int, key_codes: torc
         q = q.contiguous()
     if scale is None:
         scale = 1.0 / math.sqrt(D)
-    if out is None and want_out:
+    if out is None and want_out and not query_path:
         out = torch.empty((B, Hq, D), dtype=q.dtype, device=q.device)
     keep = [q]
     a = _lib.DecodeArgs()
@@ -255,7 +258,7 @@ def decode(q: torch.Tensor, *, n_kv_heads: int, key_format: int, key_codes: torc
         a.out, a.o_stride_b, a.o_stride_h = out.data_ptr(), out.stride(0), out.stride(1)
     if partial_out is not None:
         a.partial_out = partial_out.data_ptr()
-    if entry != "smaq_decode_noalloc":
+    if entry != "smaq_decode_noalloc" and not query_path:
         need = decode_workspace_bytes(B, Hq, n_kv_heads, D, num_ctas)
         if workspace is None or workspace.numel() < need:
             workspace = torch.empty((max(need, 256),), dtype=torch.uint8, device=q.device)
@@ -268,6 +271,13 @@ def decode(q: torch.Tensor, *, n_kv_heads: int, key_format: int, key_codes: torc
         c16 = centroids_f16.to(torch.float16).contiguous()
         keep.append(c16)
         a.centroids_f16 = c16.data_ptr()
+    if query_path:
+        if out is None and partial_out is None:
+            a.out = 1  # any non-null output: only the kernel choice is asked for
+        st = lib.smaq_decode_kernel_path(a)
+        if st < 0:
+            _lib.check(-st, "smaq_decode_kernel_path")
+        return st
     if entry == "smaq_decode_noalloc":
         # fixed scratch inside the library: no workspace is passed (see include/smaq_b200.h)
         a.workspace, a.workspace_bytes = None, 0

@@ -23,10 +23,9 @@ from smaq_b200.store import CompressedKVStore
 MIN_HISTORY_FOR_SMAQ = 16
 
 
-def compute_hybrid_attention(query: torch.Tensor, store: CompressedKVStore, recent_k: Optional[torch.Tensor],
-                             recent_v: Optional[torch.Tensor], num_query_heads: int,
-                             scale: Optional[float] = None) -> torch.Tensor:
-    """``query [T, Hq, D]`` -> ``[T, Hq, D]`` in the query dtype."""
+def _decode_call(query: torch.Tensor, store: CompressedKVStore, recent_k: Optional[torch.Tensor],
+                 recent_v: Optional[torch.Tensor], num_query_heads: int, scale: Optional[float]):
+    """The ``ops.decode`` arguments of one compute_hybrid_attention call (None: nothing to attend)."""
     ops._cuda(query, recent_k, recent_v)
     D = store.head_dim
     Hkv = store.num_kv_heads
@@ -37,7 +36,7 @@ def compute_hybrid_attention(query: torch.Tensor, store: CompressedKVStore, rece
     has_hist = n >= MIN_HISTORY_FOR_SMAQ
     has_recent = recent_k is not None and recent_k.shape[0] > 0
     if not has_hist and not has_recent:
-        return torch.zeros(T, num_query_heads, D, device=query.device, dtype=query.dtype)
+        return None
     dev = query.device
     q = query.reshape(T, num_query_heads, D)
     if store.capacity == 0:
@@ -53,7 +52,8 @@ def compute_hybrid_attention(query: torch.Tensor, store: CompressedKVStore, rece
         qz = strat.quantizer
         kw = dict(key_bits=strat.bits, E_inv=qz.E_inv, centroids=qz.centroids, key_norms=view["norms"])
     else:
-        kw = dict(centroids=strat.quantizer.decoded_centroids)
+        # an fp16-valued codebook selects the tensor-core block-VQ kernel (decode-layout rows)
+        kw = dict(centroids=strat.quantizer.decoded_centroids, centroids_f16=strat.quantizer.fp16_codebook())
     if has_recent:
         W = recent_k.shape[0]
         rk = recent_k.reshape(1, W, Hkv, D).expand(T, W, Hkv, D)
@@ -61,11 +61,34 @@ def compute_hybrid_attention(query: torch.Tensor, store: CompressedKVStore, rece
         rl = torch.full((T,), W, dtype=torch.int32, device=dev)
     else:
         rk = rv = rl = None
-    return ops.decode(q, n_kv_heads=Hkv, key_format=store.key_format, key_codes=view["codes"],
-                      v_data=view["vdata"], v_scales=view["vscales"], v_zeros=view["vzeros"], hist_len=hist,
-                      page_size=view["page_size"], block_table=bt, value_bits=store.value_bits,
-                      group_size=store.value_group_size, recent_k=rk, recent_v=rv, recent_len=rl, scale=scale,
-                      min_history=MIN_HISTORY_FOR_SMAQ, **kw)
+    return q, dict(n_kv_heads=Hkv, key_format=store.key_format, key_codes=view["codes"], v_data=view["vdata"],
+                   v_scales=view["vscales"], v_zeros=view["vzeros"], hist_len=hist, page_size=view["page_size"],
+                   block_table=bt, value_bits=store.value_bits, group_size=store.value_group_size, recent_k=rk,
+                   recent_v=rv, recent_len=rl, scale=scale, min_history=MIN_HISTORY_FOR_SMAQ,
+                   layout=view["layout"], **kw)
+
+
+def compute_hybrid_attention(query: torch.Tensor, store: CompressedKVStore, recent_k: Optional[torch.Tensor],
+                             recent_v: Optional[torch.Tensor], num_query_heads: int,
+                             scale: Optional[float] = None) -> torch.Tensor:
+    """``query [T, Hq, D]`` -> ``[T, Hq, D]`` in the query dtype."""
+    call = _decode_call(query, store, recent_k, recent_v, num_query_heads, scale)
+    if call is None:
+        return torch.zeros(query.shape[0], num_query_heads, store.head_dim, device=query.device, dtype=query.dtype)
+    q, kw = call
+    return ops.decode(q, **kw)
+
+
+def hybrid_kernel_path(query: torch.Tensor, store: CompressedKVStore, recent_k: Optional[torch.Tensor],
+                       recent_v: Optional[torch.Tensor], num_query_heads: int,
+                       scale: Optional[float] = None) -> Optional[int]:
+    """The decode kernel path compute_hybrid_attention would run for these arguments
+    (``ops.PATH_*``; None when there is nothing to attend).  Launches nothing."""
+    call = _decode_call(query, store, recent_k, recent_v, num_query_heads, scale)
+    if call is None:
+        return None
+    q, kw = call
+    return ops.decode(q, query_path=True, **kw)
 
 
 class HybridAttentionBackend(AttentionBackend):

@@ -6,9 +6,12 @@ store rows ``[Hkv, capacity, row]`` (one page of ``capacity`` tokens per head, s
 include/smaq_b200.h), and ``append_chunk`` quantizes straight into rows ``n .. n+T`` with one
 ``smaq_append`` launch.  Block-VQ indices are kept as uint8 (the reference keeps int64).
 
-``get_flat_cache`` still returns the reference's logical view: ``SMAQQuantized`` /
-``BlockVQQuantized`` plus ``ValueQuantized`` with ``[Hkv, N, ...]`` shapes (the block-VQ
-indices converted to int64 on request).
+Rows use ``SMAQ_LAYOUT_DECODE`` (the reference's bytes permuted inside each row, see
+include/smaq_b200.h) whenever the format has a fast decode kernel: bf16 keys/values, head_dim
+128, 2-bit values in groups of 32, and 3/4-bit scalar keys or 8-dim block-VQ keys.  Other
+formats keep the reference byte order.  ``get_flat_cache`` always returns the reference's
+logical view: ``SMAQQuantized`` / ``BlockVQQuantized`` plus ``ValueQuantized`` with
+``[Hkv, N, ...]`` shapes in the reference byte order (block-VQ indices as int64).
 """
 
 from __future__ import annotations
@@ -18,7 +21,7 @@ from typing import Any, NamedTuple, Optional
 import torch
 
 from smaq_b200 import ops
-from smaq_b200._lib import SMAQ_KEYS_BVQ, SMAQ_KEYS_SCALAR
+from smaq_b200._lib import SMAQ_KEYS_BVQ, SMAQ_KEYS_SCALAR, SMAQ_LAYOUT_DECODE, SMAQ_LAYOUT_REFERENCE
 from smaq_b200.block_vq import BlockVQQuantized
 from smaq_b200.calibration import IdentityCalibrationProvider
 from smaq_b200.core import CacheCapabilities, CalibrationProvider
@@ -75,6 +78,7 @@ class CompressedKVStore:
         self._dtype: Optional[torch.dtype] = None
         self._buf: dict[str, torch.Tensor] = {}
         self._flat: Optional[FlatCache] = None
+        self.layout = SMAQ_LAYOUT_REFERENCE
 
     # ------------------------------------------------------------------ bookkeeping
     @property
@@ -115,13 +119,23 @@ class CompressedKVStore:
             b["norms"] = torch.empty((H, cap), dtype=dtype, device=dev)
         return b
 
+    def _decode_layout_ok(self, dtype: torch.dtype) -> bool:
+        """True when the rows can use the fast decode kernels' byte order."""
+        if dtype != torch.bfloat16 or self.head_dim != 128 or self.value_bits != 2 or self.value_group_size != 32:
+            return False
+        if self.key_format == SMAQ_KEYS_SCALAR:
+            return self.key_strategy.bits in (3, 4)
+        return self.key_strategy.quantizer.block_dim == 8
+
     def _reserve(self, n_new: int, dtype: torch.dtype):
         if self._dtype is None:
             self._dtype = dtype
+            self.layout = SMAQ_LAYOUT_DECODE if self._decode_layout_ok(dtype) else SMAQ_LAYOUT_REFERENCE
         need = self._n + n_new
         if need <= self._cap:
             return
         cap = max(need, 2 * self._cap, self._initial_capacity)
+        cap = (cap + 15) // 16 * 16   # decode-layout pages hold a multiple of 16 rows
         nb = self._alloc(cap, self._dtype)
         if self._n:
             for k, t in self._buf.items():
@@ -151,14 +165,16 @@ class CompressedKVStore:
                 kw = dict(key_format=SMAQ_KEYS_BVQ, E_blocks=qz.E_blocks, centroids=qz.centroids)
             ops.append(key, value, n_heads=self.num_kv_heads, slot_offset=self._n, page_size=self._cap,
                        key_codes=self._buf["codes"], value_bits=self.value_bits, group_size=self.value_group_size,
-                       v_data=self._buf["vdata"], v_scales=self._buf["vscales"], v_zeros=self._buf["vzeros"], **kw)
+                       v_data=self._buf["vdata"], v_scales=self._buf["vscales"], v_zeros=self._buf["vzeros"],
+                       layout=self.layout, **kw)
         self._n += T
         self._chunk_lengths.append(T)
         self._flat = None
 
     def kernel_view(self) -> dict:
         """Raw device rows for the decode kernel: streams shaped ``[1, Hkv, capacity, ...]``."""
-        return {k: v.unsqueeze(0) for k, v in self._buf.items()} | {"page_size": self._cap, "n": self._n}
+        return {k: v.unsqueeze(0) for k, v in self._buf.items()} | {"page_size": self._cap, "n": self._n,
+                                                                      "layout": self.layout}
 
     def get_flat_cache(self) -> Optional[FlatCache]:
         if self._n == 0:
@@ -166,14 +182,20 @@ class CompressedKVStore:
         if self._flat is not None:
             return self._flat
         n, b = self._n, self._buf
+        dec = self.layout == SMAQ_LAYOUT_DECODE
+        codes, vdata = b["codes"][:, :n], b["vdata"][:, :n]
         if self.key_format == SMAQ_KEYS_SCALAR:
-            kq = SMAQQuantized(indices=b["codes"][:, :n], norms=b["norms"][:, :n], bits=self.key_strategy.bits)
+            if dec:
+                codes = ops.scalar_codes_to_reference(codes)
+            kq = SMAQQuantized(indices=codes, norms=b["norms"][:, :n], bits=self.key_strategy.bits)
         else:
             qz = self.key_strategy.quantizer
-            kq = BlockVQQuantized(indices=b["codes"][:, :n].to(torch.int64), n_blocks=qz.n_blocks,
-                                  block_dim=qz.block_dim)
-        vq = ValueQuantized(data=b["vdata"][:, :n], scales=b["vscales"][:, :n], zeros=b["vzeros"][:, :n],
-                            bits=self.value_bits)
+            if dec:
+                codes = ops.bvq_to_reference(codes)
+            kq = BlockVQQuantized(indices=codes.to(torch.int64), n_blocks=qz.n_blocks, block_dim=qz.block_dim)
+        if dec:
+            vdata = ops.values_to_reference(vdata)
+        vq = ValueQuantized(data=vdata, scales=b["vscales"][:, :n], zeros=b["vzeros"][:, :n], bits=self.value_bits)
         self._flat = FlatCache(key_q=kq, value_q=vq, num_tokens=n)
         return self._flat
 

@@ -63,3 +63,28 @@ def test_status_calls_validate_without_a_gpu():
     lib = _lib.load()
     assert lib.smaq_decode_status(None, 0, 2, None) == 1
     assert b"bad sizes" in lib.smaq_last_error()
+
+
+def test_kernel_path_query_without_a_gpu():
+    """smaq_decode_kernel_path picks the fused kernels for their formats and the general path
+    otherwise; it validates like smaq_decode and launches nothing."""
+    from smaq_b200 import _lib, ops
+    lib = _lib.load()
+    d = _lib.DecodeArgs()
+    d.q, d.q_dtype, d.batch, d.n_q_heads, d.n_kv_heads, d.head_dim = 4096, _lib.SMAQ_BF16, 2, 32, 8, 128
+    d.key_codes, d.v_data, d.v_scales, d.v_zeros, d.hist_len, d.out = 4096, 8192, 12288, 16384, 20480, 24576
+    d.value_bits, d.group_size, d.page_size, d.kv_dtype = 2, 32, 1024, _lib.SMAQ_BF16
+    d.key_format, d.block_dim, d.n_centroids, d.centroids = _lib.SMAQ_KEYS_BVQ, 8, 256, 28672
+    d.layout = _lib.SMAQ_LAYOUT_DECODE
+    assert lib.smaq_decode_kernel_path(d) == ops.PATH_GENERAL      # no fp16 codebook given
+    d.centroids_f16 = 32768
+    assert lib.smaq_decode_kernel_path(d) == ops.PATH_FUSED_BVQ
+    d.layout = _lib.SMAQ_LAYOUT_REFERENCE
+    assert lib.smaq_decode_kernel_path(d) == ops.PATH_GENERAL
+    d.layout = _lib.SMAQ_LAYOUT_DECODE
+    d.key_format, d.key_bits, d.E_inv, d.key_norms = _lib.SMAQ_KEYS_SCALAR, 4, 36864, 40960
+    assert lib.smaq_decode_kernel_path(d) == ops.PATH_FUSED_SCALAR
+    d.q_dtype = _lib.SMAQ_F32
+    assert lib.smaq_decode_kernel_path(d) == ops.PATH_GENERAL
+    d.n_q_heads = 33
+    assert lib.smaq_decode_kernel_path(d) == -1                     # invalid head counts
