@@ -1,38 +1,47 @@
 """Benchmark: compressed-KV decode attention (SMAQ hot path) on B200.
 
-Default workload: Llama-3-8B KV shape -- 32 layers, 32 query / 8 KV
-heads, head_dim 128, bf16 -- batch 16 sequences x 32768 compressed history tokens (block-VQ
-keys: 8-dim blocks, 256-entry fp16-valued codebook k-means-fit on 16K calibration keys; 2-bit
-values in groups of 32) plus a 128-token exact bf16 window, one decode token per sequence.
-A step = the attention of all 32 layers for one decode token of every sequence.
+Default workload: Llama-3-70B KV shape -- 80 layers, 64 query / 8 KV
+heads, head_dim 128, bf16 -- 4 sequences x 131072 compressed history tokens (block-VQ keys:
+8-dim blocks, 256-entry fp16-valued codebook k-means-fit on 16K calibration keys; 2-bit values
+in groups of 32) plus a 128-token exact bf16 window, one decode token per sequence.  A step is
+the attention of all 80 layers for one decode token of every sequence.  With N ranks the KV
+heads are split over the ranks (N <= 8, no collective: each rank's query heads only read its
+own KV heads), so the total work is fixed: ``scaling: strong``.  At N = 1 the line also carries
+``cfg1``: configs[1] (Llama-3-8B, 32 layers, 32/8 heads, 16 x 32768 tokens) measured the same
+way, the 32K-context point of the metric.
 
-    python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--workload append]
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--workload W]
 
-``--workload paged`` measures configs[3] (Qwen2.5-7B KV shape, 64 sequences of 1K-64K tokens in
-a 16-token paged store, 4-bit scalar keys, 64-token window); ``--workload longctx`` configs[4]
-(Llama-3-70B KV shape, 4 x 128K, KV heads sharded over the ranks, strong scaling).
-``--workload append`` measures BASELINE.json configs[2] instead: a batch of 8 x 8192 new tokens x
-8 KV heads x head_dim 128 in bf16 quantized into store rows (tcgen05 rotation + 3-bit scalar key
-codes, 2-bit values in groups of 32); GB/s counts input plus output bytes.
+``--workload decode`` is configs[1] alone (N > 1: every rank serves its own 16 sequences,
+``scaling: weak``); ``--workload paged`` is configs[3] (Qwen2.5-7B KV shape, 64 sequences of
+1K-64K tokens in a 16-token paged store, 4-bit scalar keys, 64-token window); ``--workload
+append`` is configs[2] (8 x 8192 new tokens x 8 KV heads quantized into store rows: tcgen05
+rotation + 3-bit scalar key codes, 2-bit values; GB/s counts input plus output bytes).
 
-N > 1 (torchrun, one rank per GPU): every rank serves its own 16 sequences (sequences are
-independent units; no collective on the data path) -> ``scaling: weak``.
+Timing: every decode step (one ``smaq_decode`` call per layer through ``smaq_b200.ops.decode``,
+each one kernel launch) is captured once in a CUDA graph and replayed; CUDA events on the
+replay stream bracket the K timed steps.  ``e2e`` replays a second graph whose every layer
+also copies that layer's query rows host -> device (pinned) before its decode and its output
+rows device -> host after it.  The KV cache of one step is far larger than L2 (126 MB), so no
+L2 flush is needed between steps.
 
-Inputs: seeded synthetic data with the spectral key distribution (no dataset).  The KV cache
-of one step (8.9 GB) is far larger than L2 (126 MB), so no explicit L2 flush is needed.
+``--impl reference`` times the reference implementation itself (gauravsaini/smaq, installed
+unmodified under baseline/_ref) on the host CPU: ``compute_hybrid_attention`` over a
+``CompressedKVStore`` holding one sequence of the workload, all host threads, scaled to the
+step.  Inputs: seeded synthetic data with the spectral key distribution (no dataset).
 """
 
 from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess
 import sys
 import tempfile
 import time
+from dataclasses import dataclass, field
 
 import numpy as np
 
@@ -40,53 +49,91 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 METRIC = "compressed-KV decode attn tokens/s & HBM GB/s (% of roofline) at 32K/128K ctx"
+REF_DIR = os.path.join(REPO, "baseline", "_ref")
+
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the decode kernel,
+# read from one ncu capture of the same kernel on the same per-launch shape; keyed by
+# (batch, history tokens, window, query heads, kv heads) of one launch.
+NCU_TRAFFIC: dict = {}
 
 
-def parse():
+def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="smaq_b200", choices=["smaq_b200", "reference"])
-    ap.add_argument("--batch", type=int, default=16)
-    ap.add_argument("--ctx", type=int, default=32768)
-    ap.add_argument("--layers", type=int, default=32)
-    ap.add_argument("--window", type=int, default=128)
-    ap.add_argument("--hq", type=int, default=32)
-    ap.add_argument("--hkv", type=int, default=8)
+    ap.add_argument("--workload", default="longctx", choices=["longctx", "decode", "append", "paged"])
+    ap.add_argument("--layers", type=int, default=0, help="build fewer layers (profiling runs only; 0: the config's)")
+    ap.add_argument("--no-cfg1", action="store_true", help="longctx at N=1: skip the configs[1] sub-measurement")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--ctas", type=int, default=0, help="decode grid size (0: one CTA per SM)")
+    ap.add_argument("--no-graph", dest="graph", action="store_false", help="launch every layer from Python")
     ap.add_argument("--no-overlap", dest="overlap", action="store_false",
                     help="plain stream ordering between layer launches (default: each layer's launch overlaps "
                          "the previous one's end; no layer writes another layer's history rows or the lengths)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "append", "longctx", "paged"])
-    ap.add_argument("--paged-layers", type=int, default=28, help="layers of the paged workload (profiling only)")
-    return ap.parse_args()
+    return ap.parse_args(argv)
 
 
-def config_of(a):
-    if a.workload == "longctx":
-        return {"workload": "cfg4_llama3_70b_bvq_longctx", "layers": a.layers, "batch": a.batch,
-                "n_q_heads": a.hq_total, "n_kv_heads": a.hkv_total, "head_dim": 128, "history_tokens": a.ctx,
-                "window_tokens": a.window, "keys": "block-VQ 8x256 (fp16 codebook)", "values": "2-bit g32",
-                "parallelism": f"kv-head x{a.head_groups}" + (f", sequence x{a.seq_splits}" if a.seq_splits > 1 else ""),
-                "per_gpu": {"n_q_heads": a.hq, "n_kv_heads": a.hkv}, "l2": "inputs larger than L2 (no flush)"}
-    return {"workload": "cfg1_llama3_8b_bvq_decode", "layers": a.layers, "batch_per_gpu": a.batch,
-            "n_q_heads": a.hq, "n_kv_heads": a.hkv, "head_dim": 128, "history_tokens": a.ctx,
-            "window_tokens": a.window, "keys": "block-VQ 8x256 (fp16 codebook)", "values": "2-bit g32",
-            "l2": "inputs larger than L2 (no flush)"}
+def peak_hbm():
+    try:
+        return float(json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
 
 
-def bytes_per_layer(a) -> int:
-    """Algorithmic HBM bytes of one layer's decode (roofline)."""
-    D = 128
-    hist = a.ctx * (D // 8 + D // 4 + 2 * 2 * (D // 32))      # 16 B idx + 32 B codes + 8 B scales + 8 B zeros
-    recent = a.window * 2 * D * 2                              # exact bf16 K and V
-    qo = a.hq * D * 2 * 2                                      # query in, output out (bf16)
-    return a.batch * (a.hkv * (hist + recent) + qo)
+# ----------------------------------------------------------------------------- decode workloads
+@dataclass
+class DecodeSpec:
+    name: str
+    layers: int
+    batch: int            # sequences this rank decodes
+    ctx: int
+    window: int
+    hq: int               # query heads on this rank
+    hkv: int              # kv heads on this rank
+    hq_total: int
+    hkv_total: int
+    scaling: str
+    parallelism: str
+    world: int = 1
+    extra: dict = field(default_factory=dict)
+
+    def config(self):
+        return {"workload": self.name, "layers": self.layers, "batch": self.batch if self.scaling == "strong"
+                else self.batch * self.world, "n_q_heads": self.hq_total, "n_kv_heads": self.hkv_total,
+                "head_dim": 128, "history_tokens": self.ctx, "window_tokens": self.window,
+                "keys": "block-VQ 8x256 (fp16 codebook)", "values": "2-bit g32", "parallelism": self.parallelism,
+                "per_gpu": {"batch": self.batch, "n_q_heads": self.hq, "n_kv_heads": self.hkv},
+                "l2": "inputs larger than L2 (no flush)"}
+
+    def bytes_per_layer(self) -> int:
+        """Algorithmic HBM bytes of one layer's decode on this rank: packed history rows
+        (16 B block indices + 32 B value codes + 8 B value scales + 8 B value zeros per
+        token-head), the exact bf16 window K and V, the bf16 query in and output out."""
+        D = 128
+        hist = self.ctx * (D // 8 + D // 4 + 2 * 2 * (D // 32))
+        recent = self.window * 2 * D * 2
+        qo = self.hq * D * 2 * 2
+        return self.batch * (self.hkv * (hist + recent) + qo)
 
 
-# ----------------------------------------------------------------------------- clocks
+def decode_spec(workload: str, world: int, layers_override: int = 0) -> DecodeSpec:
+    if workload == "longctx":
+        from smaq_b200.distributed import make_plan
+        plan = make_plan(world, 8)
+        if plan.seq_splits > 1:
+            raise SystemExit("longctx: more ranks than KV heads is not benchmarked")
+        g = plan.head_groups
+        s = DecodeSpec("cfg4_llama3_70b_bvq_longctx", 80, 4, 131072, 128, 64 // g, 8 // g, 64, 8, "strong",
+                       f"kv-head x{g}", world)
+    else:
+        s = DecodeSpec("cfg1_llama3_8b_bvq_decode", 32, 16, 32768, 128, 32, 8, 32, 8, "weak",
+                       f"replicas x{world} (independent sequences)", world)
+    if layers_override:
+        s.layers = layers_override
+    return s
+
+
 class Clocks:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -137,11 +184,10 @@ class Clocks:
                 "samples": len(sm), "power_w_max": max(power)}
 
 
-# ----------------------------------------------------------------------------- workload
 def make_codebook(dev):
     """256-entry block-VQ codebook fit by seeded k-means on 16K calibration keys, fp16 values."""
     import torch
-    from smaq_b200 import synthetic as syn
+    from smaq_b200 import ops, synthetic as syn
     from smaq_b200.block_vq import SMAQBlockVQ
     vq = SMAQBlockVQ(128, device=dev)
     ck = torch.from_numpy(syn.keys((16384,), 128, seed=21)).to(dev)
@@ -149,7 +195,6 @@ def make_codebook(dev):
     vq.fit(ck, cq, seed=syn.SEED_KMEANS)
     for name in ("E_blocks", "E_inv_blocks", "centroids", "decoded_centroids"):
         getattr(vq, name).copy_(getattr(vq, name).half().float())
-    from smaq_b200 import ops
     vq.cb16 = ops.fp16_codebook(vq.decoded_centroids)
     assert vq.cb16 is not None
     return vq
@@ -163,8 +208,10 @@ def spectral_keys_gpu(n, gen, U, lam_sqrt, outl, dtype):
     return x.to(dtype)
 
 
-def build_layers(a, dev, vq, seed0: int):
-    """Per layer: batched store rows [B, Hkv, ctx, ...], recent window, queries."""
+def build_layers(spec: DecodeSpec, dev, vq, seed0: int, head0: int = 0):
+    """Per layer: store rows [B, Hkv, ctx, ...] (decode layout), exact window, queries, outputs.
+    ``head0``: first global KV head of this rank (keys and values of a KV head do not depend on
+    how the heads are sharded)."""
     import torch
     from smaq_b200 import ops, synthetic as syn
     from smaq_b200._lib import SMAQ_KEYS_BVQ, SMAQ_LAYOUT_DECODE
@@ -172,111 +219,310 @@ def build_layers(a, dev, vq, seed0: int):
     U = torch.from_numpy(U_np.astype(np.float32)).to(dev)
     lam = torch.from_numpy(np.sqrt(syn.spectrum(128)).astype(np.float32)).to(dev)
     outl = torch.from_numpy(outl).to(dev)
-    B, H, T, D, W = a.batch, a.hkv, a.ctx, 128, a.window
+    B, H, T, D, W = spec.batch, spec.hkv, spec.ctx, 128, spec.window
     bf = torch.bfloat16
     layers = []
-    for li in range(a.layers):
-        gen = torch.Generator(device=dev).manual_seed(seed0 * 1000 + li)
+    for li in range(spec.layers):
         L = {
             "codes": torch.empty((B, H, T, 16), dtype=torch.uint8, device=dev),
             "vdata": torch.empty((B, H, T, 32), dtype=torch.uint8, device=dev),
             "vs": torch.empty((B, H, T, 4), dtype=bf, device=dev),
             "vz": torch.empty((B, H, T, 4), dtype=bf, device=dev),
+            "rk": torch.empty((B, W, H, D), dtype=bf, device=dev),
+            "rv": torch.empty((B, W, H, D), dtype=bf, device=dev),
+            "q": torch.empty((B, spec.hq, D), dtype=bf, device=dev),
+            "out": torch.empty((B, spec.hq, D), dtype=bf, device=dev),
         }
-        for b in range(B):
-            k = spectral_keys_gpu(T * H, gen, U, lam, outl, bf).reshape(T, H, D)
-            v = torch.randn((T, H, D), generator=gen, device=dev, dtype=torch.float32).to(bf)
-            ops.append(k, v, n_heads=H, slot_offset=b * T, page_size=T, key_format=SMAQ_KEYS_BVQ,
-                       E_blocks=vq.E_blocks, centroids=vq.centroids, key_codes=L["codes"], v_data=L["vdata"],
-                       v_scales=L["vs"], v_zeros=L["vz"], layout=SMAQ_LAYOUT_DECODE)
-        L["rk"] = spectral_keys_gpu(B * W * H, gen, U, lam, outl, bf).reshape(B, W, H, D)
-        L["rv"] = torch.randn((B, W, H, D), generator=gen, device=dev, dtype=torch.float32).to(bf)
-        L["q"] = (torch.randn((B, a.hq, D), generator=gen, device=dev, dtype=torch.float32)).to(bf)
-        L["out"] = torch.empty((B, a.hq, D), dtype=bf, device=dev)
+        G = spec.hq // spec.hkv
+        for hl in range(H):
+            gen = torch.Generator(device=dev).manual_seed(seed0 * 100003 + li * 131 + head0 + hl)
+            for b in range(B):
+                k = spectral_keys_gpu(T, gen, U, lam, outl, bf).reshape(T, 1, D)
+                v = torch.randn((T, 1, D), generator=gen, device=dev, dtype=torch.float32).to(bf)
+                ops.append(k, v, n_heads=1, slot_offset=(b * H + hl) * T, page_size=T, key_format=SMAQ_KEYS_BVQ,
+                           E_blocks=vq.E_blocks, centroids=vq.centroids, key_codes=L["codes"], v_data=L["vdata"],
+                           v_scales=L["vs"], v_zeros=L["vz"], layout=SMAQ_LAYOUT_DECODE)
+            L["rk"][:, :, hl] = spectral_keys_gpu(B * W, gen, U, lam, outl, bf).reshape(B, W, D)
+            L["rv"][:, :, hl] = torch.randn((B, W, D), generator=gen, device=dev, dtype=torch.float32).to(bf)
+            L["q"][:, hl * G:(hl + 1) * G] = torch.randn((B, G, D), generator=gen, device=dev,
+                                                        dtype=torch.float32).to(bf)
         layers.append(L)
     torch.cuda.synchronize()
     return layers
 
 
-def decode_layer(a, L, vq, hl, rl, ws, q=None, out=None):
+def decode_layer(spec: DecodeSpec, L, vq, hl, rl, ws, overlap: bool):
     from smaq_b200 import ops
     from smaq_b200._lib import SMAQ_KEYS_BVQ, SMAQ_LAYOUT_DECODE
-    return ops.decode(L["q"] if q is None else q, n_kv_heads=a.hkv, key_format=SMAQ_KEYS_BVQ,
-                      centroids=vq.decoded_centroids, key_codes=L["codes"], v_data=L["vdata"], v_scales=L["vs"],
-                      v_zeros=L["vz"], hist_len=hl, page_size=a.ctx, recent_k=L["rk"], recent_v=L["rv"],
-                      recent_len=rl, out=L["out"] if out is None else out, workspace=ws, layout=SMAQ_LAYOUT_DECODE,
-                      centroids_f16=vq.cb16, num_ctas=getattr(a, "ctas", 0), overlap_prior=getattr(a, "overlap", False))
+    return ops.decode(L["q"], n_kv_heads=spec.hkv, key_format=SMAQ_KEYS_BVQ, centroids=vq.decoded_centroids,
+                      key_codes=L["codes"], v_data=L["vdata"], v_scales=L["vs"], v_zeros=L["vz"], hist_len=hl,
+                      page_size=spec.ctx, recent_k=L["rk"], recent_v=L["rv"], recent_len=rl, out=L["out"],
+                      workspace=ws, layout=SMAQ_LAYOUT_DECODE, centroids_f16=vq.cb16, overlap_prior=overlap)
 
 
-def stack_io(layers):
-    """Put every layer's query rows in one device buffer and its outputs in another (each layer
-    keeps views), with pinned host mirrors, so an end-to-end step moves all queries host->device
-    in one copy and all outputs device->host in one copy."""
+def time_decode(spec: DecodeSpec, dev, vq, steps: int, warmup: int, overlap: bool, use_graph: bool, barrier):
+    """Device time of one step (all layers), of one layer launch alone, and of one end-to-end
+    step (per-layer host<->device copies of queries and outputs)."""
     import torch
-    Q = torch.stack([L["q"] for L in layers])
-    O = torch.stack([L["out"] for L in layers])
+    from smaq_b200 import ops
+    layers = build_layers(spec, dev, vq, seed0=1 + spec.extra.get("rank", 0), head0=spec.extra.get("head0", 0))
+    hl = torch.full((spec.batch,), spec.ctx, dtype=torch.int32, device=dev)
+    rl = torch.full((spec.batch,), spec.window, dtype=torch.int32, device=dev)
+    ws = torch.empty(ops.decode_workspace_bytes(spec.batch, spec.hq, spec.hkv, 128), dtype=torch.uint8, device=dev)
+    hQ = torch.empty((spec.layers,) + tuple(layers[0]["q"].shape), dtype=torch.bfloat16).pin_memory()
+    hO = torch.empty_like(hQ).pin_memory()
     for i, L in enumerate(layers):
-        L["q"], L["out"] = Q[i], O[i]
-    hQ = torch.empty_like(Q, device="cpu").pin_memory()
-    hQ.copy_(Q.cpu())
-    hO = torch.empty_like(O, device="cpu").pin_memory()
-    return Q, O, hQ, hO
+        hQ[i].copy_(L["q"].cpu())
+
+    def step():
+        for L in layers:
+            decode_layer(spec, L, vq, hl, rl, ws, overlap)
+
+    def e2e_step():
+        for i, L in enumerate(layers):
+            L["q"].copy_(hQ[i], non_blocking=True)
+            decode_layer(spec, L, vq, hl, rl, ws, overlap)
+            hO[i].copy_(L["out"], non_blocking=True)
+
+    for _ in range(max(3, warmup)):
+        step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream()
+    run, run_e2e = step, e2e_step
+    if use_graph:
+        g, ge = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                step()
+            with torch.cuda.graph(ge, stream=stream):
+                e2e_step()
+        torch.cuda.synchronize()
+        run, run_e2e = g.replay, ge.replay
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn, n):
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, warmup)):
+                fn()
+            torch.cuda.synchronize()
+            barrier()
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(n):
+                fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            barrier()
+        return e0.elapsed_time(e1) / n
+
+    clocks = Clocks(dev.index or 0)
+    clocks.start()
+    time.sleep(0.3)
+    ms = timed(run, steps)
+    ck = clocks.stop()
+    e2e_ms = timed(run_e2e, steps)
+    # one layer launch alone between two events (cold start of that launch: no overlap)
+    iso = []
+    with torch.cuda.stream(stream):
+        for L in layers[: min(8, len(layers))]:
+            torch.cuda.synchronize()
+            e0.record(stream)
+            decode_layer(spec, L, vq, hl, rl, ws, False)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            iso.append(e0.elapsed_time(e1))
+    ops.decode_status(spec.batch, spec.hkv, ws)
+    del layers
+    torch.cuda.empty_cache()
+    return {"ms": ms, "e2e_ms": e2e_ms, "iso_ms": statistics.median(iso), "clocks": ck,
+            "h2d": hQ.numel() * hQ.element_size(), "d2h": hO.numel() * hO.element_size()}
 
 
-# ----------------------------------------------------------------------------- CPU baseline
-def cpu_sample(a, seconds_cap: float = 20.0):
-    """Time the CPU port of the reference path (oracle, fp32 like the reference's torch ops) on
-    one layer x one sequence, and scale to the metric's unit."""
+def decode_line(spec: DecodeSpec, t: dict, steps: int, warmup: int) -> dict:
+    peak, src = peak_hbm()
+    bpl = spec.bytes_per_layer()
+    launch_ms = t["ms"] / spec.layers
+    achieved = bpl / (launch_ms * 1e-3) / 1e9
+    tokens = spec.batch if spec.scaling == "strong" else spec.batch * spec.world
+    traffic = NCU_TRAFFIC.get((spec.batch, spec.ctx, spec.window, spec.hq, spec.hkv))
+    return {
+        "metric": METRIC, "value": tokens / (t["ms"] * 1e-3), "unit": "tokens/s", "n_gpus": spec.world,
+        "steps": steps, "warmup": max(3, warmup), "ms_per_step": t["ms"], "higher_is_better": True,
+        "scaling": spec.scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": spec.config(),
+        "hbm_gbs": spec.world * bpl * spec.layers / (t["ms"] * 1e-3) / 1e9,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "traffic_source": "ncu dram bytes per launch, same per-launch shape"
+                     if traffic else None, "peak_source": src,
+                     "kernel": "one fused decode launch per layer (history + window + merge)",
+                     "algorithmic_bytes_per_launch": bpl, "launch_us": launch_ms * 1e3,
+                     "launch_us_isolated": t["iso_ms"] * 1e3,
+                     "launch_time": "timed region / launches (CUDA-graph replay, consecutive launches overlap); "
+                                    "isolated = one launch alone between two events"},
+        "e2e": {"value": tokens / (t["e2e_ms"] * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": t["h2d"],
+                "d2h_bytes_per_step": t["d2h"],
+                "note": "per layer: pinned host -> device copy of its query rows, decode, device -> host copy of "
+                        "its output rows; one CUDA-graph replay per step"},
+        "gpu_launches": spec.layers * steps,
+        "clocks": t["clocks"],
+    }
+
+
+def run_decode(a, rank: int, world: int):
+    import torch
+    import torch.distributed as dist
+    from smaq_b200 import build
+    build.build()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    spec = decode_spec(a.workload, world, a.layers)
+    if spec.scaling == "weak":
+        spec.extra["rank"] = rank     # replicas: every rank its own sequences
+    else:
+        from smaq_b200.distributed import make_plan
+        spec.extra["head0"] = make_plan(world, 8).kv_heads(rank).start
+    vq = make_codebook(dev)
+    t = time_decode(spec, dev, vq, a.steps, a.warmup, a.overlap, a.graph, barrier)
+    if world > 1:
+        v = torch.tensor([t["ms"], t["e2e_ms"], t["iso_ms"]], device=dev)
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        t["ms"], t["e2e_ms"], t["iso_ms"] = v.tolist()
+    line = decode_line(spec, t, a.steps, a.warmup)
+    if world == 1 and a.workload == "longctx" and not a.no_cfg1:
+        s1 = decode_spec("decode", 1)
+        t1 = time_decode(s1, dev, vq, a.steps, a.warmup, a.overlap, a.graph, barrier)
+        l1 = decode_line(s1, t1, a.steps, a.warmup)
+        line["cfg1"] = {k: l1[k] for k in ("value", "unit", "ms_per_step", "config", "hbm_gbs", "roofline", "e2e",
+                                           "clocks")}
+    if rank == 0:
+        if world == 1 and not a.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(spec)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------- reference (CPU)
+def import_reference():
+    """The reference package installed unmodified under baseline/_ref (None if absent)."""
+    if not os.path.isdir(os.path.join(REF_DIR, "smaq")):
+        return None
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    import smaq
+    if not os.path.abspath(smaq.__file__).startswith(REF_DIR):
+        return None
+    return smaq
+
+
+def _timed_runs(fn, seconds_cap: float, max_runs: int = 5):
+    runs = []
+    t_end = time.perf_counter() + seconds_cap
+    while True:
+        t0 = time.perf_counter()
+        fn()
+        runs.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end or len(runs) >= max_runs:
+            return statistics.median(runs), len(runs)
+
+
+def reference_decode_sample(spec: DecodeSpec, key_format: str = "bvq", bits: int = 4, seconds_cap: float = 20.0,
+                            max_runs: int = 5, warmup: int = 1):
+    """The reference's compute_hybrid_attention on CPU (all host threads) for one layer and one
+    sequence of the workload, scaled to a full step.  The store is the reference's own
+    CompressedKVStore, filled through append_chunk."""
+    import torch
+    from smaq_b200 import synthetic as syn
+    smaq = import_reference()
+    if smaq is None:
+        return None
+    from smaq.score import compute_hybrid_attention
+    from smaq.store import CompressedKVStore
+    from smaq.strategies import SMAQBlockVQStrategy, SMAQFullMetricScalarStrategy
+    torch.set_num_threads(os.cpu_count() or 1)
+    cpu = torch.device("cpu")
+    D = 128
+    ctx, hq, hkv, window, layers = spec.ctx, spec.hq_total, spec.hkv_total, spec.window, spec.layers
+    batch = spec.batch if spec.scaling == "strong" else spec.batch * spec.world
+    if key_format == "bvq":
+        strat = SMAQBlockVQStrategy(D, device=cpu)
+        strat.fit(torch.from_numpy(syn.calibration_queries(4096, D)), torch.from_numpy(syn.keys((4096,), D, seed=21)))
+    else:
+        strat = SMAQFullMetricScalarStrategy(D, bits=bits, device=cpu)
+        strat.fit(torch.from_numpy(syn.calibration_queries(512, D)))
+    store = CompressedKVStore(D, hkv, device=cpu, key_strategy=strat, key_bits=bits)
+    chunk = 8192
+    for t0 in range(0, ctx, chunk):
+        n = min(chunk, ctx - t0)
+        k = torch.from_numpy(syn.keys((n, hkv), D, seed=1000 + t0 // chunk)).to(torch.bfloat16)
+        v = torch.from_numpy(syn.values((n, hkv), D, seed=2000 + t0 // chunk)).to(torch.bfloat16)
+        store.append_chunk(k, v)
+    rk = torch.from_numpy(syn.keys((window, hkv), D, seed=3)).to(torch.bfloat16)
+    rv = torch.from_numpy(syn.values((window, hkv), D, seed=4)).to(torch.bfloat16)
+    q = torch.from_numpy(syn.queries((1, hq), D, seed=5)).to(torch.bfloat16)
+    for _ in range(max(1, warmup)):   # the first call also builds the reference's flat cache
+        compute_hybrid_attention(q, store, rk, rv, hq)
+    t, n_runs = _timed_runs(lambda: compute_hybrid_attention(q, store, rk, rv, hq), seconds_cap, max_runs)
+    step_s = t * layers * batch
+    return {"value": batch / step_s, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "reference",
+            "sample": f"reference compute_hybrid_attention (baseline/_ref, torch {torch.__version__} CPU), 1 layer x "
+                      f"1 sequence ({ctx} history + {window} window tokens, {hq}/{hkv} heads), median of {n_runs} "
+                      f"runs = {t * 1e3:.1f} ms, scaled x{layers * batch}"}
+
+
+def port_decode_sample(spec: DecodeSpec, seconds_cap: float = 20.0):
+    """Fallback when the reference is not installed: the numpy restatement (fp32) on one layer x
+    one sequence, scaled."""
     from oracle import smaq_oracle as O
     from smaq_b200 import synthetic as syn
-    try:
-        from threadpoolctl import threadpool_info
-        cores = max([i.get("num_threads", 1) for i in threadpool_info()] + [1])
-    except Exception:
-        cores = os.cpu_count() or 1
     rng = np.random.default_rng(5)
-    H, T, D, W = a.hkv, a.ctx, 128, a.window
+    H, T, D, W = spec.hkv_total, spec.ctx, 128, spec.window
     idx = rng.integers(0, 256, size=(H, T, 16))
     dec = rng.standard_normal((16, 256, 8)).astype(np.float32)
     vdata = rng.integers(0, 256, size=(H, T, 32), dtype=np.uint8)
     vs = np.abs(rng.standard_normal((H, T, 4))).astype(np.float32)
     vz = rng.standard_normal((H, T, 4)).astype(np.float32)
-    q = syn.queries((1, a.hq), D, seed=9)
+    q = syn.queries((1, spec.hq_total), D, seed=9)
     rk = syn.keys((W, H), D, seed=10)
     rv = syn.values((W, H), D, seed=11)
-    runs = []
-    t_end = time.perf_counter() + seconds_cap
-    while True:
-        t0 = time.perf_counter()
-        K = O.bvq_dequantize(idx, dec, work=np.float32)           # the reference materialises k_hat
+
+    def one():
+        K = O.bvq_dequantize(idx, dec, work=np.float32)
         V = O.dequantize_values(vdata, vs, vz, 2, 32)
-        O.hybrid_attention(q, "bf16", K, V, rk, rv, a.hq, H, work=np.float32)
-        runs.append(time.perf_counter() - t0)
-        if time.perf_counter() > t_end or len(runs) >= 5:
-            break
-    t = statistics.median(runs)
-    step_s = t * a.layers * a.batch                                 # one layer x one sequence -> full step
-    return {"value": a.batch / step_s, "unit": "tokens/s", "cores": int(cores), "kind": "port",
-            "sample": f"1 layer x 1 sequence ({T} history + {W} window tokens, {H} kv heads), "
-                      f"median of {len(runs)} runs = {t*1e3:.1f} ms, scaled x{a.layers * a.batch}"}
+        O.hybrid_attention(q, "bf16", K, V, rk, rv, spec.hq_total, H, work=np.float32)
+
+    t, n_runs = _timed_runs(one, seconds_cap)
+    batch = spec.batch if spec.scaling == "strong" else spec.batch * spec.world
+    return {"value": batch / (t * spec.layers * batch), "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"numpy restatement, 1 layer x 1 sequence ({T} + {W} tokens), median of {n_runs} runs = "
+                      f"{t * 1e3:.1f} ms, scaled x{spec.layers * batch}"}
+
+
+def cpu_baseline(spec: DecodeSpec, seconds_cap: float = 20.0, max_runs: int = 5, warmup: int = 1):
+    return (reference_decode_sample(spec, seconds_cap=seconds_cap, max_runs=max_runs, warmup=warmup)
+            or port_decode_sample(spec, seconds_cap))
 
 
 def run_reference(a, rank: int, world: int):
     if rank != 0:
         return
-    for _ in range(max(0, a.warmup)):
-        pass
-    vals = []
-    info = None
-    for _ in range(max(1, a.steps)):
-        info = cpu_sample(a, seconds_cap=max(2.0, 60.0 / max(1, a.steps)))
-        vals.append(info["value"])
-    v = statistics.median(vals)
+    spec = decode_spec(a.workload, world, a.layers)
+    # one store is built, then K timed calls (each one layer x one sequence), median taken
+    info = cpu_baseline(spec, seconds_cap=120.0, max_runs=max(1, a.steps), warmup=max(1, a.warmup))
+    v = info["value"]
+    tokens = spec.batch if spec.scaling == "strong" else spec.batch * world
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
-            "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * a.batch / v, "higher_is_better": True,
-            "scaling": "strong" if a.workload == "longctx" else "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": config_of(a),
-            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": info["cores"], "kind": "port",
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * tokens / v,
+            "higher_is_better": True, "scaling": spec.scaling, "vs_baseline": None, "dtype": "bf16-io/f32",
+            "data": "synthetic", "config": spec.config(),
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": info["cores"], "kind": info["kind"],
                              "sample": info["sample"]},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -301,48 +547,55 @@ def append_bytes():
     return k_in, v_in, k_out, v_out
 
 
-def append_cpu_sample(seconds_cap: float = 20.0):
-    """The reference's append path restated in torch CPU ops (oracle.torch_append: norm, divide,
-    fp32 matmul, searchsorted, pack; value codec) on all host threads, on a bounded sample of
-    token-heads, scaled to the full batch."""
+def append_cpu_sample(seconds_cap: float = 20.0, max_runs: int = 5):
+    """The reference's CompressedKVStore.append_chunk (smaq/store.py:83-95: SMAQ 3-bit scalar
+    keys + 2-bit values, bf16) on the host CPU with all threads, on a bounded sample of
+    token-heads, scaled to the full batch.  Falls back to the torch CPU restatement of the same
+    ops when the reference is not installed."""
     import torch
-    from oracle import smaq_oracle as O
     from smaq_b200 import synthetic as syn
-    from smaq_b200.quantizer import SMAQQuantizer
     torch.set_num_threads(os.cpu_count() or 1)
-    rows = 65536
-    k = torch.from_numpy(syn.keys((rows,), AP_D, seed=31)).to(torch.bfloat16)
-    v = torch.from_numpy(syn.values((rows,), AP_D, seed=32)).to(torch.bfloat16)
-    quant = SMAQQuantizer(AP_D, bits=AP_BITS, device=torch.device("cpu"))
-    quant.fit(torch.from_numpy(syn.calibration_queries(512, AP_D)))
-    E, bnd = quant.E.float(), quant.decision_boundaries.float().contiguous()
-    runs = []
-    t_end = time.perf_counter() + seconds_cap
-    while True:
-        t0 = time.perf_counter()
-        O.torch_append(k, v, E, bnd, AP_BITS)
-        runs.append(time.perf_counter() - t0)
-        if time.perf_counter() > t_end or len(runs) >= 5:
-            break
-    t = statistics.median(runs)
+    tokens = 8192
+    rows = tokens * AP_H
+    k = torch.from_numpy(syn.keys((tokens, AP_H), AP_D, seed=31)).to(torch.bfloat16)
+    v = torch.from_numpy(syn.values((tokens, AP_H), AP_D, seed=32)).to(torch.bfloat16)
+    calq = torch.from_numpy(syn.calibration_queries(512, AP_D))
+    smaq = import_reference()
+    if smaq is not None:
+        from smaq.store import CompressedKVStore
+        from smaq.strategies import SMAQFullMetricScalarStrategy
+        strat = SMAQFullMetricScalarStrategy(AP_D, bits=AP_BITS, device=torch.device("cpu"))
+        strat.fit(calq)
+        store = CompressedKVStore(AP_D, AP_H, key_bits=AP_BITS, device=torch.device("cpu"), key_strategy=strat)
+
+        def one():
+            store.append_chunk(k, v)
+        kind, what = "reference", "reference CompressedKVStore.append_chunk (baseline/_ref)"
+    else:
+        from oracle import smaq_oracle as O
+        from smaq_b200.quantizer import SMAQQuantizer
+        quant = SMAQQuantizer(AP_D, bits=AP_BITS, device=torch.device("cpu"))
+        quant.fit(calq)
+        E, bnd = quant.E.float(), quant.decision_boundaries.float().contiguous()
+        kr, vr = k.reshape(rows, AP_D), v.reshape(rows, AP_D)
+
+        def one():
+            O.torch_append(kr, vr, E, bnd, AP_BITS)
+        kind, what = "port", "torch CPU restatement of the append ops"
+    t, n_runs = _timed_runs(one, seconds_cap, max_runs)
     total = sum(append_bytes())
     scale = AP_B * AP_T * AP_H / rows
-    return {"value": total / (t * scale) / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{rows} token-heads, median of {len(runs)} runs = {t*1e3:.1f} ms, scaled x{scale:.0f}"}
+    return {"value": total / (t * scale) / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": kind,
+            "sample": f"{what}, {tokens} tokens x {AP_H} heads, median of {n_runs} runs = {t * 1e3:.1f} ms, "
+                      f"scaled x{scale:.0f}"}
 
 
-def run_append(a, rank: int, world: int):
+def append_inputs(dev, rank: int = 0):
+    """configs[2] inputs and destination rows on ``dev``: keys/values [B*T, H, D] bf16 with the
+    spectral key distribution, the fitted 3-bit scalar quantizer, and decode-layout rows."""
     import torch
-    import torch.distributed as dist
-    from smaq_b200 import build, ops, synthetic as syn
-    from smaq_b200._lib import SMAQ_KEYS_SCALAR, SMAQ_LAYOUT_DECODE
+    from smaq_b200 import synthetic as syn
     from smaq_b200.quantizer import SMAQQuantizer
-    build.build()
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
     quant = SMAQQuantizer(AP_D, bits=AP_BITS, device=dev)
     quant.fit(torch.from_numpy(syn.calibration_queries(512, AP_D)).to(dev))
     U_np, outl = syn.basis(AP_D)
@@ -354,18 +607,40 @@ def run_append(a, rank: int, world: int):
     k = spectral_keys_gpu(N * AP_H, gen, U, lam, outl, torch.bfloat16).reshape(N, AP_H, AP_D)
     v = torch.randn((N, AP_H, AP_D), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
     rows = N * AP_H
-    codes = torch.empty((rows, AP_D // 2), dtype=torch.uint8, device=dev)
-    norms = torch.empty((rows,), dtype=torch.bfloat16, device=dev)
-    vd = torch.empty((rows, AP_D // 4), dtype=torch.uint8, device=dev)
-    vs = torch.empty((rows, AP_D // 32), dtype=torch.bfloat16, device=dev)
-    vz = torch.empty_like(vs)
-    E, bnd = quant.E.contiguous(), quant.decision_boundaries.contiguous()
+    out = {"codes": torch.empty((rows, AP_D // 2), dtype=torch.uint8, device=dev),
+           "norms": torch.empty((rows,), dtype=torch.bfloat16, device=dev),
+           "vd": torch.empty((rows, AP_D // 4), dtype=torch.uint8, device=dev),
+           "vs": torch.empty((rows, AP_D // 32), dtype=torch.bfloat16, device=dev)}
+    out["vz"] = torch.empty_like(out["vs"])
+    return k, v, quant, out
+
+
+def append_step(k, v, quant, o, keys=True, values=True):
+    """One configs[2] append: every sequence's 8192 new tokens land in its own store page
+    (page_size 8192), decode layout."""
+    from smaq_b200 import ops
+    from smaq_b200._lib import SMAQ_KEYS_SCALAR, SMAQ_LAYOUT_DECODE
+    ops.append(k if keys else None, v if values else None, n_heads=AP_H, page_size=AP_T,
+               key_format=SMAQ_KEYS_SCALAR, key_bits=AP_BITS, E=quant.E, boundaries=quant.decision_boundaries,
+               key_codes=o["codes"], key_norms=o["norms"], v_data=o["vd"], v_scales=o["vs"], v_zeros=o["vz"],
+               layout=SMAQ_LAYOUT_DECODE)
+
+
+def run_append(a, rank: int, world: int):
+    import torch
+    import torch.distributed as dist
+    from smaq_b200 import build
+    build.build()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    k, v, quant, o = append_inputs(dev, rank)
+    codes, norms, vd, vs, vz = o["codes"], o["norms"], o["vd"], o["vs"], o["vz"]
 
     def step(kk=k, vv=v, keys=True, values=True):
-        # every sequence's 8192 new tokens land in its own store page (page_size 8192)
-        ops.append(kk if keys else None, vv if values else None, n_heads=AP_H, page_size=AP_T,
-                   key_format=SMAQ_KEYS_SCALAR, key_bits=AP_BITS, E=E, boundaries=bnd, key_codes=codes,
-                   key_norms=norms, v_data=vd, v_scales=vs, v_zeros=vz, layout=SMAQ_LAYOUT_DECODE)
+        append_step(kk, vv, quant, o, keys, values)
 
     def barrier():
         if world > 1:
@@ -474,17 +749,14 @@ def run_append(a, rank: int, world: int):
 def run_append_reference(a, rank: int):
     if rank != 0:
         return
-    vals, info = [], None
-    for _ in range(max(1, a.steps)):
-        info = append_cpu_sample(seconds_cap=max(2.0, 60.0 / max(1, a.steps)))
-        vals.append(info["value"])
-    v = statistics.median(vals)
+    info = append_cpu_sample(seconds_cap=120.0, max_runs=max(1, a.steps))
+    v = info["value"]
     total = sum(append_bytes())
     line = {"impl": "reference", "metric": APPEND_METRIC, "value": v, "unit": "GB/s",
             "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": a.steps, "warmup": a.warmup,
             "ms_per_step": 1e3 * total / (v * 1e9), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16-io/f32-matmul", "data": "synthetic", "config": append_config(),
-            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": info["cores"], "kind": "port",
+            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": info["cores"], "kind": info["kind"],
                              "sample": info["sample"]},
             "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -512,13 +784,20 @@ def paged_config():
             "l2": "inputs larger than L2 (no flush)"}
 
 
-def paged_cpu_sample(seconds_cap: float = 20.0):
-    """The reference's hybrid attention (oracle port, fp32) for one layer x one sequence of the
-    mean length, scaled to the step."""
-    from oracle import smaq_oracle as O
-    from smaq_b200 import synthetic as syn
+def paged_cpu_sample(seconds_cap: float = 20.0, max_runs: int = 5):
+    """The reference's compute_hybrid_attention (4-bit SMAQ scalar keys) on the host CPU for one
+    layer x one sequence of the mean length, scaled to the step; the numpy restatement when the
+    reference is not installed."""
     lens = paged_lengths()
     n = int(np.mean(lens))
+    spec = DecodeSpec("cfg3_qwen2.5_7b_paged_scalar4", PG_LAYERS, PG_B, n, PG_W, PG_HQ, PG_HKV, PG_HQ, PG_HKV,
+                      "weak", "single GPU")
+    info = reference_decode_sample(spec, key_format="scalar", bits=PG_BITS, seconds_cap=seconds_cap,
+                                   max_runs=max_runs)
+    if info is not None:
+        return info
+    from oracle import smaq_oracle as O
+    from smaq_b200 import synthetic as syn
     rng = np.random.default_rng(6)
     D = 128
     codes = rng.integers(0, 256, size=(PG_HKV, n, 64), dtype=np.uint8)
@@ -531,35 +810,28 @@ def paged_cpu_sample(seconds_cap: float = 20.0):
     q = syn.queries((1, PG_HQ), D, seed=9)
     rk = syn.keys((PG_W, PG_HKV), D, seed=10)
     rv = syn.values((PG_W, PG_HKV), D, seed=11)
-    runs = []
-    t_end = time.perf_counter() + seconds_cap
-    while True:
-        t0 = time.perf_counter()
+
+    def one():
         K = O.scalar_score_keys(codes, norms, PG_BITS, Einv, cent, D)
         V = O.dequantize_values(vdata, vs, vz, 2, 32)
         O.hybrid_attention(q, "bf16", K, V, rk, rv, PG_HQ, PG_HKV, work=np.float32)
-        runs.append(time.perf_counter() - t0)
-        if time.perf_counter() > t_end or len(runs) >= 5:
-            break
-    t = statistics.median(runs)
-    step_s = t * PG_LAYERS * PG_B
-    return {"value": PG_B / step_s, "unit": "tokens/s", "cores": 1, "kind": "port",
-            "sample": f"1 layer x 1 sequence of {n} tokens, median of {len(runs)} runs = {t*1e3:.1f} ms, "
-                      f"scaled x{PG_LAYERS * PG_B}"}
+
+    t, n_runs = _timed_runs(one, seconds_cap, max_runs)
+    return {"value": PG_B / (t * PG_LAYERS * PG_B), "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"numpy restatement, 1 layer x 1 sequence of {n} tokens, median of {n_runs} runs = "
+                      f"{t * 1e3:.1f} ms, scaled x{PG_LAYERS * PG_B}"}
 
 
-def run_paged(a, rank: int, world: int):
+def build_paged_layers(n_layers: int, dev, rank: int = 0):
+    """configs[3] on ``dev``: per layer a shuffled 16-token paged store (decode layout) filled
+    through slot mappings, block table, exact window, queries, outputs.  Returns
+    ``(layers, quantizer, lengths)``."""
     import torch
-    from smaq_b200 import build, ops, synthetic as syn
+    from smaq_b200 import ops, synthetic as syn
     from smaq_b200._lib import SMAQ_KEYS_SCALAR, SMAQ_LAYOUT_DECODE
     from smaq_b200.quantizer import SMAQQuantizer
-    build.build()
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
     D = 128
     lens = paged_lengths()
-    n_layers = a.paged_layers
     quant = SMAQQuantizer(D, bits=PG_BITS, device=dev)
     quant.fit(torch.from_numpy(syn.calibration_queries(512, D)).to(dev))
     U_np, outl = syn.basis(D)
@@ -601,68 +873,99 @@ def run_paged(a, rank: int, world: int):
         L["out"] = torch.empty((PG_B, PG_HQ, D), dtype=bf, device=dev)
         layers.append(L)
     torch.cuda.synchronize()
+    return layers, quant, lens
+
+
+def paged_decode(L, quant, hl, rl, ws, overlap: bool):
+    from smaq_b200 import ops
+    from smaq_b200._lib import SMAQ_KEYS_SCALAR, SMAQ_LAYOUT_DECODE
+    return ops.decode(L["q"], n_kv_heads=PG_HKV, key_format=SMAQ_KEYS_SCALAR, key_bits=PG_BITS, E_inv=quant.E_inv,
+                      centroids=quant.centroids, key_norms=L["norms"], key_codes=L["codes"], v_data=L["vdata"],
+                      v_scales=L["vs"], v_zeros=L["vz"], hist_len=hl, page_size=PG_PAGE, block_table=L["bt"],
+                      recent_k=L["rk"], recent_v=L["rv"], recent_len=rl, out=L["out"], workspace=ws,
+                      layout=SMAQ_LAYOUT_DECODE, overlap_prior=overlap)
+
+
+def run_paged(a, rank: int, world: int):
+    import torch
+    from smaq_b200 import build, ops
+    build.build()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    D = 128
+    n_layers = a.layers or PG_LAYERS
+    layers, quant, lens = build_paged_layers(n_layers, dev, rank)
     hl = torch.from_numpy(lens.astype(np.int32)).to(dev)
     rl = torch.full((PG_B,), PG_W, dtype=torch.int32, device=dev)
     ws = torch.empty(ops.decode_workspace_bytes(PG_B, PG_HQ, PG_HKV, D), dtype=torch.uint8, device=dev)
-
-    def dec(L, q=None):
-        ops.decode(L["q"] if q is None else q, n_kv_heads=PG_HKV, key_format=SMAQ_KEYS_SCALAR, key_bits=PG_BITS,
-                   E_inv=quant.E_inv, centroids=quant.centroids, key_norms=L["norms"], key_codes=L["codes"],
-                   v_data=L["vdata"], v_scales=L["vs"], v_zeros=L["vz"], hist_len=hl, page_size=PG_PAGE,
-                   block_table=L["bt"], recent_k=L["rk"], recent_v=L["rv"], recent_len=rl, out=L["out"], workspace=ws,
-                   layout=SMAQ_LAYOUT_DECODE, overlap_prior=a.overlap)
+    hQ = torch.empty((n_layers, PG_B, PG_HQ, D), dtype=torch.bfloat16).pin_memory()
+    hO = torch.empty_like(hQ).pin_memory()
+    for i, L in enumerate(layers):
+        hQ[i].copy_(L["q"].cpu())
 
     def step():
         for L in layers:
-            dec(L)
+            paged_decode(L, quant, hl, rl, ws, a.overlap)
+
+    def e2e_step():
+        for i, L in enumerate(layers):
+            L["q"].copy_(hQ[i], non_blocking=True)
+            paged_decode(L, quant, hl, rl, ws, a.overlap)
+            hO[i].copy_(L["out"], non_blocking=True)
 
     for _ in range(max(3, a.warmup)):
         step()
     torch.cuda.synchronize()
+    stream = torch.cuda.Stream()
+    run, run_e2e = step, e2e_step
+    if a.graph:
+        g, ge = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                step()
+            with torch.cuda.graph(ge, stream=stream):
+                e2e_step()
+        torch.cuda.synchronize()
+        run, run_e2e = g.replay, ge.replay
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn):
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, a.warmup)):
+                fn()
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(a.steps):
+                fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / a.steps
+
     clocks = Clocks(local)
     clocks.start()
     time.sleep(0.3)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(a.steps):
-        step()
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / a.steps
+    ms = timed(run)
     ck = clocks.stop()
-    Q, O, hQ, hO = stack_io(layers)
-
-    def e2e_step():
-        Q.copy_(hQ, non_blocking=True)
-        step()
-        hO.copy_(O, non_blocking=True)
-
-    e2e_step()
-    torch.cuda.synchronize()
-    e0.record()
-    for _ in range(a.steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / a.steps
+    e2e_ms = timed(run_e2e)
+    ops.decode_status(PG_B, PG_HKV, ws)
     bpl = paged_bytes_per_layer(lens)
-    try:
-        peak = float(json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))["hbm_gbs"])
-    except Exception:
-        peak = 6650.0
+    peak, src = peak_hbm()
     achieved = bpl * n_layers / (ms * 1e-3) / 1e9
     # tokens/s of a full 28-layer step (ms scaled when fewer layers were built for profiling)
     ms_full = ms * PG_LAYERS / n_layers
     line = {"metric": METRIC, "value": PG_B / (ms_full * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": a.steps,
             "warmup": max(3, a.warmup), "ms_per_step": ms_full, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32-accum/bf16-io", "data": "synthetic", "config": paged_config(),
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": paged_config(),
             "hbm_gbs": achieved,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "traffic": None, "kernel": "smaq_decode (scalar keys, paged) per step",
+                         "traffic": None, "peak_source": src,
+                         "kernel": "one fused scalar-key decode launch per layer (paged)",
                          "algorithmic_bytes_per_launch": bpl},
             "e2e": {"value": PG_B / (e2e_ms * PG_LAYERS / n_layers * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": hQ.numel() * hQ.element_size(),
-                    "d2h_bytes_per_step": hO.numel() * hO.element_size()},
+                    "d2h_bytes_per_step": hO.numel() * hO.element_size(),
+                    "note": "per layer: query rows host -> device, decode, output rows device -> host"},
             "gpu_launches": n_layers * a.steps, "clocks": ck}
     if not a.no_cpu_baseline:
         line["cpu_baseline"] = paged_cpu_sample()
@@ -675,158 +978,27 @@ def main():
     a = parse()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
     if a.workload == "append":
-        if a.impl == "reference":
-            run_append_reference(a, rank)
-        else:
-            run_append(a, rank, world)
+        (run_append_reference(a, rank) if a.impl == "reference" else run_append(a, rank, world))
         return
     if a.workload == "paged":
         if a.impl == "reference":
             if rank == 0:
-                info = paged_cpu_sample(seconds_cap=max(2.0, 60.0 / max(1, a.steps)))
+                info = paged_cpu_sample(seconds_cap=120.0, max_runs=max(1, a.steps))
                 print(json.dumps({"impl": "reference", "metric": METRIC, "value": info["value"], "unit": "tokens/s",
                                   "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
                                   "ms_per_step": 1e3 * PG_B / info["value"], "higher_is_better": True,
-                                  "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                                  "scaling": "weak", "vs_baseline": None, "dtype": "bf16-io/f32", "data": "synthetic",
                                   "config": paged_config(), "cpu_baseline": info,
                                   "e2e": {"value": info["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                                           "d2h_bytes_per_step": 0}}), flush=True)
         else:
             run_paged(a, rank, world)
         return
-    if a.workload == "longctx":
-        # Llama-3-70B KV shape, 4 x 128K, 80 layers; strong scaling,
-        # KV heads sharded over the ranks (smaq_b200.distributed.make_plan)
-        from smaq_b200.distributed import make_plan
-        plan = make_plan(world, 8)
-        if plan.seq_splits > 1:
-            raise SystemExit("longctx: more ranks than KV heads is not benchmarked")
-        a.batch, a.ctx, a.layers, a.window = 4, 131072, 80, 128
-        a.hq_total, a.hkv_total = 64, 8
-        a.head_groups, a.seq_splits = plan.head_groups, plan.seq_splits
-        if a.impl != "reference":  # the CPU reference arm times the whole (unsharded) layer
-            a.hq, a.hkv = 64 // plan.head_groups, 8 // plan.head_groups
-        else:
-            a.hq, a.hkv = 64, 8
     if a.impl == "reference":
         run_reference(a, rank, world)
         return
-    import torch
-    import torch.distributed as dist
-    from smaq_b200 import build
-    build.build()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
-    vq = make_codebook(dev)
-    layers = build_layers(a, dev, vq, seed0=rank + 1)
-    hl = torch.full((a.batch,), a.ctx, dtype=torch.int32, device=dev)
-    rl = torch.full((a.batch,), a.window, dtype=torch.int32, device=dev)
-    from smaq_b200 import ops
-    ws = torch.empty(ops.decode_workspace_bytes(a.batch, a.hq, a.hkv, 128, a.ctas), dtype=torch.uint8, device=dev)
-
-    def step():
-        for L in layers:
-            decode_layer(a, L, vq, hl, rl, ws)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    for _ in range(max(3, a.warmup)):
-        step()
-    torch.cuda.synchronize()
-    clocks = Clocks(local)
-    clocks.start()
-    time.sleep(0.3)
-    barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(a.steps):
-        step()
-    e1.record()
-    torch.cuda.synchronize()
-    barrier()
-    ms = e0.elapsed_time(e1) / a.steps
-    ck = clocks.stop()
-    # per-layer decode call time (plan + decode + merge kernels) for the roofline
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in layers]
-    for _ in range(2):
-        for L, (s0, s1) in zip(layers, evs):
-            s0.record()
-            decode_layer(a, L, vq, hl, rl, ws)
-            s1.record()
-        torch.cuda.synchronize()
-    layer_ms = statistics.mean(s0.elapsed_time(s1) for s0, s1 in evs)
-    # end to end through the public API with host buffers: H2D queries, decode, D2H outputs
-    Q, O, hQ, hO = stack_io(layers)
-
-    def e2e_step():
-        Q.copy_(hQ, non_blocking=True)
-        step()
-        hO.copy_(O, non_blocking=True)
-
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    barrier()
-    e0.record()
-    for _ in range(a.steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize()
-    barrier()
-    e2e_ms = e0.elapsed_time(e1) / a.steps
-    if world > 1:
-        t = torch.tensor([ms, e2e_ms, layer_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms, layer_ms = t.tolist()
-    bpl = bytes_per_layer(a)
-    peak_gbs = None
-    peak_src = "fallback 6650 GB/s"
-    try:
-        peak_gbs = float(json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))["hbm_gbs"])
-        peak_src = "measured"
-    except Exception:
-        peak_gbs = 6650.0
-    # average launch duration over the timed region: one decode launch per layer and nothing
-    # else in a step (consecutive launches overlap when --no-overlap is not given)
-    launch_ms = ms / a.layers
-    achieved = bpl / (launch_ms * 1e-3) / 1e9
-    # DRAM bytes per launch from one ncu capture of this workload (profiles/decode_bvq_cfg1_kernel.md)
-    default_shape = (a.batch, a.ctx, a.window, a.hq, a.hkv) == (16, 32768, 128, 32, 8)
-    traffic = 284.2e6 if default_shape else None
-    h2d = hQ.numel() * hQ.element_size()
-    d2h = hO.numel() * hO.element_size()
-    if rank == 0:
-        strong = a.workload == "longctx"
-        tokens = a.batch if strong else a.batch * world
-        line = {
-            "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
-            "steps": a.steps, "warmup": max(3, a.warmup), "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "f32-accum/bf16-io",
-            "data": "synthetic", "config": config_of(a),
-            "hbm_gbs": world * bpl * a.layers / (ms * 1e-3) / 1e9,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s",
-                         "frac": achieved / peak_gbs, "traffic": traffic, "peak_source": peak_src,
-                         "kernel": "smaq_decode per layer (one decode_v3_kernel launch)",
-                         "algorithmic_bytes_per_launch": bpl, "launch_us": launch_ms * 1e3,
-                         "launch_us_isolated": layer_ms * 1e3,
-                         "launch_time": "timed region / launches; isolated = one launch between two events"},
-            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
-            "gpu_launches": a.layers * a.steps,
-            "clocks": ck,
-        }
-        if world == 1 and not a.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_sample(a)
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+    run_decode(a, rank, world)
 
 
 if __name__ == "__main__":
