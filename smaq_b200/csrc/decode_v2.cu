@@ -32,53 +32,26 @@
 
 namespace smaq {
 
-#ifndef SMAQ_ABL
-#define SMAQ_ABL 0  // profiling builds only: bit 1 skips P.V, 2 skips score MMAs, 4 skips staging;
-                    // lookup-table path: 32 skips P.V, 64 score lookups, 128 scale staging, 256 softmax
-#endif
-#ifdef SMAQ_PROF  // profiling builds only: per-phase clock totals of thread 0 of every CTA
-// [0..13] phase totals, [7] whole-CTA total, [14] whole-CTA maximum, [15] CTA count,
-// [19] cycles thread 0 spends in chunk waits, [20] chunk waits whose data had not landed, [21] chunk waits
-__device__ unsigned long long g_v3_prof[32];
-#define V3_PROF(k)                                                \
-  do {                                                            \
-    if (threadIdx.x == 0) {                                       \
-      const long long now_ = clock64();                           \
-      atomicAdd(&g_v3_prof[k], (unsigned long long)(now_ - prof_t)); \
-      prof_t = now_;                                              \
-    }                                                             \
-  } while (0)
-#else
-#define V3_PROF(k) do {} while (0)
-#endif
 constexpr int CH = 32;  // tokens per chunk
 constexpr int ST_IDX = 0, ST_V = CH * 16, ST_S = CH * 48, ST_Z = CH * 56, STAGE_BYTES = CH * 64;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
+// History weights are p = 2^(s - m + kShift) <= 64: fp16 keeps them normal down to 2^-20 of the
+// maximum, and p * scale stays finite for value scales below 1023.
+constexpr float kShift = 6.f;
 
-#ifndef SMAQ_V3_WARPS
-#define SMAQ_V3_WARPS 16
-#define SMAQ_V3_STAGES 3
-#endif
-// G <= 4 (score lookup table): warps per CTA, ring stages, CTAs per SM, partition-table size
-#ifndef SMAQ_V3_LUT_WARPS
-#define SMAQ_V3_LUT_WARPS 16
-#define SMAQ_V3_LUT_STAGES 3
-#define SMAQ_V3_LUT_CTAS 1
-#define SMAQ_V3_LUT_SEG 2048
-#endif
 template <int GM>
 struct V3Cfg {
-  static constexpr int WARPS = GM == 4 ? SMAQ_V3_LUT_WARPS : SMAQ_V3_WARPS;
+  static constexpr int WARPS = 16;
   static constexpr int THREADS = WARPS * 32;
-  static constexpr int STAGES = GM == 4 ? SMAQ_V3_LUT_STAGES : SMAQ_V3_STAGES;
-  static constexpr int CTAS = GM == 4 ? SMAQ_V3_LUT_CTAS : 1;    // resident CTAs per SM
+  static constexpr int STAGES = 3;
+  static constexpr int CTAS = 1;    // resident CTAs per SM
   static constexpr int CB_BYTES = 256 * 16 * 16;                 // fp16 codebook [c][block'][8]
   static constexpr int Q_BYTES = GM * 128 * 4;                   // fp32 query rows
   static constexpr int SZ_BYTES = 2 * 4 * CH * 2;                // fp16 scales | zeros [j][ks][slot]
   static constexpr int WARP_BYTES = STAGES * STAGE_BYTES + SZ_BYTES + 256;  // ring | s,z | misc
   static constexpr int BAR_BYTES = WARPS * STAGES * 8;
-  static constexpr int MAX_FUSED_SEG = GM == 4 ? SMAQ_V3_LUT_SEG : 2048;  // in-kernel partition table
+  static constexpr int MAX_FUSED_SEG = 2048;  // in-kernel partition table
   static constexpr int PLAN_BYTES = (MAX_FUSED_SEG + 4) * 8 + 33 * 8 + 16 + MAX_FUSED_SEG * 4;  // table | scan | flag | tokens
   static constexpr int SMEM = CB_BYTES + Q_BYTES + WARPS * WARP_BYTES + BAR_BYTES + PLAN_BYTES;
   static_assert(GM * (128 + 2) * 4 <= STAGES * STAGE_BYTES, "merge record must fit in a ring");
@@ -188,55 +161,92 @@ struct V3Lane {
 __device__ __forceinline__ uint32_t lds32(uint32_t off) { return *reinterpret_cast<const uint32_t*>(sm + off); }
 __device__ __forceinline__ uint2 lds64(uint32_t off) { return *reinterpret_cast<const uint2*>(sm + off); }
 __device__ __forceinline__ void sts16(uint32_t off, uint16_t v) { *reinterpret_cast<uint16_t*>(sm + off) = v; }
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
 __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
   uint32_t r;
   asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
 }
 
-// One 32-token chunk for one warp.  Thread (gid, tig): score/MMA-B role = head gid and the
-// tokens t = 4i + tig; P.V A role = value word gid of those tokens.  FULL: all 32 tokens valid.
-// Shared addresses are 32-bit: st = this stage, szs = fp16 scales [j][ks][slot] then zeros.
+// p * scale as fp16 hi + lo (an exact two-product: lo = fma(p, s, -hi)).  The dequantized
+// values cancel strongly around their zero points (|code * scale| ~ |zero| >> |output| for a
+// long, nearly uniform history), so one fp16 rounding per term is too coarse there.
+__device__ __forceinline__ uint32_t two_prod_lo(uint32_t p, uint32_t sc, uint32_t hi) {
+  return hfma2(p, sc, hi ^ 0x80008000u);
+}
+
+// Fold one chunk's zero-point sums into acc and clear them.  zacc rows 0..3 are value groups,
+// columns 2 tig, 2 tig + 1 heads; value row r of acc is in units of 2^-24 4^r (the fp16-subnormal
+// codes).  Folding every chunk keeps acc at sum p * value: the tensor cores' fp32 accumulation
+// never carries the two large cancelling sums (p * scale * code and p * zero) across a history.
+// keep: this thread's acc columns take the fold (false for the lo columns of the G <= 4 path).
+__device__ __forceinline__ void fold_zero(float (&acc)[8][4], float (&zacc)[4], bool keep) {
+  const int lane = threadIdx.x & 31, tig = lane & 3;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float za = __shfl_sync(0xffffffffu, zacc[0], j * 4 + tig);
+    float zb = __shfl_sync(0xffffffffu, zacc[1], j * 4 + tig);
+    if (!keep) za = zb = 0.f;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const float k0 = hh ? 1.0f / 1048576.0f : 1.0f / 16777216.0f;   // 4^r 2^-24, r = 2 hh
+      const float k1 = hh ? 1.0f / 262144.0f : 1.0f / 4194304.0f;     // r = 2 hh + 1
+      acc[2 * j + hh][0] = fmaf(za, k0, acc[2 * j + hh][0]);
+      acc[2 * j + hh][2] = fmaf(za, k1, acc[2 * j + hh][2]);
+      acc[2 * j + hh][1] = fmaf(zb, k0, acc[2 * j + hh][1]);
+      acc[2 * j + hh][3] = fmaf(zb, k1, acc[2 * j + hh][3]);
+    }
+  }
+  zacc[0] = zacc[1] = zacc[2] = zacc[3] = 0.f;
+}
+
+// The chunk's value scales and zeros as fp16, in MMA k-slot order (one token per lane).
+template <bool FULL>
+__device__ __forceinline__ void stage_scales(uint32_t st, uint32_t szs, const V3Lane& L, int nv) {
+  const int lane = threadIdx.x & 31;
+  uint2 s2 = lds64(st + ST_S + lane * 8);
+  uint2 z2 = lds64(st + ST_Z + lane * 8);
+  if (!FULL && lane >= nv) s2 = z2 = make_uint2(0u, 0u);  // rows past the end may hold anything
+  const uint32_t sp0 = pack_f16x2(bf16lo(s2.x), bf16hi(s2.x)), sp1 = pack_f16x2(bf16lo(s2.y), bf16hi(s2.y));
+  const uint32_t zp0 = pack_f16x2(bf16lo(z2.x), bf16hi(z2.x)), zp1 = pack_f16x2(bf16lo(z2.y), bf16hi(z2.y));
+  const uint32_t o = szs + L.sz_off;
+  sts16(o + 0, uint16_t(sp0)); sts16(o + 64, uint16_t(sp0 >> 16));
+  sts16(o + 128, uint16_t(sp1)); sts16(o + 192, uint16_t(sp1 >> 16));
+  sts16(o + 256, uint16_t(zp0)); sts16(o + 320, uint16_t(zp0 >> 16));
+  sts16(o + 384, uint16_t(zp1)); sts16(o + 448, uint16_t(zp1 >> 16));
+}
+
+// One 32-token chunk for one warp (G in 5..8).  Thread (gid, tig): score/MMA-B role = head gid
+// and the tokens t = 4i + tig; P.V A role = value word gid of those tokens.  FULL: all 32 tokens
+// valid.  Shared addresses are 32-bit: st = this stage, szs = fp16 scales [j][ks][slot] then
+// zeros.  History weights are p = 2^(s - m + kShift).
 template <bool FULL>
 __device__ __forceinline__ void v3_chunk(uint32_t st, uint32_t cb_s, uint32_t szs, const V3Lane& L,
                                          const uint32_t (&qa)[4][4], int G, float lscale, int nv,
                                          float (&acc)[8][4], float (&zacc)[4], float& mrun, float& lrun) {
   const int lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
-
-  // ---- the chunk's value scales and zeros as fp16, in MMA k-slot order (one token per lane)
-  if (!(SMAQ_ABL & 4)) {
-    uint2 s2 = lds64(st + ST_S + lane * 8);
-    uint2 z2 = lds64(st + ST_Z + lane * 8);
-    if (!FULL && lane >= nv) s2 = z2 = make_uint2(0u, 0u);  // rows past the end may hold anything
-    const uint32_t sp0 = pack_f16x2(bf16lo(s2.x), bf16hi(s2.x)), sp1 = pack_f16x2(bf16lo(s2.y), bf16hi(s2.y));
-    const uint32_t zp0 = pack_f16x2(bf16lo(z2.x), bf16hi(z2.x)), zp1 = pack_f16x2(bf16lo(z2.y), bf16hi(z2.y));
-    const uint32_t o = szs + L.sz_off;
-    sts16(o + 0, uint16_t(sp0)); sts16(o + 64, uint16_t(sp0 >> 16));
-    sts16(o + 128, uint16_t(sp1)); sts16(o + 192, uint16_t(sp1 >> 16));
-    sts16(o + 256, uint16_t(zp0)); sts16(o + 320, uint16_t(zp0 >> 16));
-    sts16(o + 384, uint16_t(zp1)); sts16(o + 448, uint16_t(zp1 >> 16));
-  }
+  stage_scales<FULL>(st, szs, L, nv);
   // ---- scores: 8 n-tiles of 4 tokens; thread ends with s[i] = score(head gid, token 4i + tig)
   float s[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const uint32_t w = lds32(st + ST_IDX + L.idx_off + i * 64);
-    uint4 e0, e1;
-    if (SMAQ_ABL & 16) { e0 = make_uint4(w, w, w, w); e1 = e0; } else {
-    e0 = lds128(cb_s + __byte_perm(w, L.base[0], L.sel[0]));
-    e1 = lds128(cb_s + __byte_perm(w, L.base[1], L.sel[1])); }
+    const uint4 e0 = lds128(cb_s + __byte_perm(w, L.base[0], L.sel[0]));
+    const uint4 e1 = lds128(cb_s + __byte_perm(w, L.base[1], L.sel[1]));
     float d[4] = {0.f, 0.f, 0.f, 0.f};
-    if (SMAQ_ABL & 2) { d[0] = __uint_as_float(e0.x ^ e1.w); } else {
     mma_f16_16816(d, qa[0], e0.x, e0.y);
     mma_f16_16816(d, qa[1], e0.z, e0.w);
     mma_f16_16816(d, qa[2], e1.x, e1.y);
-    mma_f16_16816(d, qa[3], e1.z, e1.w); }
+    mma_f16_16816(d, qa[3], e1.z, e1.w);
     const float sc = (d[0] + d[3]) * lscale;
     s[i] = (FULL || 4 * i + tig < nv) ? sc : -INFINITY;  // heads >= G score 0: harmless
   }
   // ---- online softmax for head gid over the 8 tokens of this thread and its 3 tig peers
-  if (!(SMAQ_ABL & 8)) {
   float mx = fmaxf(fmaxf(fmaxf(s[0], s[1]), fmaxf(s[2], s[3])), fmaxf(fmaxf(s[4], s[5]), fmaxf(s[6], s[7])));
   mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
   mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
@@ -247,34 +257,26 @@ __device__ __forceinline__ void v3_chunk(uint32_t st, uint32_t cb_s, uint32_t sz
   float ls = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    s[i] = fast_exp2(s[i] - mn);  // p; 0 for masked tokens
+    s[i] = fast_exp2(s[i] - (mn - kShift));  // p; 0 for masked tokens
     ls += s[i];
   }
   lrun = lrun * alpha + ls;
   if (__any_sync(0xffffffffu, grew)) {
-    // acc / zacc columns 2tig, 2tig+1 belong to heads 2tig, 2tig+1: fetch their alphas
+    // acc columns 2tig, 2tig+1 belong to heads 2tig, 2tig+1: fetch their alphas
     const float aa = __shfl_sync(0xffffffffu, alpha, (2 * tig) * 4);
     const float ab = __shfl_sync(0xffffffffu, alpha, (2 * tig + 1) * 4);
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
       acc[m][0] *= aa; acc[m][1] *= ab; acc[m][2] *= aa; acc[m][3] *= ab;
     }
-    zacc[0] *= aa; zacc[1] *= ab; zacc[2] *= aa; zacc[3] *= ab;
   }
-  } else { lrun += s[0] + s[1] + s[2] + s[3] + s[4] + s[5] + s[6] + s[7]; }
   __syncwarp();  // fp16 scales / zeros visible to the warp
   // ---- P.V: k-step ks covers tokens 16ks + tig + 4u (u = 0..3) = this thread's s[4ks + u]
 #pragma unroll
-  for (int ks = 0; ks < ((SMAQ_ABL & 1) ? 0 : 2); ++ks) {
+  for (int ks = 0; ks < 2; ++ks) {
     const uint32_t p01 = pack_f16x2(s[4 * ks + 0], s[4 * ks + 1]);   // k-slots 2tig, 2tig+1
     const uint32_t p23 = pack_f16x2(s[4 * ks + 2], s[4 * ks + 3]);   // k-slots 2tig+8, 2tig+9
     const uint32_t sb = szs + ks * 32 + tig * 4;
-    uint32_t b0[4], b1[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      b0[j] = hmul2(p01, lds32(sb + j * 64));
-      b1[j] = hmul2(p23, lds32(sb + j * 64 + 16));
-    }
     // zero-point term on the tensor cores: rows = value groups, B = p
     {
       uint32_t az[4] = {0u, 0u, 0u, 0u};
@@ -292,14 +294,19 @@ __device__ __forceinline__ void v3_chunk(uint32_t st, uint32_t cb_s, uint32_t sz
     const uint32_t x23[4] = {u23, u23 >> 8, v23, v23 >> 8};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
+      const uint32_t sc0 = lds32(sb + j * 64), sc1 = lds32(sb + j * 64 + 16);
+      const uint32_t bh0 = hmul2(p01, sc0), bh1 = hmul2(p23, sc1);
+      const uint32_t bl0 = two_prod_lo(p01, sc0, bh0), bl1 = two_prod_lo(p23, sc1, bh1);
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const uint32_t m0 = 0x00030003u << (4 * hh), m1 = 0x00030003u << (4 * hh + 2);
         const uint32_t a[4] = {x01[j] & m0, x01[j] & m1, x23[j] & m0, x23[j] & m1};
-        mma_f16_16816(acc[2 * j + hh], a, b0[j], b1[j]);
+        mma_f16_16816(acc[2 * j + hh], a, bh0, bh1);
+        mma_f16_16816(acc[2 * j + hh], a, bl0, bl1);
       }
     }
   }
+  fold_zero(acc, zacc, true);
   __syncwarp();
 }
 
@@ -309,6 +316,8 @@ __device__ __forceinline__ void v3_chunk(uint32_t st, uint32_t cb_s, uint32_t sz
 // sum of its 16 entries.  Lane = token.  Lane L visits block j ^ (L & 15) at step j, so the
 // eight lanes of every load phase hit eight distinct 16-byte bank groups.  The softmax keeps
 // one reference maximum per head for the warp and rescales only when a score exceeds it.
+// P.V: columns 0..3 of the MMA are the four heads with B = hi(p * scale), columns 4..7 the same
+// heads with B = lo(p * scale); the epilogue adds column g + 4 to column g.
 struct LutLane {
   uint32_t xl;     // (L & 15) << 4
   uint32_t sel;    // byte_perm selector: byte i <- byte i ^ (L & 3)
@@ -321,19 +330,7 @@ __device__ __forceinline__ void v3_chunk_lut(uint32_t st, uint32_t szs, uint32_t
                                              float (&mref)[4], float (&lsum)[4]) {
   const int lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
-  // ---- the chunk's value scales and zeros as fp16, in MMA k-slot order (one token per lane)
-  if (!(SMAQ_ABL & 128)) {
-    uint2 s2 = lds64(st + ST_S + lane * 8);
-    uint2 z2 = lds64(st + ST_Z + lane * 8);
-    if (!FULL && lane >= nv) s2 = z2 = make_uint2(0u, 0u);  // rows past the end may hold anything
-    const uint32_t sp0 = pack_f16x2(bf16lo(s2.x), bf16hi(s2.x)), sp1 = pack_f16x2(bf16lo(s2.y), bf16hi(s2.y));
-    const uint32_t zp0 = pack_f16x2(bf16lo(z2.x), bf16hi(z2.x)), zp1 = pack_f16x2(bf16lo(z2.y), bf16hi(z2.y));
-    const uint32_t o = szs + L.sz_off;
-    sts16(o + 0, uint16_t(sp0)); sts16(o + 64, uint16_t(sp0 >> 16));
-    sts16(o + 128, uint16_t(sp1)); sts16(o + 192, uint16_t(sp1 >> 16));
-    sts16(o + 256, uint16_t(zp0)); sts16(o + 320, uint16_t(zp0 >> 16));
-    sts16(o + 384, uint16_t(zp1)); sts16(o + 448, uint16_t(zp1 >> 16));
-  }
+  stage_scales<FULL>(st, szs, L, nv);
   // ---- scores of token `lane`
   const uint4 w = *reinterpret_cast<const uint4*>(sm + st + ST_IDX + lane * 16);
   // decode-layout byte order -> natural block order, then XOR-permute the bytes by (L & 15)
@@ -345,9 +342,8 @@ __device__ __forceinline__ void v3_chunk_lut(uint32_t st, uint32_t szs, uint32_t
                          __byte_perm(n3, 0, X.sel)};
   // heads (0, 1) and (2, 3) accumulate as packed fp32 pairs (one add.f32x2 per pair)
   uint64_t s01 = 0ull, s23 = 0ull;
-  if (SMAQ_ABL & 64) { s01 = r[0] | (uint64_t(r[1]) << 32); s23 = r[2] | (uint64_t(r[3]) << 32); }
 #pragma unroll
-  for (int j = 0; j < ((SMAQ_ABL & 64) ? 0 : 16); ++j) {
+  for (int j = 0; j < 16; ++j) {
     const uint32_t c256 = __byte_perm(r[j >> 2], 0, 0x4404 | ((j & 3) << 4));  // code * 256
     const ulonglong2 e = *reinterpret_cast<const ulonglong2*>(sm + (c256 | (X.xl ^ uint32_t(j << 4))));
     asm("add.rn.f32x2 %0, %0, %1;" : "+l"(s01) : "l"(e.x));
@@ -356,9 +352,9 @@ __device__ __forceinline__ void v3_chunk_lut(uint32_t st, uint32_t szs, uint32_t
   float s[4] = {__uint_as_float(uint32_t(s01)), __uint_as_float(uint32_t(s01 >> 32)),
                 __uint_as_float(uint32_t(s23)), __uint_as_float(uint32_t(s23 >> 32))};
   if (!FULL && lane >= nv) s[0] = s[1] = s[2] = s[3] = -INFINITY;
-  // ---- softmax: p = exp2(s - mref); the reference maximum only moves up
+  // ---- softmax: p = exp2(s - mref + kShift); the reference maximum only moves up
   const bool grow = (s[0] > mref[0]) | (s[1] > mref[1]) | (s[2] > mref[2]) | (s[3] > mref[3]);
-  if (!(SMAQ_ABL & 256) && __any_sync(0xffffffffu, grow)) {
+  if (__any_sync(0xffffffffu, grow)) {
     float al[4];
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
@@ -367,34 +363,36 @@ __device__ __forceinline__ void v3_chunk_lut(uint32_t st, uint32_t szs, uint32_t
       mref[g] = mn;
       lsum[g] *= al[g];
     }
-    // acc / zacc columns 2tig, 2tig+1 belong to heads 2tig, 2tig+1 (heads >= 4 unused)
-    const float aa = tig == 0 ? al[0] : tig == 1 ? al[2] : 1.f;
-    const float ab = tig == 0 ? al[1] : tig == 1 ? al[3] : 1.f;
+    // acc columns 2tig, 2tig+1 belong to heads (2tig, 2tig+1) mod 4 (columns 4..7: lo parts)
+    const float aa = (tig & 1) ? al[2] : al[0];
+    const float ab = (tig & 1) ? al[3] : al[1];
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
       acc[m][0] *= aa; acc[m][1] *= ab; acc[m][2] *= aa; acc[m][3] *= ab;
     }
-    zacc[0] *= aa; zacc[1] *= ab; zacc[2] *= aa; zacc[3] *= ab;
   }
   // p in fp16, k-slot order per head (the B operand layout of the P.V MMA)
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
-    const float pg = (SMAQ_ABL & 256) ? s[g] : fast_exp2(s[g] - mref[g]);  // 0 for masked tokens
+    const float pg = fast_exp2(s[g] - (mref[g] - kShift));  // 0 for masked tokens
     lsum[g] += pg;
     sts16(pb + g * 64 + L.sz_off, __half_as_ushort(__float2half_rn(pg)));
   }
   __syncwarp();  // p, fp16 scales / zeros visible to the warp
   // ---- P.V: k-step ks covers tokens 16ks + tig + 4u (u = 0..3)
+  const bool lo_col = gid >= 4;
 #pragma unroll
-  for (int ks = 0; ks < ((SMAQ_ABL & 32) ? 0 : 2); ++ks) {
-    const uint32_t p01 = gid < 4 ? lds32(pb + gid * 64 + ks * 32 + tig * 4) : 0u;        // k-slots 2tig, 2tig+1
-    const uint32_t p23 = gid < 4 ? lds32(pb + gid * 64 + ks * 32 + tig * 4 + 16) : 0u;   // k-slots 2tig+8, 2tig+9
+  for (int ks = 0; ks < 2; ++ks) {
+    const uint32_t p01 = lds32(pb + (gid & 3) * 64 + ks * 32 + tig * 4);        // k-slots 2tig, 2tig+1
+    const uint32_t p23 = lds32(pb + (gid & 3) * 64 + ks * 32 + tig * 4 + 16);   // k-slots 2tig+8, 2tig+9
     const uint32_t sb = szs + ks * 32 + tig * 4;
     uint32_t b0[4], b1[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      b0[j] = hmul2(p01, lds32(sb + j * 64));
-      b1[j] = hmul2(p23, lds32(sb + j * 64 + 16));
+      const uint32_t sc0 = lds32(sb + j * 64), sc1 = lds32(sb + j * 64 + 16);
+      const uint32_t h0 = hmul2(p01, sc0), h1 = hmul2(p23, sc1);
+      b0[j] = lo_col ? two_prod_lo(p01, sc0, h0) : h0;
+      b1[j] = lo_col ? two_prod_lo(p23, sc1, h1) : h1;
     }
     {
       uint32_t az[4] = {0u, 0u, 0u, 0u};
@@ -420,6 +418,7 @@ __device__ __forceinline__ void v3_chunk_lut(uint32_t st, uint32_t szs, uint32_t
       }
     }
   }
+  fold_zero(acc, zacc, tig < 2);
   __syncwarp();
 }
 
@@ -713,11 +712,6 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3
   int* sntab = arrive_flag + 4;
   const int64_t* plan = p.plan;
   const int* ntab = nullptr;
-#ifdef SMAQ_PROF
-  long long prof_t = clock64();
-  const long long prof_t0 = prof_t;
-  if (threadIdx.x == 0) atomicAdd(&g_v3_prof[15], 1ull);
-#endif
   if (p.fused) {
     // overlapped launch: the next launch on the stream may be scheduled now; its CTAs take an SM
     // only when one of ours has exited
@@ -783,7 +777,6 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3
       if (e == 0) v3_final_merge(p, plan, ntab, pair);
     }
   }
-  V3_PROF(0);
   if (lo >= hi) return;
 
   // per-lane constants of the score gather (B column = (token gid>>1, half gid&1), block quad tig)
@@ -858,7 +851,6 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3
     if (s & 1) {
       // ---------------- exact recent window: warp w takes 8-token chunks w, w + WARPS, ...
       __syncthreads();  // qs complete
-      V3_PROF(8);
       const int ntok = int(t1 - t0);
       WarpState<GM> ws;
       ws.init();
@@ -866,7 +858,6 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3
       // keeps its latency (key row loads, then value row loads) to about one round
       for (int ch = wid; ch * 8 < ntok; ch += WARPS)
         v3_window_chunk<GM>(p, qs, b, h, t0 + int64_t(ch) * 8, min(8, ntok - ch * 8), ws);
-      V3_PROF(9);
 #pragma unroll
       for (int g = 0; g < GM; ++g) {
 #pragma unroll
@@ -877,11 +868,8 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3
         }
       }
       __syncthreads();
-      V3_PROF(10);
       v3_merge<GM, WARPS>(p, reinterpret_cast<const float*>(wreg0), C::WARP_BYTES / 4, c + s);
-      V3_PROF(11);
       if (p.fused) v3_arrive(p, plan, ntab, s, arrive_flag);
-      V3_PROF(1);
       continue;
     }
 
@@ -910,7 +898,6 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3
           const int cc = c0 + k * (C::THREADS >> 4);
           cw[k] = cc < p.nc ? __ldg(cb4 + cc) : make_uint4(0u, 0u, 0u, 0u);
         }
-        V3_PROF(2);
         __syncthreads();  // qs complete
         float qv[4][8];
 #pragma unroll
@@ -943,7 +930,6 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3
           *reinterpret_cast<float4*>(cb + (cc * 16 + blk) * 16) = make_float4(r4[0], r4[1], r4[2], r4[3]);
         }
       }
-      V3_PROF(3);
     } else if (!cb_ready) {  // first history segment: copy the codebook while its first chunks load
       // codebook -> shared, entry (block b, code cc) at cc * 256 + sigma(b) * 16
       for (int u = threadIdx.x; u < 16 * 256; u += blockDim.x) {
@@ -986,21 +972,10 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3
     for (int i = 0; i < 4; ++i) X.sel |= uint32_t(i ^ (lane & 3)) << (4 * i);
     X.swp8 = (lane & 8) != 0;
     X.swp4 = (lane & 4) != 0;
-    V3_PROF(4);
     for (int i = 0; i < mine; ++i) {
       const int stg = i % ST;
       uint8_t* stage = wreg + stg * STAGE_BYTES;
-#ifdef SMAQ_PROF
-      const long long w0_ = clock64();
-      if (threadIdx.x == 0 && !mbar_test(&wbar[stg], (phase >> stg) & 1u)) atomicAdd(&g_v3_prof[20], 1ull);
-#endif
       if (!failed && !mbar_wait(&wbar[stg], (phase >> stg) & 1u)) failed = true;
-#ifdef SMAQ_PROF
-      if (threadIdx.x == 0) {
-        atomicAdd(&g_v3_prof[19], (unsigned long long)(clock64() - w0_));
-        atomicAdd(&g_v3_prof[21], 1ull);
-      }
-#endif
       phase ^= 1u << stg;
       const int nv = min(CH, ntok - (wid + WARPS * i) * CH);
       if constexpr (GM == 4) {
@@ -1020,69 +995,55 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3
       }
     }
 
-    V3_PROF(5);
-    // ---- warp epilogue: per head (m, l, zero term) -> misc, then the value sums -> record
+    // ---- warp epilogue: per head (m, l), then the value sums -> record (the zero-point terms
+    // were folded into acc chunk by chunk)
     if constexpr (GM == 4) {
 #pragma unroll
       for (int g = 0; g < 4; ++g) {
         const float l = warp_sum(lsum[g]);
         if (lane == 0) {
-          rec[GM * D + g * 2] = (mine && mref[g] != -INFINITY) ? mref[g] * kLn2 : -INFINITY;  // natural log
+          rec[GM * D + g * 2] = (mine && mref[g] != -INFINITY) ? (mref[g] - kShift) * kLn2 : -INFINITY;
           rec[GM * D + g * 2 + 1] = l;
         }
       }
-      __syncwarp();  // p buffer (misc) reads done before the zero terms reuse it
+      // columns 4..7 hold the lo parts of heads 0..3: add them to columns 0..3
+#pragma unroll
+      for (int m = 0; m < 8; ++m)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[m][e] += __shfl_xor_sync(0xffffffffu, acc[m][e], 2);
     } else {
       float l = lrun;
       l += __shfl_xor_sync(0xffffffffu, l, 1);
       l += __shfl_xor_sync(0xffffffffu, l, 2);
       if (tig == 0 && gid < GM) {
-        rec[GM * D + gid * 2] = (mine && mrun != -INFINITY) ? mrun * kLn2 : -INFINITY;  // natural log
+        rec[GM * D + gid * 2] = (mine && mrun != -INFINITY) ? (mrun - kShift) * kLn2 : -INFINITY;  // natural log
         rec[GM * D + gid * 2 + 1] = l;
       }
     }
-    // zero term: zacc row gid = value group j (< 4), columns 2tig, 2tig+1 = heads
-    if (gid < 4) {
-      if (2 * tig < GM) misc[(2 * tig) * 4 + gid] = zacc[0];
-      if (2 * tig + 1 < GM) misc[(2 * tig + 1) * 4 + gid] = zacc[1];
-    }
-    __syncwarp();
     {
       const int ga = 2 * tig, gb = 2 * tig + 1;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float za = ga < GM ? misc[ga * 4 + j] : 0.f;
-        const float zb = gb < GM ? misc[gb * 4 + j] : 0.f;
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const int d0 = 32 * j + 4 * gid + 2 * hh;       // row gid -> code r = 2hh; row gid+8 -> 2hh+1
           const float s0 = hh ? 1048576.0f : 16777216.0f;  // 2^24 * 4^-r
           const float s1 = hh ? 262144.0f : 4194304.0f;    // 2^24 * 4^-(r+1)
           if (ga < GM) {
-            rec[ga * D + d0] = fmaf(acc[2 * j + hh][0], s0, za);
-            rec[ga * D + d0 + 1] = fmaf(acc[2 * j + hh][2], s1, za);
+            rec[ga * D + d0] = acc[2 * j + hh][0] * s0;
+            rec[ga * D + d0 + 1] = acc[2 * j + hh][2] * s1;
           }
           if (gb < GM) {
-            rec[gb * D + d0] = fmaf(acc[2 * j + hh][1], s0, zb);
-            rec[gb * D + d0 + 1] = fmaf(acc[2 * j + hh][3], s1, zb);
+            rec[gb * D + d0] = acc[2 * j + hh][1] * s0;
+            rec[gb * D + d0 + 1] = acc[2 * j + hh][3] * s1;
           }
         }
       }
     }
     __syncthreads();
-    V3_PROF(12);
     v3_merge<GM, WARPS>(p, reinterpret_cast<const float*>(wreg0), C::WARP_BYTES / 4, c + s);
-    V3_PROF(13);
     if (p.fused) v3_arrive(p, plan, ntab, s, arrive_flag);
-    V3_PROF(6);
   }
-#ifdef SMAQ_PROF
-  if (threadIdx.x == 0) {  // whole-CTA time: sum (7) and maximum (14) over CTAs
-    const unsigned long long tot = (unsigned long long)(clock64() - prof_t0);
-    atomicAdd(&g_v3_prof[7], tot);
-    atomicMax(&g_v3_prof[14], tot);
-  }
-#endif
   if (failed && lane == 0) atomicExch(reinterpret_cast<int*>(p.plan + p.n_seg + 2), 1);
 }
 
@@ -1207,7 +1168,6 @@ __device__ __forceinline__ void sk_chunk(uint32_t st, uint32_t szs, uint32_t pb,
     for (int m = 0; m < 8; ++m) {
       acc[m][0] *= al2[0]; acc[m][1] *= al2[1]; acc[m][2] *= al2[0]; acc[m][3] *= al2[1];
     }
-    zacc[0] *= al2[0]; zacc[1] *= al2[1]; zacc[2] *= al2[0]; zacc[3] *= al2[1];
   }
   // p -> fp16 in the P.V B layout: row = head, k-slot of token t (see V3Lane::sz_off)
 #pragma unroll
@@ -1219,7 +1179,7 @@ __device__ __forceinline__ void sk_chunk(uint32_t st, uint32_t szs, uint32_t pb,
       const uint32_t slot = uint32_t(2 * (16 * T + 2 * v + (u & 1) + 8 * (u >> 1)));
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        const float pv = fast_exp2(s[T][2 * r + c] - mref[c]);
+        const float pv = fast_exp2(s[T][2 * r + c] - (mref[c] - kShift));
         lsum[c] += pv;
         sts16(pb + (2 * tig + c) * 64 + slot, __half_as_ushort(__float2half_rn(pv)));
       }
@@ -1232,12 +1192,6 @@ __device__ __forceinline__ void sk_chunk(uint32_t st, uint32_t szs, uint32_t pb,
     const uint32_t p01 = lds32(pb + gid * 64 + ks * 32 + tig * 4);
     const uint32_t p23 = lds32(pb + gid * 64 + ks * 32 + tig * 4 + 16);
     const uint32_t sb = szs + ks * 32 + tig * 4;
-    uint32_t b0[4], b1[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      b0[j] = hmul2(p01, lds32(sb + j * 64));
-      b1[j] = hmul2(p23, lds32(sb + j * 64 + 16));
-    }
     {
       uint32_t az[4] = {0u, 0u, 0u, 0u};
       if (gid < 4) {
@@ -1254,14 +1208,19 @@ __device__ __forceinline__ void sk_chunk(uint32_t st, uint32_t szs, uint32_t pb,
     const uint32_t x23[4] = {u23, u23 >> 8, v23, v23 >> 8};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
+      const uint32_t sc0 = lds32(sb + j * 64), sc1 = lds32(sb + j * 64 + 16);
+      const uint32_t bh0 = hmul2(p01, sc0), bh1 = hmul2(p23, sc1);
+      const uint32_t bl0 = two_prod_lo(p01, sc0, bh0), bl1 = two_prod_lo(p23, sc1, bh1);
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const uint32_t m0 = 0x00030003u << (4 * hh), m1 = 0x00030003u << (4 * hh + 2);
         const uint32_t a[4] = {x01[j] & m0, x01[j] & m1, x23[j] & m0, x23[j] & m1};
-        mma_f16_16816(acc[2 * j + hh], a, b0[j], b1[j]);
+        mma_f16_16816(acc[2 * j + hh], a, bh0, bh1);
+        mma_f16_16816(acc[2 * j + hh], a, bl0, bl1);
       }
     }
   }
+  fold_zero(acc, zacc, true);
   __syncwarp();
 }
 
@@ -1488,7 +1447,7 @@ __global__ void __launch_bounds__(SCfg::THREADS, 1) decode_s_kernel(DecodeParams
       l += __shfl_xor_sync(0xffffffffu, l, 16);
       if (gid == 0) {
         const int g = 2 * tig + cc;
-        rec[GM * D + g * 2] = (mine && mref[cc] != -INFINITY) ? mref[cc] * kLn2 : -INFINITY;
+        rec[GM * D + g * 2] = (mine && mref[cc] != -INFINITY) ? (mref[cc] - kShift) * kLn2 : -INFINITY;
         rec[GM * D + g * 2 + 1] = l;
       }
     }
@@ -1589,19 +1548,6 @@ static int launch_v3_t(DecodeParams& p, int grid_req, cudaStream_t s, int* grid_
 
 int decode_v2_max_fused_segments(int G) { return G <= 4 ? V3Cfg<4>::MAX_FUSED_SEG : V3Cfg<8>::MAX_FUSED_SEG; }
 
-#ifdef SMAQ_PROF
-// Profiling builds only: copy the 32 counters of g_v3_prof to `out` (room for 32), then
-// optionally clear them.
-extern "C" int smaq_debug_v3_prof(unsigned long long* out, int reset) {
-  cudaDeviceSynchronize();
-  cudaMemcpyFromSymbol(out, g_v3_prof, sizeof(unsigned long long) * 32);
-  if (reset) {
-    unsigned long long z[32] = {};
-    cudaMemcpyToSymbol(g_v3_prof, z, sizeof(z));
-  }
-  return 0;
-}
-#endif
 
 int launch_decode_v2(DecodeParams& p, int grid_req, cudaStream_t s, int* grid_out, bool query_only) {
   if (p.G <= 4) return launch_v3_t<4>(p, grid_req, s, grid_out, query_only);

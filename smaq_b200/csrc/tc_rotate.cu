@@ -364,7 +364,10 @@ __global__ void __launch_bounds__(TR_THREADS, 1) tc_scalar_key_kernel(
       uint4 raw[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) raw[j] = *reinterpret_cast<const uint4*>(R + sw128_chunk(t, (j < 4 ? j : j + 4) + 4 * hf));
-      mbar_arrive(&bars->a_empty[s]);  // the stage may be refilled once every row is in registers
+      // the stage may be refilled once every row is in registers; the refill is an async-proxy
+      // (TMA) write, so the generic-proxy reads above are ordered before it by a proxy fence
+      fence_async_smem();
+      mbar_arrive(&bars->a_empty[s]);
       // sum of squares in the SIMT kernel's order: partials of 4 elements (fma chain) per SIMT
       // lane, then the xor-butterfly tree of warp_sum (lanes 16 apart, then 8, 4, 2, 1)
       float p[16];  // p[j] = partial of SIMT lane (j < 8 ? 8hf + j : 16 + 8hf + j - 8)
