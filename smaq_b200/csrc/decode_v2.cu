@@ -146,6 +146,7 @@ __device__ __forceinline__ void v3_merge(const DecodeParams& p, const float* rec
       out[G * D + g * 2 + 1] = L;
     }
   }
+  fence_proxy_async_smem();  // the records sit in the rings, which bulk copies refill next
   __syncthreads();
 }
 
@@ -307,6 +308,7 @@ __device__ __forceinline__ void v3_chunk(uint32_t st, uint32_t cb_s, uint32_t sz
     }
   }
   fold_zero(acc, zacc, true);
+  fence_proxy_async_smem();  // the stage is refilled by a bulk copy after this barrier
   __syncwarp();
 }
 
@@ -419,6 +421,7 @@ __device__ __forceinline__ void v3_chunk_lut(uint32_t st, uint32_t szs, uint32_t
     }
   }
   fold_zero(acc, zacc, tig < 2);
+  fence_proxy_async_smem();  // the stage is refilled by a bulk copy after this barrier
   __syncwarp();
 }
 
@@ -1221,6 +1224,7 @@ __device__ __forceinline__ void sk_chunk(uint32_t st, uint32_t szs, uint32_t pb,
     }
   }
   fold_zero(acc, zacc, true);
+  fence_proxy_async_smem();  // the stage is refilled by a bulk copy after this barrier
   __syncwarp();
 }
 

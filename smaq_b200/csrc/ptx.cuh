@@ -64,6 +64,13 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Order this thread's earlier generic-proxy accesses to shared memory before later async-proxy
+// (bulk copy / TMA) writes to it: a thread that read a staging buffer executes this before the
+// barrier after which the buffer is refilled by a bulk copy.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Prefetch [src, src + bytes) into L2 (bulk, no shared-memory destination).  src 16-byte
 // aligned, bytes a multiple of 16.
 __device__ __forceinline__ void l2_prefetch(const void* src, uint32_t bytes) {
