@@ -70,6 +70,7 @@ def test_cfg1_layer_matches_oracle(cuda, codebook):
         for h in (range(spec.hkv) if b != 7 else (3,)):
             ref = _bvq_pair_ref(L, codebook, b, h, G)
             worst = max(worst, O.rel_l2(out[b, h * G:(h + 1) * G], ref))
+    print(f"cfg1 worst rel-L2 {worst:.3e}")
     assert worst <= TOL_BF16, worst
 
 
@@ -85,6 +86,7 @@ def test_cfg4_layer_matches_oracle_and_head_shard(cuda, codebook):
     for b, h in ((0, 0), (0, 5), (3, 7), (2, 2)):
         ref = _bvq_pair_ref(L, codebook, b, h, G)
         worst = max(worst, O.rel_l2(out[b, h * G:(h + 1) * G], ref))
+    print(f"cfg4 worst rel-L2 {worst:.3e}")
     assert worst <= TOL_BF16, worst
     shard = bench.decode_spec("longctx", 8)
     assert (shard.hq, shard.hkv) == (8, 1)
@@ -132,6 +134,7 @@ def test_cfg3_paged_layer_matches_oracle(cuda):
         ref, _, _ = O.hybrid_attention(tn(L["q"][b:b + 1]), "bf16", K, V, tn(L["rk"][b]), tn(L["rv"][b]),
                                        bench.PG_HQ, bench.PG_HKV)
         worst = max(worst, O.rel_l2(out[b:b + 1], ref))
+    print(f"cfg3 worst rel-L2 {worst:.3e}")
     assert worst <= TOL_BF16, worst
 
 
