@@ -519,6 +519,173 @@ __device__ __forceinline__ void v3_window_chunk(const DecodeParams& p, const flo
   }
 }
 
+// ---------------------------------------------------------------- exact window on tensor cores
+// Used when the window rows are bf16 or fp16 of the query's dtype with 16-byte aligned rows.
+// Warp w takes 8-token chunks w, w + WARPS, ... of the window segment.
+//  * Scores: mma m16n8k16, A = query rows (head gid; rows 8-15 zero), B = key rows (token gid).
+//    The contraction runs over the head dim in a permuted order so that lane tig reads dims
+//    [32 tig, 32 tig + 32) of its token's key row with four 16-byte loads: k-step ks takes dims
+//    32 tig + 4 ks + {0,1} as fragment slots (2 tig, 2 tig + 1) and + {2,3} as (2 tig + 8, +9);
+//    the query fragments use the same order, so every dot product is the plain one.
+//  * P.V: mma m16n8k8, A = the weights in the score fragment layout (head gid, tokens 2 tig,
+//    2 tig + 1) split into hi + lo of the value dtype, B = the chunk's value rows staged in
+//    shared memory (row pitch WIN_ROW: the 8 rows of one ldmatrix phase hit 8 distinct bank
+//    groups) and read transposed by ldmatrix.
+// This is _exact_scores / _apply_weights of smaq/score.py:99-124 in the kernel's softmax units
+// (natural log, as the merge records expect).
+constexpr int WIN_ROW = 272;
+
+__device__ __forceinline__ bool window_mma_ok(const DecodeParams& p) {
+  return (p.r_dtype == SMAQ_BF16 || p.r_dtype == SMAQ_F16) && p.r_dtype == p.q_dtype &&
+         ((reinterpret_cast<uintptr_t>(p.rk) | reinterpret_cast<uintptr_t>(p.rv)) & 15) == 0 &&
+         ((p.r_sb | p.r_st | p.r_sh) & 7) == 0;
+}
+
+template <bool BF>
+__device__ __forceinline__ uint32_t pack16x2(float lo, float hi) {
+  uint32_t r;
+  if constexpr (BF) asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  else asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+template <bool BF>
+__device__ __forceinline__ float2 unpack16x2(uint32_t w) {
+  if constexpr (BF) return make_float2(bf16lo(w), bf16hi(w));
+  else return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
+// D[16x8] = A[16x16] B[16x8] + D with A rows 8-15 zero: only D rows 0-7 (d0, d1) are kept.
+template <bool BF>
+__device__ __forceinline__ void mma_k16_top(float& d0, float& d1, uint32_t a0, uint32_t a2, uint32_t b0,
+                                            uint32_t b1) {
+  float x2, x3;
+  const uint32_t z = 0u;
+  const float zf = 0.f;
+  if constexpr (BF)
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%10,%10};"
+        : "+f"(d0), "+f"(d1), "=f"(x2), "=f"(x3)
+        : "r"(a0), "r"(z), "r"(a2), "r"(z), "r"(b0), "r"(b1), "f"(zf));
+  else
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%10,%10};"
+        : "+f"(d0), "+f"(d1), "=f"(x2), "=f"(x3)
+        : "r"(a0), "r"(z), "r"(a2), "r"(z), "r"(b0), "r"(b1), "f"(zf));
+}
+
+// D[16x8] = A[16x8] B[8x8] + D, A rows 8-15 zero.
+template <bool BF>
+__device__ __forceinline__ void mma_k8_top(float& d0, float& d1, uint32_t a0, uint32_t b0) {
+  float x2, x3;
+  const uint32_t z = 0u;
+  const float zf = 0.f;
+  if constexpr (BF)
+    asm("mma.sync.aligned.m16n8k8.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%7,%7};"
+        : "+f"(d0), "+f"(d1), "=f"(x2), "=f"(x3)
+        : "r"(a0), "r"(z), "r"(b0), "f"(zf));
+  else
+    asm("mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%7,%7};"
+        : "+f"(d0), "+f"(d1), "=f"(x2), "=f"(x3)
+        : "r"(a0), "r"(z), "r"(b0), "f"(zf));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+
+// The window tokens [t0, t0 + ntok) of pair (b, h) for this warp; writes the warp's merge record
+// (acc[GM][D], then (m, l) per head, natural-log units) at rec.  ring: >= 16 * WIN_ROW bytes of
+// this warp's shared memory, free for the duration.  Key and value rows go to shared memory by
+// cp.async (zero-filled past the window's end), so no registers are held while they load.
+template <int GM, int WARPS, bool BF>
+__device__ __forceinline__ void v3_window_mma(const DecodeParams& p, const float* qs, int b, int h, int64_t t0,
+                                              int ntok, uint8_t* ring, float* rec) {
+  constexpr int D = 128;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int G = p.G;
+  const int64_t base = b * p.r_sb + h * p.r_sh;
+  float m = -INFINITY, l = 0.f;  // l: this lane's partial row sum
+  float acc[16][2];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) acc[j][0] = acc[j][1] = 0.f;
+  const uint32_t ks_s = smem_u32(ring), vs_s = ks_s + 8 * WIN_ROW;  // shared-window addresses
+  const uint32_t ks_o = uint32_t(ring - sm);                        // offset for lds64
+  const float scale = p.scale;
+  for (int ch = wid; ch * 8 < ntok; ch += WARPS) {
+    const int64_t tb = t0 + int64_t(ch) * 8;
+    const int nvalid = min(8, ntok - ch * 8);
+    // 8 key rows then 8 value rows, 16 pieces of 16 bytes each
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = lane + 32 * k, tok = (i >> 4) & 7, c16 = i & 15;
+      const uint16_t* row = static_cast<const uint16_t*>(k < 4 ? p.rk : p.rv) + base +
+                            (tb + min(tok, nvalid - 1)) * p.r_st;
+      cp_async16(ks_s + (i >> 4) * WIN_ROW + c16 * 16, row + c16 * 8, tok < nvalid ? 16u : 0u);
+    }
+    cp_async_wait_all();
+    __syncwarp();
+    // scores of head gid for tokens 2 tig, 2 tig + 1
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (gid < GM) q4 = *reinterpret_cast<const float4*>(qs + gid * D + 32 * tig + 4 * ks);
+      const uint2 kb = lds64(ks_o + gid * WIN_ROW + 64 * tig + 8 * ks);
+      mma_k16_top<BF>(s0, s1, pack16x2<BF>(q4.x, q4.y), pack16x2<BF>(q4.z, q4.w), kb.x, kb.y);
+    }
+    // online softmax (the 4 lanes of group gid hold head gid)
+    const float x0 = (2 * tig < nvalid) ? s0 * scale : -INFINITY;
+    const float x1 = (2 * tig + 1 < nvalid) ? s1 * scale : -INFINITY;
+    float cm = fmaxf(x0, x1);
+    cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 1));
+    cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 2));
+    const float mn = fmaxf(m, cm);
+    const float alpha = expf(m - mn);
+    const float p0 = expf(x0 - mn), p1 = expf(x1 - mn);
+    m = mn;
+    l = l * alpha + (p0 + p1);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      acc[j][0] *= alpha;
+      acc[j][1] *= alpha;
+    }
+    const uint32_t phi = pack16x2<BF>(p0, p1);
+    const float2 ph = unpack16x2<BF>(phi);
+    const uint32_t plo = pack16x2<BF>(p0 - ph.x, p1 - ph.y);
+#pragma unroll
+    for (int j4 = 0; j4 < 4; ++j4) {
+      uint32_t vb[4];
+      ldsm_x4_trans(vs_s + (lane & 7) * WIN_ROW + (4 * j4 + (lane >> 3)) * 16, vb);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        mma_k8_top<BF>(acc[4 * j4 + u][0], acc[4 * j4 + u][1], phi, vb[u]);
+        mma_k8_top<BF>(acc[4 * j4 + u][0], acc[4 * j4 + u][1], plo, vb[u]);
+      }
+    }
+    __syncwarp();  // staging area free for the next chunk
+  }
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
+  if (gid < GM) {  // (the record overwrites the staging area: every lane is past its last read)
+    const bool live = gid < G;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float2 v = make_float2(0.f, 0.f);
+      if (live) v = make_float2(acc[j][0], acc[j][1]);
+      *reinterpret_cast<float2*>(rec + gid * D + 8 * j + 2 * tig) = v;
+    }
+    if (tig == 0) {
+      rec[GM * D + gid * 2] = live ? m : -INFINITY;
+      rec[GM * D + gid * 2 + 1] = live ? l : 0.f;
+    }
+  }
+}
+
 // The stream-K partition (what decode_plan_kernel writes) computed by one CTA into shared
 // memory: prefix cost of every segment, then total and per-CTA slice.  Block-wide scan.
 __device__ void v3_plan(const DecodeParams& p, int64_t* plan, int64_t* scratch /* [33] */, int* ntab) {
@@ -738,6 +905,16 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3
   // Overlapped launch: the first history chunks of this CTA are requested before waiting for
   // the previous launch on the stream (the caller promises that launch writes neither the
   // history rows nor the lengths); queries, the window, outputs and the workspace only after.
+  if (GM != 4 && lo < hi) {
+    // codebook -> shared, entry (block b, code cc) at cc * 256 + sigma(b) * 16; a constant of
+    // the launch, so copied before the dependency wait (published by the loop's first barrier)
+    for (int u = threadIdx.x; u < 16 * 256; u += blockDim.x) {
+      const int blk = u >> 8, cc = u & 255;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (cc < p.nc) v = __ldg(reinterpret_cast<const uint4*>(cb16) + blk * p.nc + cc);
+      *reinterpret_cast<uint4*>(cb + cc * 256 + cb_sigma(blk) * 16) = v;
+    }
+  }
   int pre_s = -1;
   if (p.pdl) {
     if (lo < hi) {
@@ -797,7 +974,6 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3
       L.sel[kp] = 0x6504u | (uint32_t((tig & 1) * 2 + kp) << 4);
     }
   }
-  bool cb_ready = false;
   const uint32_t cb_s = uint32_t(cb - sm);
   const uint32_t ring_s = uint32_t(wreg - sm);
   __syncthreads();
@@ -859,15 +1035,20 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3
       ws.init();
       // 8 tokens per warp and round: the window is short, so spreading it over every warp
       // keeps its latency (key row loads, then value row loads) to about one round
-      for (int ch = wid; ch * 8 < ntok; ch += WARPS)
-        v3_window_chunk<GM>(p, qs, b, h, t0 + int64_t(ch) * 8, min(8, ntok - ch * 8), ws);
+      if (window_mma_ok(p)) {
+        if (p.r_dtype == SMAQ_BF16) v3_window_mma<GM, WARPS, true>(p, qs, b, h, t0, ntok, wreg, rec);
+        else v3_window_mma<GM, WARPS, false>(p, qs, b, h, t0, ntok, wreg, rec);
+      } else {
+        for (int ch = wid; ch * 8 < ntok; ch += WARPS)
+          v3_window_chunk<GM>(p, qs, b, h, t0 + int64_t(ch) * 8, min(8, ntok - ch * 8), ws);
 #pragma unroll
-      for (int g = 0; g < GM; ++g) {
+        for (int g = 0; g < GM; ++g) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) rec[g * D + lane * 4 + e] = g < G ? ws.acc[g][e] : 0.f;
-        if (lane == 0) {
-          rec[GM * D + g * 2] = g < G ? ws.m[g] : -INFINITY;
-          rec[GM * D + g * 2 + 1] = g < G ? ws.l[g] : 0.f;
+          for (int e = 0; e < 4; ++e) rec[g * D + lane * 4 + e] = g < G ? ws.acc[g][e] : 0.f;
+          if (lane == 0) {
+            rec[GM * D + g * 2] = g < G ? ws.m[g] : -INFINITY;
+            rec[GM * D + g * 2 + 1] = g < G ? ws.l[g] : 0.f;
+          }
         }
       }
       __syncthreads();
@@ -933,15 +1114,6 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3
           *reinterpret_cast<float4*>(cb + (cc * 16 + blk) * 16) = make_float4(r4[0], r4[1], r4[2], r4[3]);
         }
       }
-    } else if (!cb_ready) {  // first history segment: copy the codebook while its first chunks load
-      // codebook -> shared, entry (block b, code cc) at cc * 256 + sigma(b) * 16
-      for (int u = threadIdx.x; u < 16 * 256; u += blockDim.x) {
-        const int blk = u >> 8, cc = u & 255;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (cc < p.nc) v = __ldg(reinterpret_cast<const uint4*>(cb16) + blk * p.nc + cc);
-        *reinterpret_cast<uint4*>(cb + cc * 256 + cb_sigma(blk) * 16) = v;
-      }
-      cb_ready = true;
     }
     __syncthreads();  // qs and codebook complete
     // A fragments of the score MMA: rows (head gid, half 0) and (head gid, half 1); k-step ks
@@ -1341,15 +1513,20 @@ __global__ void __launch_bounds__(SCfg::THREADS, 1) decode_s_kernel(DecodeParams
       const int ntok = int(t1 - t0);
       WarpState<GM> ws;
       ws.init();
-      for (int ch = wid; ch * 8 < ntok; ch += WARPS)
-        v3_window_chunk<GM>(p, qs, b, h, t0 + int64_t(ch) * 8, min(8, ntok - ch * 8), ws);
+      if (window_mma_ok(p)) {
+        if (p.r_dtype == SMAQ_BF16) v3_window_mma<GM, WARPS, true>(p, qs, b, h, t0, ntok, wreg, rec);
+        else v3_window_mma<GM, WARPS, false>(p, qs, b, h, t0, ntok, wreg, rec);
+      } else {
+        for (int ch = wid; ch * 8 < ntok; ch += WARPS)
+          v3_window_chunk<GM>(p, qs, b, h, t0 + int64_t(ch) * 8, min(8, ntok - ch * 8), ws);
 #pragma unroll
-      for (int g = 0; g < GM; ++g) {
+        for (int g = 0; g < GM; ++g) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) rec[g * D + lane * 4 + e] = g < G ? ws.acc[g][e] : 0.f;
-        if (lane == 0) {
-          rec[GM * D + g * 2] = g < G ? ws.m[g] : -INFINITY;
-          rec[GM * D + g * 2 + 1] = g < G ? ws.l[g] : 0.f;
+          for (int e = 0; e < 4; ++e) rec[g * D + lane * 4 + e] = g < G ? ws.acc[g][e] : 0.f;
+          if (lane == 0) {
+            rec[GM * D + g * 2] = g < G ? ws.m[g] : -INFINITY;
+            rec[GM * D + g * 2 + 1] = g < G ? ws.l[g] : 0.f;
+          }
         }
       }
       __syncthreads();

@@ -80,6 +80,12 @@ __device__ __forceinline__ void l2_prefetch(const void* src, uint32_t bytes) {
 // Programmatic dependent launch (sm_90+): wait until the previous grid on the stream has
 // completed and its memory is visible; allow the next grid on the stream to be scheduled.
 // Both are no-ops for a launch without the programmatic-serialization attribute.
+// 16-byte global -> shared copy (cp.async, L2 only); src_bytes 0 fills the 16 bytes with zeros.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
