@@ -6,10 +6,11 @@ namespace smaq {
 
 constexpr int DEC_WARPS = 8;
 constexpr int DEC_THREADS = DEC_WARPS * 32;
-// Partition weight of one exact-window token in units of one compressed token-head (an exact
-// bf16 K+V token is 512 B against 48-114 B for a compressed one)
+// Partition weight of one exact-window token in units of one compressed token-head: measured
+// time per window token (an exact bf16 K+V row of 512 B, read at full load latency) against one
+// streamed compressed token-head; 12 balances the single-launch kernels' CTAs best
 #ifndef SMAQ_RECENT_COST
-#define SMAQ_RECENT_COST 8
+#define SMAQ_RECENT_COST 12
 #endif
 constexpr int RECENT_COST = SMAQ_RECENT_COST;
 constexpr int DEC_MAX_CTAS_PER_SM = 8;  // grid cap when the caller lets the library choose

@@ -40,6 +40,12 @@ constexpr float kLn2 = 0.6931471805599453f;
 // maximum, and p * scale stays finite for value scales below 1023.
 constexpr float kShift = 6.f;
 
+// Floats of shared scratch the final merge of a pair with nt slots needs (G query heads).
+__host__ __device__ constexpr int final_scratch_floats(int G, int nt) { return 2 * G * nt + 2 * G + 3 + 512 * 8; }
+// Row pitch of the exact window's staged key / value rows (bytes): 8 rows of one ldmatrix
+// phase fall in 8 distinct 16-byte bank groups.
+constexpr int WIN_ROW = 272;
+
 template <int GM>
 struct V3Cfg {
   static constexpr int WARPS = 16;
@@ -52,10 +58,12 @@ struct V3Cfg {
   static constexpr int WARP_BYTES = STAGES * STAGE_BYTES + SZ_BYTES + 256;  // ring | s,z | misc
   static constexpr int BAR_BYTES = WARPS * STAGES * 8;
   static constexpr int MAX_FUSED_SEG = 2048;  // in-kernel partition table
-  static constexpr int PLAN_BYTES = (MAX_FUSED_SEG + 4) * 8 + 33 * 8 + 16 + MAX_FUSED_SEG * 4;  // table | scan | flag | tokens
+  static constexpr int PLAN_BYTES = (MAX_FUSED_SEG + 4) * 8 + 33 * 8 + 16 + MAX_FUSED_SEG * 4 + 3 * 32 * 4;  // table | scan | flag | tokens | arrivals
   static constexpr int SMEM = CB_BYTES + Q_BYTES + WARPS * WARP_BYTES + BAR_BYTES + PLAN_BYTES;
   static_assert(GM * (128 + 2) * 4 <= STAGES * STAGE_BYTES, "merge record must fit in a ring");
+  static_assert(16 * WIN_ROW <= STAGES * STAGE_BYTES, "window rows must fit in a ring");
   static_assert(SMEM <= (CTAS == 1 ? 232448 : 233472 / CTAS - 1024), "shared memory budget");
+  static_assert(final_scratch_floats(GM, 2 * 512) * 4 <= WARPS * WARP_BYTES, "final-merge scratch");
 };
 
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
@@ -102,9 +110,10 @@ __device__ __forceinline__ V3Src v3_src(const DecodeParams& p, int b, int h, int
 __device__ __forceinline__ void v3_issue(const DecodeParams& p, const V3Src& src, int b, int h, int64_t t0,
                                          int nv, int kc, uint8_t* stage, uint64_t* bar) {
   const uint32_t ncopy = (uint32_t(nv) + 15u) & ~15u;
+  const uint64_t pol = evict_first_policy();  // streamed once
   mbar_arrive_expect_tx(bar, ncopy * src.row_bytes);
   if (!p.bt) {
-    bulk_g2s(stage + src.dst_off, src.base + size_t(kc) * CH * src.row_bytes, ncopy * src.row_bytes, bar);
+    bulk_g2s_hint(stage + src.dst_off, src.base + size_t(kc) * CH * src.row_bytes, ncopy * src.row_bytes, bar, pol);
     return;
   }
   const int64_t ps = p.page_size;
@@ -115,7 +124,7 @@ __device__ __forceinline__ void v3_issue(const DecodeParams& p, const V3Src& src
     uint32_t len = ncopy - done;
     if (int64_t(len) > ps - off) len = uint32_t(ps - off);
     const int64_t r = (int64_t(p.bt[b * p.bt_stride + pg]) * p.Hkv + h) * ps + off;
-    bulk_g2s(stage + src.dst_off + done * src.row_bytes, src.base + r * src.row_bytes, len * src.row_bytes, bar);
+    bulk_g2s_hint(stage + src.dst_off + done * src.row_bytes, src.base + r * src.row_bytes, len * src.row_bytes, bar, pol);
     done += len;
     t += len;
   }
@@ -533,7 +542,6 @@ __device__ __forceinline__ void v3_window_chunk(const DecodeParams& p, const flo
 //    groups) and read transposed by ldmatrix.
 // This is _exact_scores / _apply_weights of smaq/score.py:99-124 in the kernel's softmax units
 // (natural log, as the merge records expect).
-constexpr int WIN_ROW = 272;
 
 __device__ __forceinline__ bool window_mma_ok(const DecodeParams& p) {
   return (p.r_dtype == SMAQ_BF16 || p.r_dtype == SMAQ_F16) && p.r_dtype == p.q_dtype &&
@@ -597,10 +605,29 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
                : "memory");
 }
 
+// Stage window chunk ch (tokens t0 + 8 ch ..) of pair (b, h) into this warp's ring: 8 key rows
+// then 8 value rows at pitch WIN_ROW, by cp.async, zero-filled past the window's end.
+__device__ __forceinline__ void v3_window_stage(const DecodeParams& p, int b, int h, int64_t t0, int ntok, int ch,
+                                                uint8_t* ring) {
+  const int lane = threadIdx.x & 31;
+  const int64_t tb = t0 + int64_t(ch) * 8;
+  const int nvalid = min(8, ntok - ch * 8);
+  const int64_t base = b * p.r_sb + h * p.r_sh;
+  const uint32_t ks_s = smem_u32(ring);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int i = lane + 32 * k, tok = (i >> 4) & 7, c16 = i & 15;
+    const uint16_t* row = static_cast<const uint16_t*>(k < 4 ? p.rk : p.rv) + base + (tb + min(tok, nvalid - 1)) * p.r_st;
+    cp_async16(ks_s + (i >> 4) * WIN_ROW + c16 * 16, row + c16 * 8, tok < nvalid ? 16u : 0u);
+  }
+}
+
 // The window tokens [t0, t0 + ntok) of pair (b, h) for this warp; writes the warp's merge record
 // (acc[GM][D], then (m, l) per head, natural-log units) at rec.  ring: >= 16 * WIN_ROW bytes of
 // this warp's shared memory, free for the duration.  Key and value rows go to shared memory by
-// cp.async (zero-filled past the window's end), so no registers are held while they load.
+// cp.async (zero-filled past the window's end), so no registers are held while they load; the
+// caller has staged the warp's first chunk (v3_window_stage, chunk wid) before loading the query
+// rows, so that the two loads overlap.
 template <int GM, int WARPS, bool BF>
 __device__ __forceinline__ void v3_window_mma(const DecodeParams& p, const float* qs, int b, int h, int64_t t0,
                                               int ntok, uint8_t* ring, float* rec) {
@@ -608,7 +635,6 @@ __device__ __forceinline__ void v3_window_mma(const DecodeParams& p, const float
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int gid = lane >> 2, tig = lane & 3;
   const int G = p.G;
-  const int64_t base = b * p.r_sb + h * p.r_sh;
   float m = -INFINITY, l = 0.f;  // l: this lane's partial row sum
   float acc[16][2];
 #pragma unroll
@@ -617,16 +643,8 @@ __device__ __forceinline__ void v3_window_mma(const DecodeParams& p, const float
   const uint32_t ks_o = uint32_t(ring - sm);                        // offset for lds64
   const float scale = p.scale;
   for (int ch = wid; ch * 8 < ntok; ch += WARPS) {
-    const int64_t tb = t0 + int64_t(ch) * 8;
     const int nvalid = min(8, ntok - ch * 8);
-    // 8 key rows then 8 value rows, 16 pieces of 16 bytes each
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int i = lane + 32 * k, tok = (i >> 4) & 7, c16 = i & 15;
-      const uint16_t* row = static_cast<const uint16_t*>(k < 4 ? p.rk : p.rv) + base +
-                            (tb + min(tok, nvalid - 1)) * p.r_st;
-      cp_async16(ks_s + (i >> 4) * WIN_ROW + c16 * 16, row + c16 * 8, tok < nvalid ? 16u : 0u);
-    }
+    if (ch != wid) v3_window_stage(p, b, h, t0, ntok, ch, ring);  // (the first chunk: by the caller)
     cp_async_wait_all();
     __syncwarp();
     // scores of head gid for tokens 2 tig, 2 tig + 1
@@ -748,8 +766,15 @@ __device__ __forceinline__ void v3_seg_ctas(const DecodeParams& p, const int64_t
 }
 
 // Merge every partial slot of pair (b, h) into the outputs (what decode_merge_kernel does for
-// one pair), reading other CTAs' slots through L2.
-__device__ void v3_final_merge(const DecodeParams& p, const int64_t* plan, const int* ntab, int pair) {
+// one pair), reading other CTAs' slots through L2.  Three passes, so that no thread waits on a
+// chain of dependent loads: every slot's (m, l) into shared memory; per head (one warp each) the
+// maximum M, the slot factors exp(m - M) and the sum L; then the value sums, each thread taking
+// four dims of one head over a share of the slots (8-byte loads, all independent), the shares
+// added through shared memory.  fsc: shared scratch of FINAL_SCRATCH(G, slots) floats, not
+// touched when the pair has no slots.  All threads of the CTA; ends with a CTA barrier when the
+// pair has slots.
+
+__device__ void v3_final_merge(const DecodeParams& p, const int64_t* plan, const int* ntab, int pair, float* fsc) {
   constexpr int D = 128;
   const int b = pair / p.Hkv, h = pair - b * p.Hkv;
   const int G = p.G;
@@ -757,42 +782,112 @@ __device__ void v3_final_merge(const DecodeParams& p, const int64_t* plan, const
   int c0[2], c1[2];
   for (int k = 0; k < 2; ++k) v3_seg_ctas(p, plan, ntab, pair * 2 + k, c0[k], c1[k]);
   const int nh = c1[0] - c0[0] + 1, nt = nh + (c1[1] - c0[1] + 1);
-  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
-    const int g = i / D, d = i - g * D;
-    // every slot's (m, l, acc) requested at once (up to 8 per pass), then combined
-    float M = -INFINITY, L = 0.f, acc[2] = {0.f, 0.f};
-    for (int j0 = 0; j0 < nt; j0 += 8) {
-      float mr[8], lr[8], ar[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int j = j0 + u;
-        mr[u] = -INFINITY;
-        lr[u] = ar[u] = 0.f;
-        if (j < nt) {
-          const int k = j < nh ? 0 : 1;
-          const int c = k ? c0[1] + (j - nh) : c0[0] + j;
-          const float* sl = p.slots + int64_t(c + pair * 2 + k) * slot_f;
-          mr[u] = __ldcg(sl + G * D + g * 2);
-          lr[u] = __ldcg(sl + G * D + g * 2 + 1);
-          ar[u] = __ldcg(sl + g * D + d);
+  if (nt == 0) {  // nobody attends this pair: zero output, empty partials
+    for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+      const int g = i / D, d = i - g * D, hq = h * G + g;
+      if (p.partial_out) {
+        float* po = p.partial_out + (int64_t(b) * p.Hq + hq) * (2 * D + 2);
+        po[d] = po[D + d] = 0.f;
+        if (d == 0) {
+          po[2 * D] = -INFINITY;
+          po[2 * D + 1] = 0.f;
         }
       }
-      float Mn = M;
+      if (p.out) store_elem(p.out, p.q_dtype, b * p.o_sb + hq * p.o_sh + d, 0.f);
+    }
+    return;
+  }
+  auto slot_ptr = [&](int j) -> const float* {
+    const int k = j < nh ? 0 : 1;
+    const int c = k ? c0[1] + (j - nh) : c0[0] + j;
+    return p.slots + int64_t(c + pair * 2 + k) * slot_f;
+  };
+  float* fm = fsc;                  // [nt][G]: m, then exp(m - M)
+  float* fl = fsc + nt * G;         // [nt][G]: l
+  float* ML = fl + nt * G;          // [G] M, [G] L
+  float* red = fsc + ((2 * G * (nt + 1) + 3) & ~3);  // [512][8]: per-thread value shares (4 history, 4 window)
+  // value shares: quad q (head q / 32, dims 4 (q % 32) ..), slots j = part, part + R, ...; the
+  // first 8 slots of every share are requested before the (m, l) pass, so both loads overlap
+  const int quads = G * (D / 4);
+  const int R = blockDim.x / quads;  // >= 2 for G <= 8; threads past R * quads only add up
+  const bool sharer = int(threadIdx.x) < R * quads;
+  const int q = threadIdx.x % quads, part = threadIdx.x / quads;
+  const int g = q / (D / 4), d4 = (q - g * (D / 4)) * 4;
+  float4 v[8];
+  auto load_batch = [&](int j0) {
 #pragma unroll
-      for (int u = 0; u < 8; ++u) Mn = fmaxf(Mn, mr[u]);
-      if (Mn == -INFINITY) continue;
-      const float sc = (M == -INFINITY) ? 0.f : expf(M - Mn);
-      acc[0] *= sc;
-      acc[1] *= sc;
-      L *= sc;
-      M = Mn;
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const float f = (mr[u] == -INFINITY) ? 0.f : expf(mr[u] - M);
-        acc[j0 + u < nh ? 0 : 1] += ar[u] * f;
-        L += lr[u] * f;
+    for (int u = 0; u < 8; ++u) {
+      const int j = j0 + u * R;
+      v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (sharer && j < nt) {  // a slot is 130 G floats: 8-byte aligned for every G, 16-byte only for even G
+        const float2* sp = reinterpret_cast<const float2*>(slot_ptr(j) + g * D + d4);
+        const float2 x = __ldcg(sp), y = __ldcg(sp + 1);
+        v[u] = make_float4(x.x, x.y, y.x, y.y);
       }
     }
+  };
+  load_batch(part);
+  for (int k = threadIdx.x; k < nt * G; k += blockDim.x) {
+    const int j = k / G, gg = k - j * G;
+    const float* sl = slot_ptr(j);
+    fm[k] = __ldcg(sl + G * D + 2 * gg);
+    fl[k] = __ldcg(sl + G * D + 2 * gg + 1);
+  }
+  __syncthreads();
+  {
+    const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int gg = wid; gg < G; gg += blockDim.x >> 5) {
+      float M = -INFINITY;
+      for (int j = lane; j < nt; j += 32) M = fmaxf(M, fm[j * G + gg]);
+      M = warp_max(M);
+      float L = 0.f;
+      for (int j = lane; j < nt; j += 32) {
+        const float m = fm[j * G + gg];
+        const float f = (m == -INFINITY) ? 0.f : expf(m - M);
+        L += fl[j * G + gg] * f;
+        fm[j * G + gg] = f;
+      }
+      L = warp_sum(L);
+      if (lane == 0) {
+        ML[gg] = M;
+        ML[G + gg] = L;
+      }
+    }
+  }
+  __syncthreads();
+  if (sharer) {
+    float4 ah = make_float4(0.f, 0.f, 0.f, 0.f), ar = ah;
+    for (int j0 = part;;) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = j0 + u * R;
+        if (j >= nt) break;
+        const float f = fm[j * G + g];
+        if (j < nh) {
+          ah.x = fmaf(v[u].x, f, ah.x); ah.y = fmaf(v[u].y, f, ah.y);
+          ah.z = fmaf(v[u].z, f, ah.z); ah.w = fmaf(v[u].w, f, ah.w);
+        } else {
+          ar.x = fmaf(v[u].x, f, ar.x); ar.y = fmaf(v[u].y, f, ar.y);
+          ar.z = fmaf(v[u].z, f, ar.z); ar.w = fmaf(v[u].w, f, ar.w);
+        }
+      }
+      j0 += 8 * R;
+      if (j0 >= nt) break;
+      load_batch(j0);
+    }
+    reinterpret_cast<float4*>(red + threadIdx.x * 8)[0] = ah;
+    reinterpret_cast<float4*>(red + threadIdx.x * 8)[1] = ar;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    const int g = i / D, d = i - g * D;
+    const int q = g * (D / 4) + (d >> 2), e = d & 3;
+    float acc[2] = {0.f, 0.f};
+    for (int r = 0; r < R; ++r) {
+      acc[0] += red[(r * quads + q) * 8 + e];
+      acc[1] += red[(r * quads + q) * 8 + 4 + e];
+    }
+    const float M = ML[g], L = ML[G + g];
     const int hq = h * G + g;
     if (p.partial_out) {
       float* po = p.partial_out + (int64_t(b) * p.Hq + hq) * (2 * D + 2);
@@ -814,39 +909,95 @@ __device__ void v3_final_merge(const DecodeParams& p, const int64_t* plan, const
       store_elem(p.out, p.q_dtype, b * p.o_sb + hq * p.o_sh + d, o);
     }
   }
+  __syncthreads();  // scratch free
 }
 
-// After this CTA wrote its slot for segment s: count it for the pair; the CTA whose slot
-// completes the pair merges it.  Counter values carry the call's epoch so that a workspace
-// never zeroed reads as "no slots yet"; the merging CTA resets the counter to 0.
-__device__ void v3_arrive(const DecodeParams& p, const int64_t* plan, const int* ntab, int s, int* flag) {
-  const int pair = s >> 1;
-  if (threadIdx.x == 0) {
+// Slot arrivals of one CTA, deferred: the CTA notes (pair, slots finished) as it goes and counts
+// them at the end of its slice (or when the list is full), one atomicAdd per pair, all pairs at
+// once; the CTA whose count completes a pair merges it and resets the counter to 0.  Counter
+// values carry the call's epoch (epoch << 32 | slots): every CTA first claims the counters of the
+// pairs its slice touches for this call (v3_claim: a counter holding another epoch -- a stale
+// or never-zeroed workspace -- restarts at 0; one holding this epoch is left alone), so that the
+// arrivals need no compare-and-swap retries.  arr (shared): [0, MAX_ARR) pairs, [MAX_ARR,
+// 2 MAX_ARR) counts, then last flags.
+constexpr int MAX_ARR = 32;
+// Largest grid of the single-launch kernels: the final merge's scratch for a pair with slots
+// from every CTA must fit in the warp rings.
+constexpr int MAX_GRID_FUSED = 512;
+
+// Claim pair `pair`'s counter for this call (see v3_flush_arrivals): restart it at 0 unless it
+// already carries this call's epoch.
+__device__ __forceinline__ void v3_claim(const DecodeParams& p, int pair) {
+  unsigned long long* cnt = reinterpret_cast<unsigned long long*>(p.pair_cnt + pair);
+  unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(cnt);
+  while (uint32_t(old >> 32) != p.epoch) {
+    const unsigned long long seen = atomicCAS(cnt, old, uint64_t(p.epoch) << 32);
+    if (seen == old) break;
+    old = seen;
+  }
+}
+
+// Claim the counters of every pair whose segments meet this CTA's slice [lo, hi) (all threads).
+__device__ __forceinline__ void v3_claim_slice(const DecodeParams& p, const int64_t* plan, int sa, int64_t hi) {
+  int s0 = sa, s1 = p.n_seg - 1;  // last segment starting below hi
+  while (s0 < s1) {
+    const int mid = (s0 + s1 + 1) >> 1;
+    if (plan[mid] < hi) s0 = mid; else s1 = mid - 1;
+  }
+  for (int pr = (sa >> 1) + int(threadIdx.x); pr <= (s0 >> 1); pr += blockDim.x) v3_claim(p, pr);
+}
+
+__device__ void v3_flush_arrivals(const DecodeParams& p, const int64_t* plan, const int* ntab, int* arr, int n,
+                                  float* fsc) {
+  __syncthreads();  // every slot store of this CTA, and the list, before the counts
+  if (int(threadIdx.x) < n) {
+    const int pair = arr[threadIdx.x];
+    const uint32_t add = uint32_t(arr[MAX_ARR + threadIdx.x]);
     int expected = 0;
     for (int k = 0; k < 2; ++k) {
       int c0, c1;
       v3_seg_ctas(p, plan, ntab, pair * 2 + k, c0, c1);
       expected += c1 - c0 + 1;
     }
-    __threadfence();  // this CTA's slot stores before the count
+    __threadfence();  // the CTA's slot stores before the count
     unsigned long long* cnt = reinterpret_cast<unsigned long long*>(p.pair_cnt + pair);
-    unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(cnt), next;
-    for (;;) {
-      const uint32_t n = (uint32_t(old >> 32) == p.epoch) ? uint32_t(old) + 1u : 1u;
-      next = (uint64_t(p.epoch) << 32) | n;
-      const unsigned long long seen = atomicCAS(cnt, old, next);
-      if (seen == old) break;
-      old = seen;
+    const unsigned long long old = atomicAdd(cnt, (unsigned long long)add);
+    bool last = false;
+    if (uint32_t(old >> 32) != p.epoch) {
+      atomicExch(reinterpret_cast<int*>(p.plan + p.n_seg + 2), 1);  // unclaimed counter: report
+    } else {
+      last = int(uint32_t(old) + add) == expected;
+      if (last) {
+        *reinterpret_cast<volatile unsigned long long*>(cnt) = 0ull;
+        __threadfence();  // every other slot store is visible before the merge reads them
+      }
     }
-    const bool last = int(uint32_t(next)) == expected;
-    if (last) {
-      *reinterpret_cast<volatile unsigned long long*>(cnt) = 0ull;
-      __threadfence();  // every other slot store is visible before the merge reads them
-    }
-    *flag = last;
+    arr[2 * MAX_ARR + threadIdx.x] = last;
   }
   __syncthreads();
-  if (*flag) v3_final_merge(p, plan, ntab, pair);
+  for (int i = 0; i < n; ++i)
+    if (arr[2 * MAX_ARR + i]) v3_final_merge(p, plan, ntab, arr[i], fsc);
+  __syncthreads();  // the list is rewritten next
+}
+
+// Note one finished slot of `pair` (all threads, after the slot's CTA barrier).  fsc: shared
+// scratch for a flush (the warp rings: free between segments).
+__device__ __forceinline__ void v3_note(const DecodeParams& p, const int64_t* plan, const int* ntab, int pair,
+                                        int* arr, int& narr, int& last_pair, float* fsc) {
+  if (pair == last_pair) {
+    if (threadIdx.x == 0) arr[MAX_ARR + narr - 1] += 1;
+    return;
+  }
+  if (narr == MAX_ARR) {
+    v3_flush_arrivals(p, plan, ntab, arr, narr, fsc);
+    narr = 0;
+  }
+  if (threadIdx.x == 0) {
+    arr[narr] = pair;
+    arr[MAX_ARR + narr] = 1;
+  }
+  ++narr;
+  last_pair = pair;
 }
 
 template <int GM>
@@ -880,6 +1031,9 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3
   int64_t* splan = reinterpret_cast<int64_t*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);
   int* arrive_flag = reinterpret_cast<int*>(splan + C::MAX_FUSED_SEG + 4 + 33);
   int* sntab = arrive_flag + 4;
+  int* arr = sntab + C::MAX_FUSED_SEG;  // deferred slot arrivals
+  int narr = 0, last_pair = -1;
+  float* fsc = reinterpret_cast<float*>(wreg0);  // final-merge scratch (rings free between segments)
   const int64_t* plan = p.plan;
   const int* ntab = nullptr;
   if (p.fused) {
@@ -954,8 +1108,9 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3
         v3_seg_ctas(p, plan, ntab, pair * 2 + k, c0, c1);
         e += c1 - c0 + 1;
       }
-      if (e == 0) v3_final_merge(p, plan, ntab, pair);
+      if (e == 0) v3_final_merge(p, plan, ntab, pair, fsc);  // (no slots: touches no shared memory)
     }
+    if (lo < hi) v3_claim_slice(p, plan, sa, hi);
   }
   if (lo >= hi) return;
 
@@ -1023,6 +1178,8 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3
     if (t1 > n) t1 = n;
     if (t0 >= t1) continue;
     const int pair = s >> 1, b = pair / p.Hkv, h = pair - b * p.Hkv;
+    if ((s & 1) && window_mma_ok(p) && (wid << 3) < int(t1 - t0))
+      v3_window_stage(p, b, h, t0, int(t1 - t0), wid, wreg);  // the window rows load with the query rows
     for (int i = threadIdx.x; i < GM * D; i += blockDim.x) {
       const int g = i / D, d = i - g * D;
       qs[i] = g < G ? load_elem(p.q, p.q_dtype, b * p.q_sb + int64_t(h * G + g) * p.q_sh + d) : 0.f;
@@ -1053,7 +1210,7 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3
       }
       __syncthreads();
       v3_merge<GM, WARPS>(p, reinterpret_cast<const float*>(wreg0), C::WARP_BYTES / 4, c + s);
-      if (p.fused) v3_arrive(p, plan, ntab, s, arrive_flag);
+      if (p.fused) v3_note(p, plan, ntab, s >> 1, arr, narr, last_pair, fsc);
       continue;
     }
 
@@ -1217,8 +1374,9 @@ __global__ void __launch_bounds__(V3Cfg<GM>::THREADS, V3Cfg<GM>::CTAS) decode_v3
     }
     __syncthreads();
     v3_merge<GM, WARPS>(p, reinterpret_cast<const float*>(wreg0), C::WARP_BYTES / 4, c + s);
-    if (p.fused) v3_arrive(p, plan, ntab, s, arrive_flag);
+    if (p.fused) v3_note(p, plan, ntab, s >> 1, arr, narr, last_pair, fsc);
   }
+  if (p.fused && narr) v3_flush_arrivals(p, plan, ntab, arr, narr, fsc);
   if (failed && lane == 0) atomicExch(reinterpret_cast<int*>(p.plan + p.n_seg + 2), 1);
 }
 
@@ -1252,9 +1410,11 @@ struct SCfg {
   static constexpr int WARP_BYTES = STAGES * SK_STAGE + SZ_BYTES + PB_BYTES;
   static constexpr int BAR_BYTES = WARPS * STAGES * 8;
   static constexpr int MAX_FUSED_SEG = 1024;
-  static constexpr int PLAN_BYTES = (MAX_FUSED_SEG + 4) * 8 + 33 * 8 + 16 + MAX_FUSED_SEG * 4;
+  static constexpr int PLAN_BYTES = (MAX_FUSED_SEG + 4) * 8 + 33 * 8 + 16 + MAX_FUSED_SEG * 4 + 3 * 32 * 4;
   static constexpr int SMEM = TAB_BYTES + Q_BYTES + B_BYTES + WARPS * WARP_BYTES + BAR_BYTES + PLAN_BYTES;
   static_assert(8 * (128 + 2) * 4 <= STAGES * SK_STAGE, "merge record must fit in a ring");
+  static_assert(16 * WIN_ROW <= STAGES * SK_STAGE, "window rows must fit in a ring");
+  static_assert(final_scratch_floats(8, 2 * 512) * 4 <= WARPS * WARP_BYTES, "final-merge scratch");
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
@@ -1430,6 +1590,9 @@ __global__ void __launch_bounds__(SCfg::THREADS, 1) decode_s_kernel(DecodeParams
   int64_t* splan = reinterpret_cast<int64_t*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);
   int* arrive_flag = reinterpret_cast<int*>(splan + C::MAX_FUSED_SEG + 4 + 33);
   int* sntab = arrive_flag + 4;
+  int* arr = sntab + C::MAX_FUSED_SEG;  // deferred slot arrivals
+  int narr = 0, last_pair = -1;
+  float* fsc = reinterpret_cast<float*>(wreg0);  // final-merge scratch (rings free between segments)
   const int64_t* plan = p.plan;
   const int* ntab = nullptr;
   if (p.fused) {
@@ -1468,7 +1631,7 @@ __global__ void __launch_bounds__(SCfg::THREADS, 1) decode_s_kernel(DecodeParams
         v3_seg_ctas(p, plan, ntab, pair * 2 + k, c0, c1);
         e += c1 - c0 + 1;
       }
-      if (e == 0) v3_final_merge(p, plan, ntab, pair);
+      if (e == 0) v3_final_merge(p, plan, ntab, pair, fsc);  // (no slots: touches no shared memory)
     }
   }
   const int64_t total = plan[p.n_seg];
@@ -1492,6 +1655,7 @@ __global__ void __launch_bounds__(SCfg::THREADS, 1) decode_s_kernel(DecodeParams
     const int mid = (sa + sb_) >> 1;
     if (plan[mid + 1] > lo) sb_ = mid; else sa = mid + 1;
   }
+  if (p.fused) v3_claim_slice(p, plan, sa, hi);
   const float lscale = p.scale * kLog2e;
   for (int s = sa; s < p.n_seg; ++s) {
     const int64_t S = plan[s];
@@ -1504,6 +1668,8 @@ __global__ void __launch_bounds__(SCfg::THREADS, 1) decode_s_kernel(DecodeParams
     if (t1 > n) t1 = n;
     if (t0 >= t1) continue;
     const int pair = s >> 1, b = pair / p.Hkv, h = pair - b * p.Hkv;
+    if ((s & 1) && window_mma_ok(p) && (wid << 3) < int(t1 - t0))
+      v3_window_stage(p, b, h, t0, int(t1 - t0), wid, wreg);  // the window rows load with the query rows
     for (int i = threadIdx.x; i < 8 * D; i += blockDim.x) {
       const int g = i / D, d = i - g * D;
       qs[i] = g < G ? load_elem(p.q, p.q_dtype, b * p.q_sb + int64_t(h * G + g) * p.q_sh + d) : 0.f;
@@ -1531,7 +1697,7 @@ __global__ void __launch_bounds__(SCfg::THREADS, 1) decode_s_kernel(DecodeParams
       }
       __syncthreads();
       v3_merge<GM, WARPS>(p, reinterpret_cast<const float*>(wreg0), C::WARP_BYTES / 4, c + s);
-      if (p.fused) v3_arrive(p, plan, ntab, s, arrive_flag);
+      if (p.fused) v3_note(p, plan, ntab, s >> 1, arr, narr, last_pair, fsc);
       continue;
     }
 
@@ -1657,8 +1823,9 @@ __global__ void __launch_bounds__(SCfg::THREADS, 1) decode_s_kernel(DecodeParams
     }
     __syncthreads();
     v3_merge<GM, WARPS>(p, reinterpret_cast<const float*>(wreg0), C::WARP_BYTES / 4, c + s);
-    if (p.fused) v3_arrive(p, plan, ntab, s, arrive_flag);
+    if (p.fused) v3_note(p, plan, ntab, s >> 1, arr, narr, last_pair, fsc);
   }
+  if (p.fused && narr) v3_flush_arrivals(p, plan, ntab, arr, narr, fsc);
   if (failed && lane == 0) atomicExch(reinterpret_cast<int*>(p.plan + p.n_seg + 2), 1);
 }
 
@@ -1672,7 +1839,7 @@ int launch_decode_s(DecodeParams& p, int grid_req, cudaStream_t s, int* grid_out
   auto kern = decode_s_kernel;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SCfg::SMEM);
   if (e != cudaSuccess) return cuda_status(e, "decode_s attr");
-  const int grid = grid_req > 0 ? grid_req : num_sms();
+  const int grid = min(grid_req > 0 ? grid_req : num_sms(), MAX_GRID_FUSED);
   *grid_out = grid;
   if (query_only) return SMAQ_OK;
   if (!p.pdl) {
@@ -1706,7 +1873,7 @@ static int launch_v3_t(DecodeParams& p, int grid_req, cudaStream_t s, int* grid_
   const int sm = V3Cfg<GM>::SMEM;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
   if (e != cudaSuccess) return cuda_status(e, "decode_v3 attr");
-  const int grid = grid_req > 0 ? grid_req : num_sms() * V3Cfg<GM>::CTAS;
+  const int grid = min(grid_req > 0 ? grid_req : num_sms() * V3Cfg<GM>::CTAS, MAX_GRID_FUSED);
   *grid_out = grid;
   if (query_only) return SMAQ_OK;
   if (!p.pdl) {

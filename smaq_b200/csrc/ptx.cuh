@@ -64,6 +64,23 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// L2 policy for data read exactly once (the history streams): evict first, so that the small
+// data read again soon -- window rows, queries, partial slots -- keeps its L2 lines.
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// bulk_g2s with an L2 cache policy (evict_first_policy).
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+
 // Order this thread's earlier generic-proxy accesses to shared memory before later async-proxy
 // (bulk copy / TMA) writes to it: a thread that read a staging buffer executes this before the
 // barrier after which the buffer is refilled by a bulk copy.
