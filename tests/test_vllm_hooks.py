@@ -1,31 +1,42 @@
-"""Host logic of the vLLM integration (smaq_b200.integration.vllm, smaq_b200.vllm_attn_backend)
-on fake model runners, mirroring smaq/integration/vllm.py and smaq/vllm_attn_backend.py.
-CPU tests keep every layer's tokens inside the exact ring (no store append, which needs the
-device); tests/test_gpu_vllm_hooks.py drives the compressed path on the GPU."""
+"""Host logic of the vLLM integration (smaq_b200.integration.vllm / paged / vllm_backend and the
+legacy smaq_b200.vllm_attn_backend) on fake model runners, CPU only.  The device launches
+(``ops.append`` / ``ops.decode``) are replaced by recorders here; tests/test_gpu_vllm_hooks.py
+runs the same batched path on the GPU against per-sequence oracle attention."""
 
 import types
 
+import numpy as np
 import pytest
 import torch
 
 from smaq_b200 import vllm_attn_backend as vab
+from smaq_b200.capture import KVCaptureEngine
+from smaq_b200.integration import paged
 from smaq_b200.integration import vllm as iv
 
 D = 64
+BS = 16
 
 
 class FakeImpl:
+    """A flash-attention implementation: vLLM-style cache writes through slots, and a forward
+    that returns 7s (so a test sees when the SMAQ path answered instead)."""
+
     def __init__(self, num_kv_heads=2, num_heads=4, head_size=D, separate_update=True):
-        self.num_kv_heads = num_kv_heads
-        self.num_heads = num_heads
-        self.head_size = head_size
+        self.num_kv_heads, self.num_heads, self.head_size = num_kv_heads, num_heads, head_size
         self.scale = head_size ** -0.5
         self.calls = []
         if separate_update:
             self.do_kv_cache_update = types.MethodType(FakeImpl._update, self)
 
     def _update(self, layer, key, value, kv_cache, slot_mapping):
-        self.calls.append(("update", key.shape[0]))
+        self.calls.append(("update", slot_mapping.shape[0]))
+        if kv_cache is not None and kv_cache.dim() == 5:
+            n, bs = slot_mapping.shape[0], kv_cache.shape[2]
+            s = slot_mapping.long()
+            ok = s >= 0
+            kv_cache[0][s[ok] // bs, s[ok] % bs] = key[:n][ok].to(kv_cache.dtype)
+            kv_cache[1][s[ok] // bs, s[ok] % bs] = value[:n][ok].to(kv_cache.dtype)
 
     def forward(self, layer, query, key, value, kv_cache, attn_metadata, output=None, output_scale=None,
                 output_block_scale=None):
@@ -49,17 +60,20 @@ class FakeMLA:
 
 
 class FakeAttn:
-    def __init__(self, impl):
+    def __init__(self, impl, kv_cache):
         self.impl = impl
-        self.kv_cache = [torch.zeros(1000, dtype=torch.float16)]
+        self.kv_cache = [kv_cache]
 
 
 class FakeRunner:
-    def __init__(self, n_layers=6, mla=False, device="cpu"):
-        impls = [FakeImpl(separate_update=(i % 2 == 0)) for i in range(n_layers)]
-        ctx = {f"layer.{i}": FakeAttn(im) for i, im in enumerate(impls)}
+    def __init__(self, n_layers=6, mla=False, device="cpu", num_blocks=64, impl_kw=None, dtype=torch.float32):
+        impls = [FakeImpl(separate_update=(i % 2 == 0), **(impl_kw or {})) for i in range(n_layers)]
+        ctx = {}
+        for i, im in enumerate(impls):
+            cache = torch.zeros(2, num_blocks, BS, im.num_kv_heads, im.head_size, dtype=dtype, device=device)
+            ctx[f"layer.{i}"] = FakeAttn(im, cache)
         if mla:
-            ctx["mla.0"] = FakeAttn(FakeMLA())
+            ctx["mla.0"] = FakeAttn(FakeMLA(), torch.zeros(1000, dtype=torch.float16))
         ctx["not_attention"] = object()
         self.compilation_config = types.SimpleNamespace(static_forward_context=ctx)
         self.device = torch.device(device)
@@ -68,6 +82,23 @@ class FakeRunner:
 
 def meta(n, max_q):
     return types.SimpleNamespace(num_actual_tokens=n, max_query_len=max_q)
+
+
+class Recorder:
+    """Stands in for the device launches of integration.paged."""
+
+    def __init__(self, monkeypatch):
+        self.appends, self.decodes = [], []
+        monkeypatch.setattr(paged.ops, "append", self._append)
+        monkeypatch.setattr(paged.ops, "decode", self._decode)
+        monkeypatch.setattr(paged.ops, "decode_workspace_bytes", lambda *a, **k: 256)
+
+    def _append(self, k, v, **kw):
+        self.appends.append(dict(k=k.clone(), v=v.clone(), **kw))
+
+    def _decode(self, q, **kw):
+        self.decodes.append(dict(q=q.clone(), **kw))
+        return torch.zeros_like(q)
 
 
 def test_modes():
@@ -95,40 +126,170 @@ def test_install_hooks_layers_and_bits():
     assert all(s.config.ring_capacity == 64 for s in states.values())
 
 
-def test_capture_routing_and_passthrough():
-    r = FakeRunner(n_layers=2)
-    states = iv.install_hooks(r, mode=iv.MODE_CAPTURE_ONLY, ring_capacity=128)
-    ctx = r.compilation_config.static_forward_context
-    im0, im1 = ctx["layer.0"].impl, ctx["layer.1"].impl   # separate update / capture in forward
-    k = torch.randn(10, 2, D)
-    q = torch.randn(10, 4, D)
-    im0.do_kv_cache_update(None, k, k, None, torch.arange(10))
-    assert states["layer.0"].engine.ring.size == 10 and im0.calls == [("update", 10)]
-    out = im1.forward(None, q, k, k, None, meta(10, 10))
-    assert torch.all(out == 7.0) and states["layer.1"].engine.ring.size == 10
-    im1.forward(None, q[:1], k[:1], k[:1], None, meta(1, 1))   # decode: one more token, passthrough
-    assert states["layer.1"].engine.ring.size == 11
-    iv.set_mode(iv.MODE_OFF)
-    im0.do_kv_cache_update(None, k[:1], k[:1], None, torch.arange(1))
-    assert states["layer.0"].engine.ring.size == 10           # off: vLLM write only
+class _CountingStore:
+    """Token counter standing in for the compressed store of the reference's capture engine."""
+
+    def __init__(self, h, d):
+        self.num_kv_heads, self.head_dim, self.device, self.num_tokens = h, d, torch.device("cpu"), 0
+
+    def append_chunk(self, k, v):
+        self.num_tokens += k.shape[0]
+
+    def reset(self):
+        self.num_tokens = 0
+
+
+def reference_split(n0, n_decode, capacity):
+    """(compressed, exact) token counts of the reference's capture engine (capture.py rule)
+    after a prompt of n0 tokens and n_decode decode tokens, as the hook's decode sees them."""
+    st = _CountingStore(1, 4)
+    eng = KVCaptureEngine(st, ring_capacity=capacity, device=torch.device("cpu"), dtype=torch.float32)
+    eng.ingest_prefill(torch.zeros(n0, 1, 4), torch.zeros(n0, 1, 4), n0)
+    for _ in range(n_decode):
+        eng.ingest_decode(torch.zeros(1, 1, 4), torch.zeros(1, 1, 4), 1)
+    h, r = st.num_tokens, eng.ring.size
+    if h < 16:  # the hook answers from exact attention over every token
+        return 0, h + r
+    return h, r
+
+
+@pytest.mark.parametrize("capacity", [8, 64, 128])
+def test_window_rule_is_the_reference_ring(capacity):
+    for n0 in (1, 5, capacity - 1, capacity, capacity + 1, 3 * capacity + 7):
+        for nd in (1, 2, capacity - 1, capacity, capacity + 3, 2 * capacity + 1):
+            L = torch.tensor([n0 + nd])
+            h, r = paged.split_history(L, torch.tensor([n0]), capacity)
+            assert (int(h), int(r)) == reference_split(n0, nd, capacity), (n0, nd)
+
+
+class Batch:
+    """Sequences in shuffled vLLM blocks, driven through a hooked implementation step by step."""
+
+    def __init__(self, prompt_lens, n_decode, num_blocks, seed=0, hkv=2, hq=4, d=D, device="cpu",
+                 dtype=torch.float32):
+        self.rng = np.random.default_rng(seed)
+        self.lens = list(prompt_lens)
+        self.hkv, self.hq, self.d, self.device, self.dtype = hkv, hq, d, torch.device(device), dtype
+        need = [(n + n_decode + BS - 1) // BS for n in prompt_lens]
+        perm = self.rng.permutation(num_blocks)[: sum(need)]
+        self.bt = torch.zeros(len(prompt_lens), max(need), dtype=torch.int32)
+        o = 0
+        for b, k in enumerate(need):
+            self.bt[b, :k] = torch.from_numpy(perm[o:o + k].astype(np.int32))
+            o += k
+        self.bt = self.bt.to(self.device)
+        self.k = [torch.empty(0, hkv, d) for _ in prompt_lens]   # every token written, per sequence
+        self.v = [torch.empty(0, hkv, d) for _ in prompt_lens]
+
+    def _slots(self, b, pos):
+        pos = torch.as_tensor(pos, dtype=torch.int64)
+        return self.bt[b].cpu().long()[pos // BS] * BS + pos % BS
+
+    def _tokens(self, n):
+        k = torch.from_numpy(self.rng.standard_normal((n, self.hkv, self.d)).astype(np.float32))
+        v = torch.from_numpy(self.rng.standard_normal((n, self.hkv, self.d)).astype(np.float32))
+        return k, v
+
+    def _step(self, impl, kv_cache, counts, pad=3):
+        ks, vs, slots = [], [], []
+        for b, n in enumerate(counts):
+            k, v = self._tokens(n)
+            slots.append(self._slots(b, range(len(self.k[b]), len(self.k[b]) + n)))
+            self.k[b], self.v[b] = torch.cat([self.k[b], k]), torch.cat([self.v[b], v])
+            ks.append(k)
+            vs.append(v)
+        N = sum(counts)
+        key = torch.cat(ks + [torch.zeros(pad, self.hkv, self.d)])        # padded rows, as vLLM pads
+        val = torch.cat(vs + [torch.zeros(pad, self.hkv, self.d)])
+        sm = torch.cat(slots + [torch.full((pad,), -1, dtype=torch.int64)])
+        dev = lambda t: t.to(self.device)
+        key, val = dev(key).to(self.dtype), dev(val).to(self.dtype)
+        impl.do_kv_cache_update(None, key, val, kv_cache, dev(sm))
+        self.lens = [len(x) for x in self.k]
+        qsl = torch.tensor([0] + list(np.cumsum(counts)), dtype=torch.int32)
+        md = types.SimpleNamespace(num_actual_tokens=N, max_query_len=max(counts), query_start_loc=dev(qsl),
+                                   seq_lens=dev(torch.tensor(self.lens, dtype=torch.int32)), block_table=self.bt,
+                                   slot_mapping=dev(sm))
+        q = dev(torch.from_numpy(self.rng.standard_normal((N + pad, self.hq, self.d)).astype(np.float32))).to(self.dtype)
+        out = impl.forward(None, q, key, val, kv_cache, md)
+        return q[:N], out, sm
+
+    def prefill(self, impl, kv_cache):
+        return self._step(impl, kv_cache, list(self.lens_prompt()))
+
+    def lens_prompt(self):
+        return self.lens
+
+    def decode(self, impl, kv_cache):
+        return self._step(impl, kv_cache, [1] * len(self.lens))
+
+
+def _batched_runner(monkeypatch, capacity=32):
+    rec = Recorder(monkeypatch)
+    r = FakeRunner(n_layers=1, num_blocks=128)
+    states = iv.install_hooks(r, mode=iv.MODE_HYBRID, ring_capacity=capacity, key_bits=3, initial_layers_count=0)
+    attn = r.compilation_config.static_forward_context["layer.0"]
+    return rec, r, states["layer.0"], attn.impl, attn.kv_cache[0]
+
+
+def test_batched_path_three_sequences(monkeypatch):
+    """Three sequences of distinct prompt lengths in shuffled blocks: one append launch per step
+    over all tokens (padding to the scratch page), prefill through vLLM's own attention, and
+    one decode launch per decode step with the block table, the reference split per sequence
+    and the exact window rows read from vLLM's cache."""
+    C = 32
+    rec, r, st, im, kv = _batched_runner(monkeypatch, C)
+    prompts = [40, 150, 9]
+    bt = Batch(prompts, n_decode=40, num_blocks=128, seed=3)
+    q, out, sm = bt.prefill(im, kv)
+    assert torch.all(out == 7.0)                                  # prefill: vLLM's attention
+    assert len(rec.appends) == 1 and rec.decodes == []
+    a = rec.appends[0]
+    slots = a["slots"]
+    assert slots.shape[0] == sum(prompts) + 3 and a["page_size"] == BS
+    assert torch.equal(slots[: sum(prompts)], sm[: sum(prompts)])
+    assert torch.all(slots[sum(prompts):] // BS == 128)               # padding -> scratch page
+    assert torch.equal(st.cache.prompt_len[bt.bt[:, 0].long()], torch.tensor(prompts, dtype=torch.int32))
+    for step in range(40):
+        q, out, _ = bt.decode(im, kv)
+        d = rec.decodes[-1]
+        assert len(rec.decodes) == step + 1 and len(rec.appends) == step + 2
+        assert torch.equal(d["block_table"], bt.bt) and d["page_size"] == BS
+        hist, rl = d["hist_len"], d["recent_len"]
+        for b, n0 in enumerate(prompts):
+            h_ref, r_ref = reference_split(n0, step + 1, C)
+            assert (int(hist[b]), int(rl[b])) == (h_ref, r_ref), (step, b)
+            L = bt.lens[b]
+            assert torch.equal(d["recent_k"][b, :r_ref], bt.k[b][L - r_ref:L])
+            assert torch.equal(d["recent_v"][b, :r_ref], bt.v[b][L - r_ref:L])
+        assert torch.equal(d["q"], q) and torch.all(out == 0)       # answered by the decode launch
+    assert iv.get_stats(r)["layer.0"]["compressed_tokens"] == sum(prompts) + 3 + 40 * (3 + 3)
+
+
+def test_capture_only_and_off_pass_through(monkeypatch):
+    rec, r, st, im, kv = _batched_runner(monkeypatch)
     iv.set_mode(iv.MODE_CAPTURE_ONLY)
+    bt = Batch([20, 30], n_decode=2, num_blocks=128, seed=4)
+    bt.prefill(im, kv)
+    _, out, _ = bt.decode(im, kv)
+    assert torch.all(out == 7.0) and len(rec.appends) == 2 and rec.decodes == []
+    iv.set_mode(iv.MODE_OFF)
+    _, out, _ = bt.decode(im, kv)
+    assert torch.all(out == 7.0) and len(rec.appends) == 2          # off: vLLM's write only
+    assert im.calls.count(("update", 2 + 3)) == 2
+    iv.set_mode(iv.MODE_HYBRID)
 
 
-def test_hybrid_without_history_passes_through_or_zeros():
-    r = FakeRunner(n_layers=1)
-    iv.install_hooks(r, mode=iv.MODE_HYBRID)
-    im = r.compilation_config.static_forward_context["layer.0"].impl
-    q = torch.randn(1, 4, D)
-    assert torch.all(im.forward(None, q, q[:, :2], q[:, :2], None, meta(1, 1)) == 7.0)
-    r2 = FakeRunner(n_layers=1)
-    iv.install_hooks(r2, mode=iv.MODE_HYBRID, no_alloc=True)
-    im2 = r2.compilation_config.static_forward_context["layer.0"].impl
-    out = im2.forward(None, q.reshape(1, 4 * D), q[:, :2].reshape(1, 2 * D), q[:, :2].reshape(1, 2 * D), None,
-                      meta(1, 1))
-    assert out.shape == (1, 4 * D) and torch.all(out == 0)
+def test_mixed_prefill_decode_step_runs_vllm_attention(monkeypatch):
+    rec, r, st, im, kv = _batched_runner(monkeypatch)
+    bt = Batch([20, 30], n_decode=4, num_blocks=128, seed=5)
+    bt.prefill(im, kv)
+    _, out, _ = bt._step(im, kv, [1, 3])                        # one decode row, one chunk row
+    assert torch.all(out == 7.0) and rec.decodes == []
+    assert int(st.cache.prompt_len[bt.bt[1, 0].long()]) == 33    # the chunk row's new prompt length
 
 
-def test_no_alloc_prefill_is_causal_attention():
+def test_no_alloc_prefill_is_causal_attention_and_empty_decode_is_zero():
     r = FakeRunner(n_layers=1)
     iv.install_hooks(r, mode=iv.MODE_HYBRID, no_alloc=True)
     im = r.compilation_config.static_forward_context["layer.0"].impl
@@ -143,22 +304,80 @@ def test_no_alloc_prefill_is_causal_attention():
     buf = torch.zeros(n, 4 * D)
     im.forward(None, q.reshape(n, -1), k.reshape(n, -1), v.reshape(n, -1), None, meta(n, n), output=buf)
     assert torch.allclose(buf.view(n, 4, D), ref, atol=1e-5)
+    dq = torch.randn(1, 4 * D)
+    out = im.forward(None, dq, dq[:, : 2 * D], dq[:, : 2 * D], None, meta(1, 1))
+    assert out.shape == (1, 4 * D) and torch.all(out == 0)     # nothing compressed yet
+    im.do_kv_cache_update(None, k, v, None, torch.arange(n))
+    st = r._smaq_layer_states["layer.0"]
+    assert st.engine.ring.size == n and im.calls == []          # no_alloc: vLLM's write skipped
 
 
-def test_mla_passthrough_and_stats_and_free():
+def test_mla_passthrough_and_stats_and_free(monkeypatch):
+    Recorder(monkeypatch)
     r = FakeRunner(n_layers=2, mla=True)
     states = vab.install_smaq_hooks(r, mode=vab.MODE_SHADOW, buffer_size=32)
     assert r._smaq_states is states and iv.get_mode() == iv.MODE_CAPTURE_ONLY
     mla = r.compilation_config.static_forward_context["mla.0"].impl
     mla.do_kv_cache_update(None, None, None, None, None, None)
     assert mla.forward_mqa("q", None, None, None) == "q" and mla.calls == ["mla_update", "mla_forward"]
+    attn0 = r.compilation_config.static_forward_context["layer.0"]
     k = torch.randn(5, 2, D)
-    r.compilation_config.static_forward_context["layer.0"].impl.do_kv_cache_update(None, k, k, None, torch.arange(5))
+    attn0.impl.do_kv_cache_update(None, k, k, attn0.kv_cache[0], torch.arange(5))
     st = iv.get_stats(r)
-    assert st["layer.0"]["buffered_tokens"] == 5 and st["_totals"]["buffered_tokens"] == 5
+    assert st["layer.0"]["compressed_tokens"] == 5 and st["_totals"]["compressed_tokens"] == 5
+    assert st["layer.0"]["memory_bytes"] == states["layer.0"].cache.device_bytes() > 0
     assert st["_totals"]["layers"] == 3
+    cache_bytes = attn0.kv_cache[0].nelement() * 4
     freed = vab.free_kv_cache(r)
-    assert freed == 2 * 1000 * 2                           # the two flash layers' caches
+    assert freed == 2 * cache_bytes                               # the two flash layers' caches
     ctx = r.compilation_config.static_forward_context
     assert ctx["layer.0"].kv_cache[0].numel() == 1 and ctx["mla.0"].kv_cache[0].numel() == 1000
-    assert iv.free_kv_cache(FakeRunner(n_layers=1)) == 0   # nothing hooked
+    assert all(t.numel() == 1 for t in r.kv_caches[:2]) and r.kv_caches[2].numel() == 1000
+    assert iv.free_kv_cache(FakeRunner(n_layers=1)) == 0          # nothing hooked
+
+
+def test_enable_no_alloc_layout_wrapper_takes_vllm_022_arguments(monkeypatch):
+    pytest.importorskip("vllm")
+    from vllm.v1.executor.abstract import Executor
+    from vllm.v1.worker.gpu_model_runner import GPUModelRunner
+    seen = []
+
+    def layout(self, kv_caches, kernel_block_sizes):
+        seen.append((dict(kv_caches), kernel_block_sizes))
+
+    monkeypatch.setattr(GPUModelRunner, "_update_hybrid_attention_mamba_layout", layout)
+    monkeypatch.setattr(GPUModelRunner, "_smaq_layout_patch", False, raising=False)
+    monkeypatch.setattr(Executor, "_smaq_patched", False, raising=False)
+    monkeypatch.setattr(Executor, "get_kv_cache_specs", lambda self: "specs")
+    vab.enable_no_alloc(key_bits=3)
+    runner = types.SimpleNamespace(shared_kv_cache_layers={"l1": "l0"})
+    GPUModelRunner._update_hybrid_attention_mamba_layout(runner, {"l0": "cache0"}, [16])
+    assert seen == [({"l0": "cache0", "l1": "cache0"}, [16])]
+
+    calls = []
+
+    class FakeExecutor:
+        def collective_rpc(self, fn):
+            calls.append(fn)
+
+    assert Executor.get_kv_cache_specs(FakeExecutor()) == "specs" and len(calls) == 1
+
+
+def test_backend_registers_as_custom():
+    pytest.importorskip("vllm")
+    from vllm.v1.attention.backends.flash_attn import FlashAttentionImpl
+    from vllm.v1.attention.backends.registry import AttentionBackendEnum
+    from smaq_b200.integration import vllm_backend as vb
+    try:
+        path = vb.register(key_bits=4, ring_capacity=64)
+        assert AttentionBackendEnum.CUSTOM.get_path() == path
+        cls = AttentionBackendEnum.CUSTOM.get_class()
+        assert cls is vb.SmaqAttentionBackend and cls.get_name() == "CUSTOM"
+        assert issubclass(cls.get_impl_cls(), FlashAttentionImpl)
+        assert iv.get_mode() == iv.MODE_HYBRID
+        cfg = vb._layer_config(types.SimpleNamespace(head_size=128, num_kv_heads=8, num_heads=32), 9,
+                               torch.device("cpu"))
+        assert (cfg.key_bits, cfg.ring_capacity, cfg.num_query_heads) == (4, 64, 32)
+    finally:
+        AttentionBackendEnum.CUSTOM.clear_override()
+        iv.set_mode(iv.MODE_CAPTURE_ONLY)
