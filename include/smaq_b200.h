@@ -22,6 +22,9 @@
  *                                  smaq/quantizer.py:154-184, SMAQBlockVQ.attention_score
  *                                  smaq/block_vq.py:273-297, dequantize_values
  *                                  smaq/kv_cache.py:94-103)
+ *   smaq_key_scores            <- SMAQQuantizer.attention_score   smaq/quantizer.py:154-184,
+ *                                 SMAQBlockVQ.attention_score     smaq/block_vq.py:273-297
+ *   smaq_attend_values         <- SMAQKVCache.attend (history)    smaq/kv_cache.py:243-267
  *   smaq_merge_partials        <- (new) log-sum-exp combine of sequence-split partials;
  *                                 the reference has no multi-GPU path.
  *
@@ -77,7 +80,8 @@ enum {
 
 int smaq_abi_version(void);
 /* No counterpart in the reference.  sizeof(smaq_append_args) for which = 0, sizeof(smaq_decode_args)
- * for which = 1, else 0: a binding compares its own mirror of the structs with these. */
+ * for which = 1, sizeof(smaq_scores_args) for 2, sizeof(smaq_attend_args) for 3, else 0: a binding
+ * compares its own mirror of the structs with these. */
 size_t smaq_args_size(int which);
 const char* smaq_last_error(void);
 
@@ -237,6 +241,83 @@ int smaq_merge_partials(const float* partials, int n_parts, int batch, int n_q_h
 int smaq_decode_status(const void* workspace, int batch, int n_kv_heads, void* stream);
 int smaq_append_status(void* stream);
 int smaq_selftest_wait_timeout(unsigned int spin_limit, void* stream);
+
+
+/* ------------------------------------------------------------------ standalone scores / attend */
+
+/* Scores of query rows against compressed history keys, without a softmax:
+ *   out[g, q, t] = scale * q[g, q] . k_hat[g, t]          (in out_dtype)
+ * Replaces SMAQQuantizer.attention_score (smaq/quantizer.py:154-184), SMAQBlockVQ.attention_score
+ * (smaq/block_vq.py:273-297) and the history half of SMAQKVCache.attention_scores
+ * (smaq/kv_cache.py:218-241).  Keys in the reference layout:
+ *   scalar: the packed row of token (g, t) at key_codes + g*codes_stride_g + t*ceil(D/(8/bits))
+ *           bytes, its norm at key_norms + g*norms_stride_g + t (norms_dtype); k_hat =
+ *           (centroids[codes] @ E_inv) * norm, computed as (q @ E_inv^T) . centroids[codes] * norm;
+ *   bvq:    index (g, t, block) at key_idx + g*idx_stride_g + t*(D/block_dim) + block (uint8, or
+ *           int64 when idx_is_int64); k_hat = decoded_centroids[block][index] ([D/bd, nc, bd] fp32).
+ * Queries: element (g, q, d) at q + g*q_stride_g + q*q_stride_q + d.  D % 32 == 0, D <= 256. */
+typedef struct smaq_scores_args {
+  const void* q;
+  int q_dtype;
+  int64_t q_stride_g, q_stride_q;
+  int64_t n_groups;
+  int n_queries;
+  int64_t n_tokens;
+  int head_dim;
+  int key_format;                  /* SMAQ_KEYS_SCALAR or SMAQ_KEYS_BVQ */
+  const uint8_t* key_codes;        /* scalar */
+  int64_t codes_stride_g;          /* bytes */
+  const void* key_norms;           /* scalar */
+  int norms_dtype;
+  int64_t norms_stride_g;          /* elements */
+  int key_bits;                    /* scalar: 2, 3 or 4 */
+  const float* E_inv;              /* scalar: [D, D] */
+  const float* centroids;          /* scalar: [2^bits] */
+  const void* key_idx;             /* bvq */
+  int idx_is_int64;
+  int64_t idx_stride_g;            /* elements */
+  int block_dim;                   /* bvq */
+  int n_centroids;                 /* bvq: <= 256 */
+  const float* decoded_centroids;  /* bvq */
+  float scale;
+  void* out;
+  int out_dtype;
+  int64_t out_stride_g, out_stride_q;  /* element (g, q, t) at out + g*.. + q*.. + t */
+} smaq_scores_args;
+int smaq_key_scores(const smaq_scores_args* args, void* stream);
+
+/* Weighted sum of compressed history values (caller-given weights, e.g. a softmax):
+ *   out[g, q, :] = sum_t w[g, q, t] * (code[g, t, :] * scale[g, t, grp] + zero[g, t, grp])
+ * Replaces the history half of SMAQKVCache.attend (smaq/kv_cache.py:243-267) with
+ * dequantize_values (smaq/kv_cache.py:94-103) fused in.  Value rows in the reference layout:
+ * row (g, t) at v_data + g*data_stride_g + t*D*bits/8 bytes; scale / zero (g, t, grp) at
+ * v_scales / v_zeros + g*sz_stride_g + t*(D/group_size) + grp.  Weights: element (g, q, t) at
+ * w + g*w_stride_g + q*w_stride_q + t.  The token range is split over CTAs; the partial sums go
+ * to the workspace (smaq_attend_workspace_size bytes) and are added in a fixed order. */
+typedef struct smaq_attend_args {
+  const void* w;
+  int w_dtype;
+  int64_t w_stride_g, w_stride_q;
+  int64_t n_groups;
+  int n_queries;
+  int64_t n_tokens;
+  int head_dim;
+  const uint8_t* v_data;
+  int64_t data_stride_g;           /* bytes */
+  const void* v_scales;
+  const void* v_zeros;
+  int sz_dtype;
+  int64_t sz_stride_g;             /* elements */
+  int value_bits;                  /* 2 or 4 */
+  int group_size;
+  void* out;
+  int out_dtype;
+  int64_t out_stride_g, out_stride_q;  /* element (g, q, d) */
+  void* workspace;
+  size_t workspace_bytes;
+} smaq_attend_args;
+size_t smaq_attend_workspace_size(int64_t n_groups, int n_queries, int64_t n_tokens, int head_dim);
+int smaq_attend_values(const smaq_attend_args* args, void* stream);
 
 #ifdef __cplusplus
 }

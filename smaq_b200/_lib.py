@@ -24,6 +24,7 @@ EXPORTS = (
     "smaq_decode_kernel_path",
     "smaq_merge_partials", "smaq_decode_noalloc", "smaq_decode_noalloc_max_workspace",
     "smaq_decode_status", "smaq_append_status", "smaq_selftest_wait_timeout",
+    "smaq_key_scores", "smaq_attend_workspace_size", "smaq_attend_values",
 )
 
 vp = C.c_void_p
@@ -59,6 +60,28 @@ class DecodeArgs(C.Structure):
     ]
 
 
+class ScoresArgs(C.Structure):
+    _fields_ = [
+        ("q", vp), ("q_dtype", i32), ("q_stride_g", i64), ("q_stride_q", i64), ("n_groups", i64),
+        ("n_queries", i32), ("n_tokens", i64), ("head_dim", i32), ("key_format", i32),
+        ("key_codes", vp), ("codes_stride_g", i64), ("key_norms", vp), ("norms_dtype", i32),
+        ("norms_stride_g", i64), ("key_bits", i32), ("E_inv", vp), ("centroids", vp),
+        ("key_idx", vp), ("idx_is_int64", i32), ("idx_stride_g", i64), ("block_dim", i32),
+        ("n_centroids", i32), ("decoded_centroids", vp), ("scale", C.c_float),
+        ("out", vp), ("out_dtype", i32), ("out_stride_g", i64), ("out_stride_q", i64),
+    ]
+
+
+class AttendArgs(C.Structure):
+    _fields_ = [
+        ("w", vp), ("w_dtype", i32), ("w_stride_g", i64), ("w_stride_q", i64), ("n_groups", i64),
+        ("n_queries", i32), ("n_tokens", i64), ("head_dim", i32), ("v_data", vp), ("data_stride_g", i64),
+        ("v_scales", vp), ("v_zeros", vp), ("sz_dtype", i32), ("sz_stride_g", i64), ("value_bits", i32),
+        ("group_size", i32), ("out", vp), ("out_dtype", i32), ("out_stride_g", i64), ("out_stride_q", i64),
+        ("workspace", vp), ("workspace_bytes", C.c_size_t),
+    ]
+
+
 _lib = None
 
 
@@ -76,7 +99,7 @@ def load() -> C.CDLL:
     lib.smaq_abi_version.restype = i32
     lib.smaq_args_size.argtypes = [i32]
     lib.smaq_args_size.restype = C.c_size_t
-    for which, mirror in ((0, AppendArgs), (1, DecodeArgs)):
+    for which, mirror in ((0, AppendArgs), (1, DecodeArgs), (2, ScoresArgs), (3, AttendArgs)):
         if lib.smaq_args_size(which) != C.sizeof(mirror):
             raise RuntimeError(f"{path}: {mirror.__name__} is {C.sizeof(mirror)} bytes here but "
                                f"{lib.smaq_args_size(which)} in the library (stale build or ABI mismatch)")
@@ -106,6 +129,12 @@ def load() -> C.CDLL:
     lib.smaq_append_status.restype = i32
     lib.smaq_selftest_wait_timeout.argtypes = [C.c_uint, vp]
     lib.smaq_selftest_wait_timeout.restype = i32
+    lib.smaq_key_scores.argtypes = [C.POINTER(ScoresArgs), vp]
+    lib.smaq_key_scores.restype = i32
+    lib.smaq_attend_workspace_size.argtypes = [i64, i32, i64, i32]
+    lib.smaq_attend_workspace_size.restype = C.c_size_t
+    lib.smaq_attend_values.argtypes = [C.POINTER(AttendArgs), vp]
+    lib.smaq_attend_values.restype = i32
     _lib = lib
     return lib
 

@@ -16,6 +16,7 @@ import torch
 import torch.nn as nn
 
 from smaq_b200 import ops
+from smaq_b200._lib import SMAQ_KEYS_BVQ
 from smaq_b200.ssf import build_smaq_metric
 
 
@@ -140,12 +141,10 @@ class SMAQBlockVQ(nn.Module):
 
     def attention_score(self, query: torch.Tensor, quantized_key: BlockVQQuantized,
                         scale: Optional[float] = None) -> torch.Tensor:
-        """``q . k_hat [* scale]`` in the query dtype (standalone scoring)."""
-        k_hat = self.dequantize(quantized_key)
-        s = torch.matmul(query.float(), k_hat.float().transpose(-2, -1))
-        if scale is not None:
-            s = s * scale
-        return s.to(query.dtype)
+        """``q . k_hat [* scale]`` in the query dtype (smaq/block_vq.py:273-297): one
+        ``smaq_key_scores`` launch over per-block score tables, no key reconstruction."""
+        return ops.key_scores(query, key_format=SMAQ_KEYS_BVQ, scale=scale, key_idx=quantized_key.indices,
+                              decoded_centroids=self.decoded_centroids)
 
     def logit_mse(self, queries: torch.Tensor, keys: torch.Tensor) -> float:
         """Held-out logit MSE ``E[(q . (k - k_hat))^2]``."""

@@ -39,6 +39,10 @@ int num_sms() {
 
 extern "C" int smaq_abi_version(void) { return SMAQ_ABI_VERSION; }
 extern "C" size_t smaq_args_size(int which) {
-  return which == 0 ? sizeof(smaq_append_args) : which == 1 ? sizeof(smaq_decode_args) : 0;
+  return which == 0 ? sizeof(smaq_append_args)
+       : which == 1 ? sizeof(smaq_decode_args)
+       : which == 2 ? sizeof(smaq_scores_args)
+       : which == 3 ? sizeof(smaq_attend_args)
+                    : 0;
 }
 extern "C" const char* smaq_last_error(void) { return smaq::g_err; }

@@ -67,35 +67,81 @@ def dequantize_values(vq: ValueQuantized, group_size: int = 32) -> torch.Tensor:
     return out.reshape(*q.shape[:-2], d)
 
 
-class SMAQKVCache:
-    """HF-style cache: compressed history plus an exact recent buffer (smaq/kv_cache.py:106-290).
+class _GrowingRows:
+    """Compressed history of an HF-style cache: every tensor field of a quantized-keys or
+    ``ValueQuantized`` tuple kept in one buffer per field that grows by doubling along the token
+    axis (axis ``len(lead)``), so an append writes only the new rows and the kernels read the
+    first ``n`` rows of each buffer in place."""
 
-    Tensors are ``[..., T, D]``.  Keys go through the strategy's GPU quantizer; values through
-    ``quantize_values``.  ``attention_scores`` returns the concatenated ``[history || buffer]``
-    logits, ``attend`` applies caller-computed weights.
-    """
+    def __init__(self):
+        self.n = 0
+        self._buf: dict[str, torch.Tensor] = {}
+        self._proto = None
+        self._axis = 0
+
+    def append(self, q: NamedTuple, axis: int) -> None:
+        fields = q._asdict()
+        m = next(v for v in fields.values() if isinstance(v, torch.Tensor)).shape[axis]
+        need = self.n + m
+        cap = next(iter(self._buf.values())).shape[axis] if self._buf else 0
+        if need > cap:
+            new_cap = max(need, 2 * cap, 64)
+            for k, v in fields.items():
+                if not isinstance(v, torch.Tensor):
+                    continue
+                shape = list(v.shape)
+                shape[axis] = new_cap
+                nb = torch.empty(shape, dtype=v.dtype, device=v.device)
+                if self.n:
+                    nb.narrow(axis, 0, self.n).copy_(self._buf[k].narrow(axis, 0, self.n))
+                self._buf[k] = nb
+        for k, v in fields.items():
+            if isinstance(v, torch.Tensor):
+                self._buf[k].narrow(axis, self.n, m).copy_(v)
+        self._proto, self._axis = q, axis
+        self.n = need
+
+    def view(self):
+        """The history as the tuple type it was appended as (views of the first n rows)."""
+        if self._proto is None:
+            return None
+        f = {k: (self._buf[k].narrow(self._axis, 0, self.n) if isinstance(v, torch.Tensor) else v)
+             for k, v in self._proto._asdict().items()}
+        return type(self._proto)(**f)
+
+
+class SMAQKVCache:
+    """HF-style cache, tensors ``[..., T, D]`` (API of smaq/kv_cache.py:106-290): compressed
+    history plus an exact buffer of the last ``buffer_size`` tokens.  A prefill longer than the
+    buffer compresses all but its last ``buffer_size`` tokens; an append that overfills the
+    buffer compresses the oldest overflow (smaq/kv_cache.py:150-216).  Keys go through the
+    strategy's GPU quantizer, values through ``quantize_values``; the history is kept in
+    growing device buffers (``_GrowingRows``).  ``attention_scores`` returns the
+    ``[history || buffer]`` logits -- the history part one ``smaq_key_scores`` launch -- and
+    ``attend`` applies caller-computed weights, the history part one ``smaq_attend_values``
+    launch with the dequantization fused."""
 
     def __init__(self, head_dim: int, Sigma_q: torch.Tensor | None = None, key_bits: int = 3,
                  value_bits: int = 2, value_group_size: int = 32, buffer_size: int = 128,
                  device: torch.device | None = None, dtype: torch.dtype = torch.float16, layer_idx: int = 0,
                  key_strategy: Any | None = None, calibration_provider: CalibrationProvider | None = None):
         self.head_dim = head_dim
-        self.key_bits = key_bits
-        self.value_bits = value_bits
-        self.value_group_size = value_group_size
+        self.key_bits, self.value_bits, self.value_group_size = key_bits, value_bits, value_group_size
         self.buffer_size = buffer_size
         self.device = torch.device(device) if device is not None else torch.device(
             "cuda" if torch.cuda.is_available() else "cpu")
         self.dtype = dtype
         self.layer_idx = layer_idx
         self.calibration_provider = calibration_provider or IdentityCalibrationProvider()
-        sigma = Sigma_q if Sigma_q is not None else self.calibration_provider.get_sigma_q(
-            layer_idx, head_dim, device=self.device)
-        self.key_quantizer = key_strategy or SMAQFullMetricScalarStrategy(
-            dim=head_dim, Sigma_q=sigma, bits=key_bits, device=self.device, dtype=torch.float32)
+        if key_strategy is None:
+            sigma = Sigma_q if Sigma_q is not None else self.calibration_provider.get_sigma_q(
+                layer_idx, head_dim, device=self.device)
+            key_strategy = SMAQFullMetricScalarStrategy(dim=head_dim, Sigma_q=sigma, bits=key_bits,
+                                                        device=self.device, dtype=torch.float32)
+        self.key_quantizer = key_strategy
         self.seq_len = 0
-        self.key_quantized: Optional[Any] = None
-        self.value_quantized: Optional[ValueQuantized] = None
+        self._keys = _GrowingRows()
+        self._values = _GrowingRows()
         self.key_buffer: Optional[torch.Tensor] = None
         self.value_buffer: Optional[torch.Tensor] = None
 
@@ -103,54 +149,46 @@ class SMAQKVCache:
     def capabilities(self) -> CacheCapabilities:
         return self.key_quantizer.capabilities
 
-    def _compress(self, k: torch.Tensor, v: torch.Tensor):
-        return (self.key_quantizer.quantize(k),
-                quantize_values(v, bits=self.value_bits, group_size=self.value_group_size))
+    @property
+    def key_quantized(self):
+        return self._keys.view()
+
+    @property
+    def value_quantized(self) -> Optional[ValueQuantized]:
+        return self._values.view()
+
+    def _compress(self, k: torch.Tensor, v: torch.Tensor) -> None:
+        axis = k.dim() - 2
+        self._keys.append(self.key_quantizer.quantize(k), axis)
+        self._values.append(quantize_values(v, bits=self.value_bits, group_size=self.value_group_size), axis)
+
+    def _keep_last(self, keys: torch.Tensor, values: torch.Tensor) -> None:
+        """Buffer the last buffer_size tokens of keys/values, compressing the rest."""
+        cut = keys.shape[-2] - self.buffer_size
+        if cut > 0:
+            self._compress(keys[..., :cut, :], values[..., :cut, :])
+            keys, values = keys[..., cut:, :], values[..., cut:, :]
+        self.key_buffer, self.value_buffer = keys, values
 
     def prefill(self, keys: torch.Tensor, values: torch.Tensor):
-        n = keys.shape[-2]
-        self.seq_len = n
-        if n <= self.buffer_size:
-            self.key_buffer, self.value_buffer = keys, values
-            return
-        cut = n - self.buffer_size
-        self.key_buffer, self.value_buffer = keys[..., cut:, :], values[..., cut:, :]
-        self.key_quantized, self.value_quantized = self._compress(keys[..., :cut, :], values[..., :cut, :])
+        self.seq_len = keys.shape[-2]
+        self._keys, self._values = _GrowingRows(), _GrowingRows()
+        self._keep_last(keys, values)
 
     def append(self, key: torch.Tensor, value: torch.Tensor):
         self.seq_len += key.shape[-2]
-        if self.key_buffer is None:
-            self.key_buffer, self.value_buffer = key, value
-        else:
-            self.key_buffer = torch.cat([self.key_buffer, key], dim=-2)
-            self.value_buffer = torch.cat([self.value_buffer, value], dim=-2)
-        if self.key_buffer.shape[-2] > self.buffer_size:
-            self._flush_buffer()
-
-    def _flush_buffer(self):
-        cut = self.key_buffer.shape[-2] - self.buffer_size
-        kq, vq = self._compress(self.key_buffer[..., :cut, :], self.value_buffer[..., :cut, :])
-        self.key_buffer = self.key_buffer[..., cut:, :]
-        self.value_buffer = self.value_buffer[..., cut:, :]
-        if self.key_quantized is None:
-            self.key_quantized, self.value_quantized = kq, vq
-            return
-        self.key_quantized = self.key_quantizer.concat_quantized([self.key_quantized, kq])
-        old = self.value_quantized
-        self.value_quantized = ValueQuantized(
-            data=torch.cat([old.data, vq.data], dim=-2), scales=torch.cat([old.scales, vq.scales], dim=-2),
-            zeros=torch.cat([old.zeros, vq.zeros], dim=-2), bits=self.value_bits)
+        if self.key_buffer is not None:
+            key = torch.cat([self.key_buffer, key], dim=-2)
+            value = torch.cat([self.value_buffer, value], dim=-2)
+        self._keep_last(key, value)
 
     def attention_scores(self, query: torch.Tensor, scale: float | None = None) -> torch.Tensor:
         if scale is None:
             scale = 1.0 / math.sqrt(self.head_dim)
         parts = []
-        if self.key_quantized is not None:
-            if getattr(self.key_quantizer, "supports_kernel", False):
-                parts.append(self.key_quantizer.attention_score(query, self.key_quantized, scale=scale,
-                                                                use_kernel=True))
-            else:
-                parts.append(self.key_quantizer.attention_score(query, self.key_quantized, scale=scale))
+        kq = self.key_quantized
+        if kq is not None:
+            parts.append(self.key_quantizer.attention_score(query, kq, scale=scale))
         if self.key_buffer is not None:
             parts.append(torch.matmul(query, self.key_buffer.transpose(-2, -1)) * scale)
         if not parts:
@@ -158,32 +196,31 @@ class SMAQKVCache:
         return torch.cat(parts, dim=-1)
 
     def attend(self, attn_weights: torch.Tensor) -> torch.Tensor:
-        outs = []
-        col = 0
-        if self.value_quantized is not None:
-            nq = self.value_quantized.data.shape[-2]
-            v = dequantize_values(self.value_quantized, self.value_group_size)
-            outs.append(torch.matmul(attn_weights[..., col:col + nq], v))
-            col += nq
+        out = None
+        n_hist = self._values.n
+        vq = self.value_quantized
+        if vq is not None:
+            out = ops.attend_values(attn_weights[..., :n_hist], vq.data, vq.scales, vq.zeros, bits=vq.bits,
+                                    group_size=self.value_group_size, head_dim=self.head_dim)
         if self.value_buffer is not None:
             nb = self.value_buffer.shape[-2]
-            outs.append(torch.matmul(attn_weights[..., col:col + nb], self.value_buffer))
-        if not outs:
+            part = torch.matmul(attn_weights[..., n_hist:n_hist + nb], self.value_buffer.to(attn_weights.dtype))
+            out = part if out is None else out + part
+        if out is None:
             return torch.zeros(*attn_weights.shape[:-1], self.head_dim, device=attn_weights.device,
                                dtype=attn_weights.dtype)
-        return sum(outs)
+        return out
 
     def memory_bytes(self) -> dict[str, int]:
-        info = {"quantized_keys": 0, "quantized_values": 0, "buffer": 0, "total": 0}
-        if self.key_quantized is not None:
-            info["quantized_keys"] += self.key_quantizer.memory_bytes(self.key_quantized)
-        if self.value_quantized is not None:
-            vq = self.value_quantized
-            info["quantized_values"] += vq.data.nelement() + 2 * vq.scales.nelement() + 2 * vq.zeros.nelement()
-        for buf in (self.key_buffer, self.value_buffer):
-            if buf is not None:
-                info["buffer"] += buf.nelement() * 2
-        info["total"] = info["quantized_keys"] + info["quantized_values"] + info["buffer"]
+        """Bytes with the reference's accounting (smaq/kv_cache.py:269-285)."""
+        info = {"quantized_keys": 0, "quantized_values": 0, "buffer": 0}
+        kq, vq = self.key_quantized, self.value_quantized
+        if kq is not None:
+            info["quantized_keys"] = self.key_quantizer.memory_bytes(kq)
+        if vq is not None:
+            info["quantized_values"] = vq.data.nelement() + 2 * (vq.scales.nelement() + vq.zeros.nelement())
+        info["buffer"] = sum(2 * b.nelement() for b in (self.key_buffer, self.value_buffer) if b is not None)
+        info["total"] = sum(info.values())
         return info
 
     def get_seq_length(self) -> int:

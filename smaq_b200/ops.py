@@ -169,6 +169,105 @@ def append(key: Optional[torch.Tensor], value: Optional[torch.Tensor], *, n_head
     _lib.check(lib.smaq_append(a, _stream()), "smaq_append")
 
 
+# --------------------------------------------------------------------- standalone scores / attend
+def _packed_rows(t: torch.Tensor) -> torch.Tensor:
+    """``t`` with packed rows (last dim contiguous, rows back to back within a group); a group
+    stride may be anything (a capacity buffer sliced along its token dim keeps its storage)."""
+    if t.stride(-1) == 1 and (t.dim() < 2 or t.shape[-2] <= 1 or t.stride(-2) == t.shape[-1]):
+        return t
+    return t.contiguous()
+
+
+def _groups(lead: torch.Size, *ts: torch.Tensor, tail: tuple[int, ...]) -> list[torch.Tensor]:
+    """Each tensor broadcast to ``lead + its own trailing dims`` and flattened to ``[G, ...]``."""
+    out = []
+    for t, k in zip(ts, tail):
+        t = t.expand(*lead, *t.shape[t.dim() - k:])
+        out.append(t.reshape(-1, *t.shape[len(lead):]))
+    return out
+
+
+def key_scores(query: torch.Tensor, *, key_format: int, scale: Optional[float] = None,
+               key_codes: Optional[torch.Tensor] = None, key_norms: Optional[torch.Tensor] = None, key_bits: int = 3,
+               E_inv: Optional[torch.Tensor] = None, centroids: Optional[torch.Tensor] = None,
+               key_idx: Optional[torch.Tensor] = None, decoded_centroids: Optional[torch.Tensor] = None
+               ) -> torch.Tensor:
+    """``scale * q . k_hat`` of ``query [..., Q, D]`` against compressed keys (reference layout):
+    scalar ``key_codes [..., N, ceil(D/(8/bits))]`` + ``key_norms [..., N]``, or block-VQ
+    ``key_idx [..., N, D/bd]`` (uint8 or int64).  Leading dims broadcast.  Returns ``[..., Q, N]`` in
+    the query dtype (smaq_key_scores)."""
+    _cuda(query, key_codes, key_idx)
+    lib = _lib.load()
+    D = query.shape[-1]
+    keys = key_codes if key_format == SMAQ_KEYS_SCALAR else key_idx
+    lead = torch.broadcast_shapes(query.shape[:-2], keys.shape[:-2])
+    N = keys.shape[-2]
+    (q,) = _groups(lead, query, tail=(2,))
+    q = q if q.stride(-1) == 1 else q.contiguous()
+    G, Q = q.shape[0], q.shape[1]
+    out = torch.empty((G, Q, N), dtype=query.dtype, device=query.device)
+    a = _lib.ScoresArgs()
+    a.q, a.q_dtype, a.q_stride_g, a.q_stride_q = q.data_ptr(), dtype_code(q.dtype), q.stride(0), q.stride(1)
+    a.n_groups, a.n_queries, a.n_tokens, a.head_dim = G, Q, N, D
+    a.key_format = key_format
+    a.scale = float(1.0 if scale is None else scale)
+    keep = [q]
+    if key_format == SMAQ_KEYS_SCALAR:
+        codes, norms = _groups(lead, key_codes, key_norms, tail=(2, 1))
+        codes, norms = _packed_rows(codes), (norms if norms.stride(-1) == 1 else norms.contiguous())
+        Ei = E_inv.to(torch.float32).contiguous()
+        cf = centroids.to(torch.float32).contiguous()
+        keep += [codes, norms, Ei, cf]
+        a.key_codes, a.codes_stride_g = codes.data_ptr(), codes.stride(0)
+        a.key_norms, a.norms_dtype, a.norms_stride_g = norms.data_ptr(), dtype_code(norms.dtype), norms.stride(0)
+        a.key_bits, a.E_inv, a.centroids = key_bits, Ei.data_ptr(), cf.data_ptr()
+    else:
+        (idx,) = _groups(lead, key_idx, tail=(2,))
+        idx = _packed_rows(idx)
+        if idx.dtype not in (torch.uint8, torch.int64):
+            idx = idx.to(torch.int64)
+        dc = decoded_centroids.to(torch.float32).contiguous()
+        keep += [idx, dc]
+        a.key_idx, a.idx_is_int64, a.idx_stride_g = idx.data_ptr(), int(idx.dtype == torch.int64), idx.stride(0)
+        a.block_dim, a.n_centroids, a.decoded_centroids = dc.shape[2], dc.shape[1], dc.data_ptr()
+    a.out, a.out_dtype, a.out_stride_g, a.out_stride_q = out.data_ptr(), dtype_code(out.dtype), out.stride(0), \
+        out.stride(1)
+    _lib.check(lib.smaq_key_scores(a, _stream()), "smaq_key_scores")
+    return out.reshape(*lead, Q, N)
+
+
+def attend_values(weights: torch.Tensor, v_data: torch.Tensor, v_scales: torch.Tensor, v_zeros: torch.Tensor, *,
+                  bits: int = 2, group_size: int = 32, head_dim: Optional[int] = None,
+                  out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """``weights [..., Q, N]`` applied to compressed values ``v_data [..., N, D*bits/8]`` with
+    ``v_scales / v_zeros [..., N, D/group_size]`` (reference layout): ``[..., Q, D]`` in the
+    weights dtype (smaq_attend_values, dequantization fused)."""
+    _cuda(weights, v_data)
+    lib = _lib.load()
+    D = head_dim or v_data.shape[-1] * 8 // bits
+    lead = torch.broadcast_shapes(weights.shape[:-2], v_data.shape[:-2])
+    w, = _groups(lead, weights, tail=(2,))
+    w = w if w.stride(-1) == 1 else w.contiguous()
+    data, sc, zs = (_packed_rows(t) for t in _groups(lead, v_data, v_scales, v_zeros, tail=(2, 2, 2)))
+    if zs.dtype != sc.dtype:
+        zs = zs.to(sc.dtype)
+    G, Q, N = w.shape
+    out = torch.empty((G, Q, D), dtype=out_dtype or weights.dtype, device=weights.device)
+    ws_bytes = int(lib.smaq_attend_workspace_size(G, Q, N, D))
+    ws = torch.empty((max(ws_bytes, 16),), dtype=torch.uint8, device=weights.device)
+    a = _lib.AttendArgs()
+    a.w, a.w_dtype, a.w_stride_g, a.w_stride_q = w.data_ptr(), dtype_code(w.dtype), w.stride(0), w.stride(1)
+    a.n_groups, a.n_queries, a.n_tokens, a.head_dim = G, Q, N, D
+    a.v_data, a.data_stride_g = data.data_ptr(), data.stride(0)
+    a.v_scales, a.v_zeros, a.sz_dtype, a.sz_stride_g = sc.data_ptr(), zs.data_ptr(), dtype_code(sc.dtype), sc.stride(0)
+    a.value_bits, a.group_size = bits, group_size
+    a.out, a.out_dtype, a.out_stride_g, a.out_stride_q = out.data_ptr(), dtype_code(out.dtype), out.stride(0), \
+        out.stride(1)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    _lib.check(lib.smaq_attend_values(a, _stream()), "smaq_attend_values")
+    return out.reshape(*lead, Q, D)
+
+
 # --------------------------------------------------------------------- decode
 def decode_workspace_bytes(batch: int, n_q_heads: int, n_kv_heads: int, head_dim: int, num_ctas: int = 0) -> int:
     return int(_lib.load().smaq_decode_workspace_size(batch, n_q_heads, n_kv_heads, head_dim, num_ctas))

@@ -22,6 +22,7 @@ from __future__ import annotations
 import torch
 
 from smaq_b200 import ops
+from smaq_b200._lib import SMAQ_KEYS_SCALAR
 from smaq_b200.quantizer import SMAQQuantized, _normal_ppf, _unpack_indices
 from smaq_b200.ssf import ssf_log
 
@@ -197,16 +198,11 @@ class RotationAdapter(torch.nn.Module):
 
     def attention_score(self, query: torch.Tensor, quantized_key: SMAQQuantized,
                         scale: float | None = None) -> torch.Tensor:
-        """Scores ``rotate_query(q) . centroids[codes] * norm [* scale]`` in the query dtype.
-
-        Standalone scoring; the fused decode kernel computes the same scores internally."""
-        ops._cuda(query, quantized_key.indices)
-        y = self.centroids[_unpack_indices(quantized_key.indices, quantized_key.bits, self.dim)]
-        s = torch.matmul(self.rotate_query(query), y.float().transpose(-2, -1))
-        s = s * quantized_key.norms.unsqueeze(-2)
-        if scale is not None:
-            s = s * scale
-        return s.to(query.dtype)
+        """Scores ``rotate_query(q) . centroids[codes] * norm [* scale]`` in the query dtype,
+        one ``smaq_key_scores`` launch (the rotation and coordinate scales fused in E_inv)."""
+        return ops.key_scores(query, key_format=SMAQ_KEYS_SCALAR, scale=scale, key_codes=quantized_key.indices,
+                              key_norms=quantized_key.norms, key_bits=quantized_key.bits, E_inv=self.E_inv,
+                              centroids=self.centroids)
 
     def forward(self, k: torch.Tensor) -> torch.Tensor:
         return self.dequantize(self.quantize(k))

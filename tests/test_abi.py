@@ -29,7 +29,9 @@ def test_struct_mirrors_match_the_library():
     lib = _lib.load()  # also raises on a mismatch
     assert lib.smaq_args_size(0) == ctypes.sizeof(_lib.AppendArgs)
     assert lib.smaq_args_size(1) == ctypes.sizeof(_lib.DecodeArgs)
-    assert lib.smaq_args_size(2) == 0
+    assert lib.smaq_args_size(2) == ctypes.sizeof(_lib.ScoresArgs)
+    assert lib.smaq_args_size(3) == ctypes.sizeof(_lib.AttendArgs)
+    assert lib.smaq_args_size(4) == 0
 
 
 def test_invalid_arguments_are_reported_without_a_gpu():
