@@ -25,6 +25,7 @@
  *   smaq_key_scores            <- SMAQQuantizer.attention_score   smaq/quantizer.py:154-184,
  *                                 SMAQBlockVQ.attention_score     smaq/block_vq.py:273-297
  *   smaq_attend_values         <- SMAQKVCache.attend (history)    smaq/kv_cache.py:243-267
+ *   smaq_kmeans                <- _kmeans (block-VQ calibration)  smaq/block_vq.py:37-79
  *   smaq_merge_partials        <- (new) log-sum-exp combine of sequence-split partials;
  *                                 the reference has no multi-GPU path.
  *
@@ -318,6 +319,19 @@ typedef struct smaq_attend_args {
 } smaq_attend_args;
 size_t smaq_attend_workspace_size(int64_t n_groups, int n_queries, int64_t n_tokens, int head_dim);
 int smaq_attend_values(const smaq_attend_args* args, void* stream);
+
+
+/* ------------------------------------------------------------------ calibration */
+
+/* Block-VQ calibration k-means on the device (SMAQBlockVQ.fit's _kmeans, smaq/block_vq.py:37-79):
+ * k-means++ seeding and n_iters Lloyd steps for n_blocks independent point sets at once.
+ * data [n_blocks][n_points][dim] fp32 (dim <= 16), centroids [n_blocks][n_centroids][dim] fp32
+ * out.  The draws come from a counter-based generator seeded with `seed`, not torch's, so the
+ * codebook matches the reference's in quality, not bit for bit.  Deterministic for a seed.
+ * Workspace: smaq_kmeans_workspace_size(n_blocks, n_points) bytes. */
+size_t smaq_kmeans_workspace_size(int n_blocks, int64_t n_points);
+int smaq_kmeans(const float* data, int n_blocks, int64_t n_points, int dim, int n_centroids, int n_iters,
+                uint64_t seed, float* centroids, void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

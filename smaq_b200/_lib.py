@@ -24,7 +24,8 @@ EXPORTS = (
     "smaq_decode_kernel_path",
     "smaq_merge_partials", "smaq_decode_noalloc", "smaq_decode_noalloc_max_workspace",
     "smaq_decode_status", "smaq_append_status", "smaq_selftest_wait_timeout",
-    "smaq_key_scores", "smaq_attend_workspace_size", "smaq_attend_values",
+    "smaq_key_scores", "smaq_attend_workspace_size", "smaq_attend_values", "smaq_kmeans_workspace_size",
+    "smaq_kmeans",
 )
 
 vp = C.c_void_p
@@ -135,6 +136,10 @@ def load() -> C.CDLL:
     lib.smaq_attend_workspace_size.restype = C.c_size_t
     lib.smaq_attend_values.argtypes = [C.POINTER(AttendArgs), vp]
     lib.smaq_attend_values.restype = i32
+    lib.smaq_kmeans_workspace_size.argtypes = [i32, i64]
+    lib.smaq_kmeans_workspace_size.restype = C.c_size_t
+    lib.smaq_kmeans.argtypes = [vp, i32, i64, i32, i32, i32, C.c_uint64, vp, vp, C.c_size_t, vp]
+    lib.smaq_kmeans.restype = i32
     _lib = lib
     return lib
 

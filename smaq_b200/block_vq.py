@@ -51,12 +51,17 @@ def _kmeans(data: torch.Tensor, n_centroids: int, n_iters: int = 20, seed: int =
         else:
             w = torch.full((n,), 1.0 / n, device=data.device, dtype=data.dtype)
         chosen.append(int(torch.multinomial(w, 1, generator=gen).item()))
-    cent = data[chosen].clone()
-    ones = torch.ones(n, device=data.device)
+    return _lloyd(data, data[chosen].clone(), n_iters)
+
+
+def _lloyd(data: torch.Tensor, cent: torch.Tensor, n_iters: int) -> torch.Tensor:
+    """Lloyd steps of ``_kmeans``: nearest centre, mean of the assigned points, empty clusters
+    keep their centre."""
+    ones = torch.ones(data.shape[0], device=data.device)
     for _ in range(n_iters):
         assign = torch.cdist(data, cent).argmin(dim=1)
         sums = torch.zeros_like(cent).index_add_(0, assign, data)
-        cnt = torch.zeros(n_centroids, device=data.device).index_add_(0, assign, ones)
+        cnt = torch.zeros(cent.shape[0], device=data.device).index_add_(0, assign, ones)
         hit = cnt > 0
         sums[hit] /= cnt[hit].unsqueeze(1)
         sums[~hit] = cent[~hit]
@@ -102,21 +107,32 @@ class SMAQBlockVQ(nn.Module):
         return math.log2(self.n_centroids) / self.block_dim
 
     def fit(self, calibration_keys: torch.Tensor, calibration_queries: torch.Tensor, kmeans_iters: int = 20,
-            seed: int = 42) -> "SMAQBlockVQ":
+            seed: int = 42, kmeans: str = "auto") -> "SMAQBlockVQ":
         """Per block: uncentered query covariance -> metric -> k-means in the shaped space ->
-        pre-decoded centroids ``centroid @ E_inv_b^T`` (smaq/block_vq.py:160-210)."""
+        pre-decoded centroids ``centroid @ E_inv_b^T`` (smaq/block_vq.py:160-210).
+
+        ``kmeans``: "device" runs every block's k-means in one ``smaq_kmeans`` call (no host
+        round trip per centre or iteration; its own generator, so a seed gives a codebook of the
+        same quality, not the reference's); "reference" runs ``_kmeans`` block by block with the
+        reference's torch generator calls (the reference's codebook on the same device); "auto"
+        is "device" for CUDA inputs, else "reference"."""
+        if kmeans not in ("auto", "device", "reference"):
+            raise ValueError(f"kmeans must be auto, device or reference, not {kmeans!r}")
         N = calibration_keys.shape[0]
-        Es, Eis, cs, ds = [], [], [], []
+        Es, Eis, shaped = [], [], []
         for b in range(self.n_blocks):
             sl = slice(b * self.block_dim, (b + 1) * self.block_dim)
             qb = calibration_queries[:, sl].float()
             E, E_inv = build_smaq_metric((qb.T @ qb) / N, c=self.c)
-            shaped = calibration_keys[:, sl].float() @ E.T
-            cent = _kmeans(shaped, self.n_centroids, kmeans_iters, seed + b)
+            shaped.append(calibration_keys[:, sl].float() @ E.T)
             Es.append(E)
             Eis.append(E_inv)
-            cs.append(cent)
-            ds.append(cent @ E_inv.T)
+        on_device = kmeans == "device" or (kmeans == "auto" and calibration_keys.is_cuda)
+        if on_device and N >= self.n_centroids:
+            cs = list(ops.kmeans(torch.stack(shaped), self.n_centroids, kmeans_iters, seed))
+        else:
+            cs = [_kmeans(x, self.n_centroids, kmeans_iters, seed + b) for b, x in enumerate(shaped)]
+        ds = [c @ Ei.T for c, Ei in zip(cs, Eis)]
         self.E_blocks = torch.stack(Es).to(self._device, self._dtype)
         self.E_inv_blocks = torch.stack(Eis).to(self._device, self._dtype)
         self.centroids = torch.stack(cs).to(self._device, self._dtype)

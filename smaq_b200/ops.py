@@ -268,6 +268,22 @@ def attend_values(weights: torch.Tensor, v_data: torch.Tensor, v_scales: torch.T
     return out.reshape(*lead, Q, D)
 
 
+# --------------------------------------------------------------------- calibration
+def kmeans(data: torch.Tensor, n_centroids: int, n_iters: int = 20, seed: int = 42) -> torch.Tensor:
+    """k-means++ + Lloyd on the device for ``data [n_blocks, n_points, dim]`` (fp32, dim <= 16):
+    ``[n_blocks, n_centroids, dim]`` centroids, one ``smaq_kmeans`` call, no host round trips
+    inside."""
+    _cuda(data)
+    lib = _lib.load()
+    x = data.to(torch.float32).contiguous()
+    nb, n, d = x.shape
+    cent = torch.empty((nb, n_centroids, d), dtype=torch.float32, device=x.device)
+    ws = torch.empty((int(lib.smaq_kmeans_workspace_size(nb, n)),), dtype=torch.uint8, device=x.device)
+    _lib.check(lib.smaq_kmeans(x.data_ptr(), nb, n, d, n_centroids, n_iters, seed & (2 ** 64 - 1), cent.data_ptr(),
+                               ws.data_ptr(), ws.numel(), _stream()), "smaq_kmeans")
+    return cent
+
+
 # --------------------------------------------------------------------- decode
 def decode_workspace_bytes(batch: int, n_q_heads: int, n_kv_heads: int, head_dim: int, num_ctas: int = 0) -> int:
     return int(_lib.load().smaq_decode_workspace_size(batch, n_q_heads, n_kv_heads, head_dim, num_ctas))
