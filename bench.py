@@ -54,7 +54,12 @@ REF_DIR = os.path.join(REPO, "baseline", "_ref")
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the decode kernel,
 # read from one ncu capture of the same kernel on the same per-launch shape; keyed by
 # (batch, history tokens, window, query heads, kv heads) of one launch.
-NCU_TRAFFIC: dict = {}
+NCU_TRAFFIC: dict = {
+    (4, 131072, 128, 64, 8): 270_843_648 + 5_184_000,     # configs[4], decode_v3_kernel<8>
+    (16, 32768, 128, 32, 8): 277_166_336 + 8_543_232,     # configs[1], decode_v3_kernel<4>
+}
+# the same for the paged configs[3] launch (decode_s_kernel) and the configs[2] key kernel
+NCU_TRAFFIC_PAGED = 1_145_590_000 + 8_393_984
 
 
 def parse(argv=None):
@@ -959,7 +964,9 @@ def run_paged(a, rank: int, world: int):
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": paged_config(),
             "hbm_gbs": achieved,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "traffic": None, "peak_source": src,
+                         "traffic": NCU_TRAFFIC_PAGED,
+                         "traffic_source": "ncu dram bytes per launch, same per-launch shape",
+                         "peak_source": src,
                          "kernel": "one fused scalar-key decode launch per layer (paged)",
                          "algorithmic_bytes_per_launch": bpl},
             "e2e": {"value": PG_B / (e2e_ms * PG_LAYERS / n_layers * 1e-3), "unit": "tokens/s",
