@@ -214,10 +214,12 @@ int smaq_decode_kernel_path(const smaq_decode_args* args);
  * cannot allocate device memory (all device memory owned by another allocator or pool, or a
  * host that reaches the GPU only through this ABI).  Scratch comes from a fixed 8 MiB array in
  * the library's device image (held on every GPU that loads the library until exit; its size is
- * smaq_decode_noalloc_max_workspace()).  Shapes whose smaq_decode_workspace_size exceeds it are
- * rejected with SMAQ_ERR_WORKSPACE.  args->workspace / workspace_bytes are ignored.  The first
- * call on a device looks up the array's device address (cudaGetSymbolAddress) with that device
- * current, so make that first call before any stream capture.  Every call shares the one array
+ * smaq_decode_noalloc_max_workspace()).  Shapes whose workspace need, for the grid the call
+ * picks, exceeds it are rejected with SMAQ_ERR_WORKSPACE before anything is launched.
+ * args->workspace / workspace_bytes are ignored.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress) with that device current, and again whenever the current
+ * context changes (a device reset reloads the module), so make the first call -- and the first
+ * after a reset -- before any stream capture.  Every call shares the one array
  * and fully rewrites what it reads, so nothing carries over between calls; calls that can
  * overlap on the GPU (different streams, or several threads) race on it -- serialise them. */
 int smaq_decode_noalloc(const smaq_decode_args* args, void* stream);

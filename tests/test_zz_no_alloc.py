@@ -18,12 +18,12 @@ pytestmark = pytest.mark.gpu
 D = 128
 
 
-def _case(cuda, fast: bool):
+def _case(cuda, fast: bool, B=3, Hkv=2, G=4):
     import torch
     from smaq_b200 import ops
     from smaq_b200._lib import SMAQ_KEYS_BVQ
     rng = np.random.default_rng(3)
-    B, Hkv, G, T, W = 3, 2, 4, 1024, 40
+    T, W = 1024, 40
     Eb = torch.from_numpy((np.eye(8)[None] + 0.1 * rng.standard_normal((16, 8, 8))).astype(np.float32)).to(cuda)
     C = torch.from_numpy(rng.standard_normal((16, 256, 8)).astype(np.float32)).to(cuda)
     dec = torch.from_numpy((rng.standard_normal((16, 256, 8)) * 0.5).astype(np.float16).astype(np.float32)).to(cuda)
@@ -41,8 +41,9 @@ def _case(cuda, fast: bool):
     rk = torch.from_numpy(syn.keys((B, W, Hkv), D, seed=61)).to(cuda).to(torch.bfloat16)
     rv = torch.from_numpy(syn.values((B, W, Hkv), D, seed=62)).to(cuda).to(torch.bfloat16)
     kw = dict(n_kv_heads=Hkv, key_format=SMAQ_KEYS_BVQ, centroids=dec, key_codes=codes, v_data=vd, v_scales=vs,
-              v_zeros=vz, hist_len=torch.tensor([1000, 17, 600], dtype=torch.int32, device=cuda), page_size=T,
-              recent_k=rk, recent_v=rv, recent_len=torch.tensor([40, 0, 5], dtype=torch.int32, device=cuda),
+              v_zeros=vz, hist_len=torch.tensor([1000, 17, 600][:B] + [700] * (B - 3), dtype=torch.int32, device=cuda),
+              page_size=T, recent_k=rk, recent_v=rv,
+              recent_len=torch.tensor([40, 0, 5][:B] + [9] * (B - 3), dtype=torch.int32, device=cuda),
               layout=layout, centroids_f16=ops.fp16_codebook(dec) if fast else None)
     return q, kw
 
@@ -63,11 +64,26 @@ def test_noalloc_rejects_shapes_beyond_its_scratch(cuda):
     import torch
     from smaq_b200 import _lib, ops
     lib = _lib.load()
-    big = 1 << 16  # 65536 sequences x 8 kv heads needs far more than the fixed scratch
-    assert ops.decode_workspace_bytes(big, 32, 8, 128) > lib.smaq_decode_noalloc_max_workspace()
-    q = torch.zeros((big, 32, 128), dtype=torch.bfloat16, device=cuda)
+    big = 1 << 16  # 65536 sequences x 2 kv heads needs far more than the fixed scratch
+    assert ops.decode_workspace_bytes(big, 8, 2, 128) > lib.smaq_decode_noalloc_max_workspace()
+    q = torch.zeros((big, 8, 128), dtype=torch.bfloat16, device=cuda)
     _, kw = _case(cuda, True)
     kw["hist_len"] = torch.zeros((big,), dtype=torch.int32, device=cuda)
     kw["recent_len"] = None
     with pytest.raises(RuntimeError, match="scratch"):
         ops.decode(q, entry="smaq_decode_noalloc", **kw)
+
+
+def test_noalloc_alternating_shapes_and_paths(cuda):
+    """Calls of different shapes in a row reuse the scratch at different offsets (plan, pair
+    counters, error word, slots); reference-layout rows take the multi-launch general path."""
+    import torch
+    from smaq_b200 import ops
+    for B, Hkv, G, fast in ((3, 2, 4, True), (1, 8, 8, True), (3, 2, 4, True), (2, 2, 8, False),
+                            (3, 2, 4, False), (1, 8, 8, True)):
+        q, kw = _case(cuda, fast, B=B, Hkv=Hkv, G=G)
+        ref = ops.decode(q, **kw).float().cpu().numpy()
+        got = ops.decode(q, entry="smaq_decode_noalloc", **kw)
+        torch.cuda.synchronize()
+        ops.decode_status(B, Hkv)          # the no-allocation scratch's error word
+        assert O.rel_l2(got.float().cpu().numpy(), ref) <= 2e-3, (B, Hkv, G, fast)
