@@ -119,14 +119,14 @@ class SMAQBlockVQ(nn.Module):
         if kmeans not in ("auto", "device", "reference"):
             raise ValueError(f"kmeans must be auto, device or reference, not {kmeans!r}")
         N = calibration_keys.shape[0]
-        Es, Eis, shaped = [], [], []
+        bd = self.block_dim
+        sig = []
         for b in range(self.n_blocks):
-            sl = slice(b * self.block_dim, (b + 1) * self.block_dim)
-            qb = calibration_queries[:, sl].float()
-            E, E_inv = build_smaq_metric((qb.T @ qb) / N, c=self.c)
-            shaped.append(calibration_keys[:, sl].float() @ E.T)
-            Es.append(E)
-            Eis.append(E_inv)
+            qb = calibration_queries[:, b * bd:(b + 1) * bd].float()
+            sig.append((qb.T @ qb) / N)
+        E_all, Ei_all = build_smaq_metric(torch.stack(sig), c=self.c)   # one batched eigh
+        Es, Eis = list(E_all), list(Ei_all)
+        shaped = [calibration_keys[:, b * bd:(b + 1) * bd].float() @ Es[b].T for b in range(self.n_blocks)]
         on_device = kmeans == "device" or (kmeans == "auto" and calibration_keys.is_cuda)
         if on_device and N >= self.n_centroids:
             cs = list(ops.kmeans(torch.stack(shaped), self.n_centroids, kmeans_iters, seed))
