@@ -68,7 +68,7 @@ def parse(argv=None):
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="smaq_b200", choices=["smaq_b200", "reference"])
-    ap.add_argument("--workload", default="longctx", choices=["longctx", "decode", "append", "paged"])
+    ap.add_argument("--workload", default="longctx", choices=["longctx", "decode", "append", "paged", "scores"])
     ap.add_argument("--layers", type=int, default=0, help="build fewer layers (profiling runs only; 0: the config's)")
     ap.add_argument("--no-cfg1", action="store_true", help="longctx at N=1: skip the configs[1] sub-measurement")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -981,6 +981,122 @@ def run_paged(a, rank: int, world: int):
 
 
 # ----------------------------------------------------------------------------- main
+
+# ----------------------------------------------------------------------------- standalone scores / attend
+SC_H, SC_G, SC_N, SC_BITS = 8, 8, 131072, 4
+
+
+def scores_config():
+    return {"workload": "hf_cache_scores_attend", "n_kv_heads": SC_H, "queries_per_kv_head": SC_G,
+            "history_tokens": SC_N, "head_dim": 128, "keys": f"scalar {SC_BITS}-bit", "values": "2-bit g32",
+            "query": "fp32 (scores out fp32, the reference's Triton output type)", "weights": "fp32",
+            "l2": "inputs larger than L2 (no flush)"}
+
+
+def scores_inputs(dev):
+    """HF-style cache history of SC_H kv heads x SC_N tokens, with SC_G query rows per head."""
+    import torch
+    from smaq_b200 import synthetic as syn
+    from smaq_b200.kv_cache import quantize_values
+    from smaq_b200.quantizer import SMAQQuantizer
+    D = 128
+    quant = SMAQQuantizer(D, bits=SC_BITS, device=dev)
+    quant.fit(torch.from_numpy(syn.calibration_queries(512, D)).to(dev))
+    U_np, outl = syn.basis(D)
+    U = torch.from_numpy(U_np.astype(np.float32)).to(dev)
+    lam = torch.from_numpy(np.sqrt(syn.spectrum(D)).astype(np.float32)).to(dev)
+    gen = torch.Generator(device=dev).manual_seed(7)
+    k = spectral_keys_gpu(SC_H * SC_N, gen, U, lam, torch.from_numpy(outl).to(dev), torch.bfloat16)
+    kq = quant.quantize(k.reshape(SC_H, SC_N, D))
+    v = torch.randn((SC_H, SC_N, D), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    vq = quantize_values(v)
+    q = torch.randn((SC_H, SC_G, D), generator=gen, device=dev, dtype=torch.float32)
+    return quant, kq, vq, q
+
+
+def run_scores(a, rank: int):
+    """One step: scores of every kv head's query rows against its compressed keys
+    (smaq_key_scores), a torch softmax, and the weighted value sum (smaq_attend_values).  The
+    reference's own GPU scoring kernel (its Triton fast path, smaq/triton_kernels.py:139-187,
+    one call per kv head) is timed beside it on the same inputs."""
+    import torch
+    from smaq_b200 import build, ops
+    build.build()
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    quant, kq, vq, q = scores_inputs(dev)
+    scale = 128 ** -0.5
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+
+    def step():
+        s = quant.attention_score(q, kq, scale=scale)
+        w = torch.softmax(s, dim=-1)
+        return ops.attend_values(w, vq.data, vq.scales, vq.zeros)
+
+    for _ in range(max(3, a.warmup)):
+        step()
+    torch.cuda.synchronize()
+    ts, ta = [], []
+    for _ in range(a.steps):
+        ev[0].record()
+        s = quant.attention_score(q, kq, scale=scale)
+        ev[1].record()
+        w = torch.softmax(s, dim=-1)
+        ev[2].record()
+        ops.attend_values(w, vq.data, vq.scales, vq.zeros)
+        ev[3].record()
+        torch.cuda.synchronize()
+        ts.append(ev[0].elapsed_time(ev[1]))
+        ta.append(ev[2].elapsed_time(ev[3]))
+    t_step = statistics.median([x + y for x, y in zip(ts, ta)]) * 1e-3
+    t_s, t_a = statistics.median(ts) * 1e-3, statistics.median(ta) * 1e-3
+    rows = SC_H * SC_N
+    b_scores = rows * (64 + 2 + SC_G * 4)           # codes + norm in, fp32 scores out
+    b_attend = rows * (SC_G * 4 + 32 + 8 + 8)       # weights + value codes + scales + zeros in
+    peak, src = peak_hbm()
+    ref_gpu = None
+    smaq = import_reference()
+    if smaq is not None:
+        try:
+            from smaq.triton_kernels import _triton_attention_scores
+            from smaq.quantizer import SMAQQuantized, SMAQQuantizer as RefQ
+            rq = RefQ(128, bits=SC_BITS, device=dev)
+            rq.E.copy_(quant.E)
+            rq.E_inv.copy_(quant.E_inv)
+            per = [(q[h], SMAQQuantized(indices=kq.indices[h], norms=kq.norms[h], bits=SC_BITS)) for h in range(SC_H)]
+            for _ in range(3):
+                for qh, kh in per:
+                    _triton_attention_scores(rq, qh, kh)
+            torch.cuda.synchronize()
+            tr = []
+            for _ in range(a.steps):
+                ev[4].record()
+                for qh, kh in per:
+                    _triton_attention_scores(rq, qh, kh)
+                ev[5].record()
+                torch.cuda.synchronize()
+                tr.append(ev[4].elapsed_time(ev[5]) * 1e-3)
+            t_r = statistics.median(tr)
+            ref_gpu = {"kernel": "reference _smaq_scores_kernel (Triton, baseline/_ref), one call per kv head",
+                       "ms": t_r * 1e3, "gbs": b_scores / t_r / 1e9, "speedup_of_smaq_key_scores": t_r / t_s}
+        except Exception as exc:  # the reference's GPU kernel is informational here
+            ref_gpu = {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
+    line = {"metric": "standalone compressed-history scores + attend GB/s", "value": (b_scores + b_attend) / t_step / 1e9,
+            "unit": "GB/s", "n_gpus": 1, "steps": a.steps, "warmup": max(3, a.warmup), "ms_per_step": t_step * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32-query/bf16-rows",
+            "data": "synthetic", "config": scores_config(),
+            "kernels": {"smaq_key_scores": {"us": t_s * 1e6, "gbs": b_scores / t_s / 1e9,
+                                            "frac": b_scores / t_s / 1e9 / peak},
+                        "smaq_attend_values": {"us": t_a * 1e6, "gbs": b_attend / t_a / 1e9,
+                                               "frac": b_attend / t_a / 1e9 / peak}},
+            "roofline": {"bound": "hbm", "achieved": (b_scores + b_attend) / t_step / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": (b_scores + b_attend) / t_step / 1e9 / peak, "traffic": None, "peak_source": src,
+                         "algorithmic_bytes_per_step": b_scores + b_attend},
+            "reference_gpu": ref_gpu, "gpu_launches": 3 * a.steps}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     a = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -1001,6 +1117,13 @@ def main():
                                           "d2h_bytes_per_step": 0}}), flush=True)
         else:
             run_paged(a, rank, world)
+        return
+    if a.workload == "scores":
+        if a.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the scores workload times the reference's GPU "
+                              "scoring kernel inside the smaq_b200 line (reference_gpu)"}), flush=True)
+        else:
+            run_scores(a, rank)
         return
     if a.impl == "reference":
         run_reference(a, rank, world)

@@ -286,6 +286,7 @@ typedef struct smaq_scores_args {
   void* out;
   int out_dtype;
   int64_t out_stride_g, out_stride_q;  /* element (g, q, t) at out + g*.. + q*.. + t */
+  int q_rotated;                   /* scalar: nonzero when q already holds q @ E_inv^T (E_inv unused) */
 } smaq_scores_args;
 int smaq_key_scores(const smaq_scores_args* args, void* stream);
 

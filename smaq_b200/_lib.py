@@ -69,7 +69,7 @@ class ScoresArgs(C.Structure):
         ("norms_stride_g", i64), ("key_bits", i32), ("E_inv", vp), ("centroids", vp),
         ("key_idx", vp), ("idx_is_int64", i32), ("idx_stride_g", i64), ("block_dim", i32),
         ("n_centroids", i32), ("decoded_centroids", vp), ("scale", C.c_float),
-        ("out", vp), ("out_dtype", i32), ("out_stride_g", i64), ("out_stride_q", i64),
+        ("out", vp), ("out_dtype", i32), ("out_stride_g", i64), ("out_stride_q", i64), ("q_rotated", i32),
     ]
 
 

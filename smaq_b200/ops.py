@@ -213,6 +213,11 @@ def key_scores(query: torch.Tensor, *, key_format: int, scale: Optional[float] =
     a.scale = float(1.0 if scale is None else scale)
     keep = [q]
     if key_format == SMAQ_KEYS_SCALAR:
+        # rotate the few query rows once (a small fp32 GEMM) instead of in every CTA
+        qr = torch.matmul(q.float(), E_inv.to(q.device, torch.float32).T).contiguous()
+        keep.append(qr)
+        a.q, a.q_dtype, a.q_stride_g, a.q_stride_q = qr.data_ptr(), SMAQ_F32, qr.stride(0), qr.stride(1)
+        a.q_rotated = 1
         codes, norms = _groups(lead, key_codes, key_norms, tail=(2, 1))
         codes, norms = _packed_rows(codes), (norms if norms.stride(-1) == 1 else norms.contiguous())
         Ei = E_inv.to(torch.float32).contiguous()
