@@ -353,7 +353,7 @@ __global__ void __launch_bounds__(SQ_WARPS * 32) scalar_key_kernel(
 // in shared memory.  Distances follow torch.cdist's matmul expansion
 //   d2 = |x|^2 + |c|^2 - 2 x.c,  dist = sqrt(clamp(d2, 0)),  argmin (first index on ties).
 // =====================================================================================
-constexpr int BQ_WARPS = 8;
+constexpr int BQ_WARPS = 16;
 constexpr int BQ_ROWS = 4;
 
 template <class DT, int EPL>
@@ -451,7 +451,10 @@ __global__ void __launch_bounds__(BQ_WARPS * 32) bvq_key_kernel(
           float dot = 0.f;
 #pragma unroll
           for (int j = 0; j < BD; ++j) dot = fmaf(-2.0f * xs[rr][j], cv[j], dot);
-          const float d = sqrtf(fmaxf(dot + xn[rr] + cn, 0.0f));
+          // squared distance, clamped at 0 as cdist does; its square root is monotone, so the
+          // argmin is the same except where two squared distances one ulp apart share a square
+          // root (a near-tie, resolved by the lower index in cdist)
+          const float d = fmaxf(dot + xn[rr] + cn, 0.0f);
           if (d < best[rr]) {
             best[rr] = d;
             bi[rr] = c;
