@@ -68,7 +68,7 @@ def parse(argv=None):
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="smaq_b200", choices=["smaq_b200", "reference"])
-    ap.add_argument("--workload", default="longctx", choices=["longctx", "decode", "append", "paged", "scores"])
+    ap.add_argument("--workload", default="longctx", choices=["longctx", "decode", "append", "append_bvq", "paged", "scores"])
     ap.add_argument("--layers", type=int, default=0, help="build fewer layers (profiling runs only; 0: the config's)")
     ap.add_argument("--no-cfg1", action="store_true", help="longctx at N=1: skip the configs[1] sub-measurement")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -982,6 +982,102 @@ def run_paged(a, rank: int, world: int):
 
 # ----------------------------------------------------------------------------- main
 
+# ----------------------------------------------------------------------------- block-VQ append
+def run_append_bvq(a, rank: int):
+    """configs[2]'s append batch with block-VQ keys (the configs[1]/[4] key format: 8-dim blocks,
+    256-entry codebook) and 2-bit values: SMAQBlockVQ.quantize (smaq/block_vq.py:216-244) plus
+    quantize_values through one smaq_append per step."""
+    import torch
+    from smaq_b200 import build, ops
+    from smaq_b200._lib import SMAQ_KEYS_BVQ, SMAQ_LAYOUT_DECODE
+    build.build()
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    vq = make_codebook(dev)
+    k, v, _, o = append_inputs(dev, rank)
+    rows = k.shape[0] * k.shape[1]
+    codes = torch.empty((rows, AP_D // 8), dtype=torch.uint8, device=dev)
+
+    def step(keys=True, values=True):
+        ops.append(k if keys else None, v if values else None, n_heads=AP_H, page_size=AP_T, key_format=SMAQ_KEYS_BVQ,
+                   E_blocks=vq.E_blocks, centroids=vq.centroids, key_codes=codes, v_data=o["vd"], v_scales=o["vs"],
+                   v_zeros=o["vz"], layout=SMAQ_LAYOUT_DECODE)
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn):
+        for _ in range(max(3, a.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(a.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / a.steps
+
+    clocks = Clocks(dev.index or 0)
+    clocks.start()
+    time.sleep(0.3)
+    ms = timed(step)
+    ck = clocks.stop()
+    key_ms = timed(lambda: step(values=False))
+    k_in = v_in = rows * AP_D * 2
+    k_out = rows * (AP_D // 8)
+    v_out = rows * (AP_D // 4 + 2 * 2 * (AP_D // 32))
+    total = k_in + v_in + k_out + v_out
+    peak, src = peak_hbm()
+    flops = rows * (AP_D // 8) * 256 * 8 * 2          # shaped-key . centroid for every code of every block
+    line = {"metric": "compressed-KV append GB/s (in+out), block-VQ keys", "value": total / (ms * 1e-3) / 1e9,
+            "unit": "GB/s", "n_gpus": 1, "steps": a.steps, "warmup": max(3, a.warmup), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16-io/f32-distances",
+            "data": "synthetic",
+            "config": {"workload": "append_bvq", "batch": AP_B, "new_tokens": AP_T, "n_kv_heads": AP_H,
+                       "head_dim": AP_D, "keys": "block-VQ 8x256", "values": "2-bit g32",
+                       "l2": "inputs larger than L2 (no flush)"},
+            "roofline": {"bound": "issue (mma.sync scores + argmin epilogue)",
+                         "achieved": (k_in + k_out) / (key_ms * 1e-3) / 1e9,
+                         "peak": peak, "unit": "GB/s", "frac": (k_in + k_out) / (key_ms * 1e-3) / 1e9 / peak,
+                         "traffic": None, "peak_source": src,
+                         "kernel": "bvq_mma_kernel (m16n8k8 bf16, codebook in three bf16 terms)",
+                         "key_kernel_us": key_ms * 1e3, "distance_tflops": flops / (key_ms * 1e-3) / 1e12,
+                         "tensor_tflops_bf16": 3 * flops / (key_ms * 1e-3) / 1e12},
+            "gpu_launches": 2 * a.steps, "clocks": ck}
+    if not a.no_cpu_baseline:
+        line["cpu_baseline"] = append_bvq_cpu_sample(vq)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def append_bvq_cpu_sample(vq, seconds_cap: float = 20.0, max_runs: int = 3):
+    """The reference's CompressedKVStore.append_chunk with SMAQBlockVQStrategy on the host CPU,
+    all threads, 1024 tokens x 8 heads, scaled to the batch."""
+    import torch
+    from smaq_b200 import synthetic as syn
+    torch.set_num_threads(os.cpu_count() or 1)
+    tokens = 1024
+    k = torch.from_numpy(syn.keys((tokens, AP_H), AP_D, seed=31)).to(torch.bfloat16)
+    v = torch.from_numpy(syn.values((tokens, AP_H), AP_D, seed=32)).to(torch.bfloat16)
+    smaq = import_reference()
+    if smaq is None:
+        return {"value": None, "unit": "GB/s", "cores": 0, "kind": "reference", "sample": "reference not installed"}
+    from smaq.store import CompressedKVStore
+    from smaq.strategies import SMAQBlockVQStrategy
+    cpu = torch.device("cpu")
+    strat = SMAQBlockVQStrategy(AP_D, device=cpu)
+    q = strat.quantizer
+    for name in ("E_blocks", "E_inv_blocks", "centroids", "decoded_centroids"):
+        setattr(q, name, getattr(vq, name).detach().to(cpu))
+    store = CompressedKVStore(AP_D, AP_H, device=cpu, key_strategy=strat)
+    t, n = _timed_runs(lambda: store.append_chunk(k, v), seconds_cap, max_runs)
+    rows = tokens * AP_H
+    per_row = AP_D * 2 * 2 + AP_D // 8 + AP_D // 4 + 2 * 2 * (AP_D // 32)
+    scale = AP_B * AP_T * AP_H / rows
+    return {"value": rows * per_row / t / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "reference",
+            "sample": f"reference CompressedKVStore.append_chunk with SMAQBlockVQStrategy (baseline/_ref), {tokens} "
+                      f"tokens x {AP_H} heads, median of {n} runs = {t * 1e3:.1f} ms (rate; x{scale:.0f} for the batch)"}
+
+
 # ----------------------------------------------------------------------------- standalone scores / attend
 SC_H, SC_G, SC_N, SC_BITS = 8, 8, 131072, 4
 
@@ -1117,6 +1213,14 @@ def main():
                                           "d2h_bytes_per_step": 0}}), flush=True)
         else:
             run_paged(a, rank, world)
+        return
+    if a.workload == "append_bvq":
+        if a.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the block-VQ append line carries the reference's "
+                                  "CPU rate as cpu_baseline"}), flush=True)
+        else:
+            run_append_bvq(a, rank)
         return
     if a.workload == "scores":
         if a.impl == "reference":

@@ -603,6 +603,175 @@ static int launch_scalar_d(const smaq_append_args& a, cudaStream_t s) {
   return fail(SMAQ_ERR_UNSUPPORTED, "scalar keys: head_dim %d not in {64,128}", a.head_dim);
 }
 
+// ---------------------------------------------------------------------------------------
+// Block-VQ encode on the tensor cores (bf16 keys, D = 128, 8-dim blocks, <= 256 codes).
+// argmin_c |k_b E_b^T - c|^2 = argmin_c (|c|^2 - 2 k_b . c'), c' = c E_b, so each block is a
+// [rows x 8] x [8 x 256] product: mma.m16n8k8 with A = the raw bf16 key (exact) and B = c'
+// split into three bf16 terms (hi + mid + lo hold c' to ~2^-24), fp32 accumulation.  Thread
+// (gid, tig) holds rows gid, gid + 8 and codes 8n + 2tig, +1 of every n-tile; the running
+// minimum per row is merged over the 4 tig lanes at the end of the block, ties to the lower
+// code (cdist + argmin's first index; a difference against the reference can only be a
+// near-tie, as |x|^2 is left out and the sum order differs).
+constexpr int BM_WARPS = 16;
+constexpr int BM_NT = 32;                         // n-tiles of 8 codes
+constexpr int BM_BBYTES = 16 * BM_NT * 3 * 32 * 4;  // B fragments [blk][nt][split][lane]
+constexpr int BM_SMEM = BM_BBYTES + 16 * 256 * 4;   // + |c|^2 [blk][code]
+
+__device__ __forceinline__ uint32_t bm_pack_bf16(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ void bm_mma(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm("mma.sync.aligned.m16n8k8.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(b0));
+}
+
+__global__ void __launch_bounds__(BM_WARPS * 32, 1) bvq_mma_kernel(
+    const __nv_bfloat16* __restrict__ k, int64_t n_tokens, int n_heads, int64_t st, int64_t sh, const RowMap rm,
+    const float* __restrict__ Eb, const float* __restrict__ cent, int nc, uint8_t* __restrict__ out, int layout) {
+  extern __shared__ __align__(16) uint8_t bm_smem[];
+  uint32_t* Bf = reinterpret_cast<uint32_t*>(bm_smem);                  // [16][32][3][32]
+  float* CN = reinterpret_cast<float*>(bm_smem + BM_BBYTES);             // [16][256]
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int gid = lane >> 2, tig = lane & 3;
+  // c' = c E_b per (block, code): fragment (nt, lane) holds c'[8nt + gid][2tig, 2tig+1]
+  for (int i = threadIdx.x; i < 16 * BM_NT * 32; i += blockDim.x) {
+    const int blk = i / (BM_NT * 32), r = i - blk * BM_NT * 32, nt = r >> 5, l = r & 31;
+    const int code = 8 * nt + (l >> 2), d0 = 2 * (l & 3);
+    float v[2] = {0.f, 0.f};
+    if (code < nc) {
+      const float* c = cent + (int64_t(blk) * nc + code) * 8;
+      const float* E = Eb + blk * 64;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc = fmaf(c[j], E[j * 8 + d0 + e], acc);
+        v[e] = acc;
+      }
+    }
+    uint32_t* dst = Bf + ((blk * BM_NT + nt) * 3) * 32 + l;
+#pragma unroll
+    for (int sp = 0; sp < 3; ++sp) {
+      const uint32_t h = bm_pack_bf16(v[0], v[1]);
+      dst[sp * 32] = h;
+      v[0] -= __uint_as_float(h << 16);
+      v[1] -= __uint_as_float(h & 0xffff0000u);
+    }
+  }
+  for (int i = threadIdx.x; i < 16 * 256; i += blockDim.x) {
+    const int blk = i >> 8, code = i & 255;
+    float sq = INFINITY;  // codes past nc never win
+    if (code < nc) {
+      const float* c = cent + (int64_t(blk) * nc + code) * 8;
+      sq = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sq = fmaf(c[j], c[j], sq);
+    }
+    CN[i] = sq;
+  }
+  __syncthreads();
+  const int64_t n_rows = n_tokens * n_heads;
+  const int64_t n_tiles = (n_rows + 15) / 16;
+  for (int64_t tile = int64_t(blockIdx.x) * BM_WARPS + wid; tile < n_tiles; tile += int64_t(gridDim.x) * BM_WARPS) {
+    const int64_t r0 = tile * 16 + gid, r1 = r0 + 8;
+    // A fragments of all 16 blocks for rows r0, r1 (dims 8 blk + 2 tig, +1)
+    uint32_t a0[16], a1[16];
+    {
+      int64_t t;
+      int h;
+      const uint32_t* p0 = nullptr;
+      const uint32_t* p1 = nullptr;
+      if (r0 < n_rows) { rm.token_head(r0, t, h); p0 = reinterpret_cast<const uint32_t*>(k + t * st + h * sh); }
+      if (r1 < n_rows) { rm.token_head(r1, t, h); p1 = reinterpret_cast<const uint32_t*>(k + t * st + h * sh); }
+#pragma unroll
+      for (int b = 0; b < 16; ++b) {
+        a0[b] = p0 ? __ldg(p0 + 4 * b + tig) : 0u;
+        a1[b] = p1 ? __ldg(p1 + 4 * b + tig) : 0u;
+      }
+    }
+    uint32_t best_idx0[4] = {0u, 0u, 0u, 0u}, best_idx1[4] = {0u, 0u, 0u, 0u};  // 4 blocks per word
+#pragma unroll 1
+    for (int b = 0; b < 16; ++b) {
+      float v0 = INFINITY, v1 = INFINITY;
+      int i0 = 0, i1 = 0;
+      const uint32_t* bb = Bf + (b * BM_NT * 3) * 32 + lane;
+      const float* cn = CN + b * 256 + 2 * tig;
+#pragma unroll 4
+      for (int nt = 0; nt < BM_NT; ++nt) {
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        bm_mma(d, a0[b], a1[b], bb[(nt * 3 + 2) * 32]);  // smallest term first
+        bm_mma(d, a0[b], a1[b], bb[(nt * 3 + 1) * 32]);
+        bm_mma(d, a0[b], a1[b], bb[(nt * 3 + 0) * 32]);
+        const float2 c2 = *reinterpret_cast<const float2*>(cn + 8 * nt);
+        const int code = 8 * nt + 2 * tig;
+        const float s0 = fmaf(-2.f, d[0], c2.x), s1 = fmaf(-2.f, d[1], c2.y);
+        const float s2 = fmaf(-2.f, d[2], c2.x), s3 = fmaf(-2.f, d[3], c2.y);
+        if (s0 < v0) { v0 = s0; i0 = code; }
+        if (s1 < v0) { v0 = s1; i0 = code + 1; }
+        if (s2 < v1) { v1 = s2; i1 = code; }
+        if (s3 < v1) { v1 = s3; i1 = code + 1; }
+      }
+#pragma unroll
+      for (int o = 1; o <= 2; o <<= 1) {
+        const float ov0 = __shfl_xor_sync(0xffffffffu, v0, o), ov1 = __shfl_xor_sync(0xffffffffu, v1, o);
+        const int oi0 = __shfl_xor_sync(0xffffffffu, i0, o), oi1 = __shfl_xor_sync(0xffffffffu, i1, o);
+        if (ov0 < v0 || (ov0 == v0 && oi0 < i0)) { v0 = ov0; i0 = oi0; }
+        if (ov1 < v1 || (ov1 == v1 && oi1 < i1)) { v1 = ov1; i1 = oi1; }
+      }
+      best_idx0[b >> 2] |= uint32_t(i0) << (8 * (b & 3));
+      best_idx1[b >> 2] |= uint32_t(i1) << (8 * (b & 3));
+    }
+    if (tig == 0) {
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        const int64_t r = rr ? r1 : r0;
+        if (r >= n_rows) continue;
+        const uint32_t* bi = rr ? best_idx1 : best_idx0;
+        int64_t t;
+        int h;
+        rm.token_head(r, t, h);
+        uint8_t* row = out + rm.row(t, h) * 16;
+        uint32_t w[4];
+        if (layout == SMAQ_LAYOUT_DECODE) {  // block b at byte 2 (4 (b / 8) + b % 4) + (b / 4) % 2
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            // bytes 4q..4q+3 hold blocks {2q', ...}: byte p <- block sigma^-1(p)
+            uint32_t v = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int p = 4 * q + e;
+              const int hi8 = p >> 3, rem = p & 7, lo4 = rem >> 1, par = rem & 1;
+              const int blk = 8 * hi8 + 4 * par + lo4;
+              v |= ((bi[blk >> 2] >> (8 * (blk & 3))) & 0xffu) << (8 * e);
+            }
+            w[q] = v;
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) w[q] = bi[q];
+        }
+        *reinterpret_cast<uint4*>(row) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+}
+
+static int launch_bvq_mma(const smaq_append_args& a, cudaStream_t s) {
+  cudaError_t e = cudaFuncSetAttribute(bvq_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BM_SMEM);
+  if (e != cudaSuccess) return cuda_status(e, "bvq_mma_kernel attr");
+  const int64_t rows = a.n_tokens * a.n_heads;
+  const int64_t tiles = (rows + 15) / 16;
+  const int64_t want = (tiles + BM_WARPS - 1) / BM_WARPS;
+  const int grid = int(want < num_sms() ? want : num_sms());
+  bvq_mma_kernel<<<grid, BM_WARPS * 32, BM_SMEM, s>>>(static_cast<const __nv_bfloat16*>(a.k), a.n_tokens, a.n_heads,
+                                                      a.k_stride_t, a.k_stride_h, make_rowmap(a), a.E_blocks,
+                                                      a.centroids, a.n_centroids, a.key_codes, a.layout);
+  return cuda_status(cudaGetLastError(), "bvq_mma_kernel");
+}
+
 template <class DT, int EPL>
 static int launch_bvq_t(const smaq_append_args& a, cudaStream_t s) {
   constexpr int D = 32 * EPL;
@@ -623,6 +792,10 @@ static int launch_bvq_t(const smaq_append_args& a, cudaStream_t s) {
 
 template <class DT>
 static int launch_bvq_d(const smaq_append_args& a, cudaStream_t s) {
+  // bf16 keys of D = 128 with 16-byte aligned rows: the tensor-core encode
+  if (DT::code == SMAQ_BF16 && a.head_dim == 128 && a.n_centroids <= 256 &&
+      ((reinterpret_cast<uintptr_t>(a.k) | uintptr_t(a.k_stride_t * 2) | uintptr_t(a.k_stride_h * 2)) & 15) == 0)
+    return launch_bvq_mma(a, s);
   switch (a.head_dim) {
     case 64: return launch_bvq_t<DT, 2>(a, s);
     case 128: return launch_bvq_t<DT, 4>(a, s);
