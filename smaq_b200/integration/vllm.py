@@ -140,11 +140,18 @@ class LayerState:
     def buffered_tokens(self) -> int:
         return self.engine.ring.size if self.engine is not None else 0
 
-    def _ensure_cache(self, kv_cache: torch.Tensor) -> PagedCompressedCache:
+    def _ensure_cache(self, kv_cache: torch.Tensor) -> Optional[PagedCompressedCache]:
         if self.cache is None:
             cfg = self.config
             if kv_cache is None or kv_cache.dim() != 5:
                 raise ValueError("SMAQ paged mode needs vLLM's [2, num_blocks, block_size, Hkv, D] KV cache")
+            if kv_cache.element_size() == 1:
+                # quantized (fp8) vLLM caches: the exact window would be fp8; leave the layer to vLLM
+                if not getattr(self, "_unsupported_logged", False):
+                    logger.warning("[SMAQ] layer %d: KV cache dtype %s not served (8-bit caches are left to vLLM)", cfg.layer_idx,
+                                   kv_cache.dtype)
+                    self._unsupported_logged = True
+                return None
             self.cache = PagedCompressedCache(kv_cache.shape[1], kv_cache.shape[2], cfg.num_kv_heads, cfg.head_dim,
                                               key_bits=cfg.key_bits, value_bits=cfg.value_bits,
                                               group_size=cfg.value_group_size, capacity=cfg.ring_capacity,
@@ -168,7 +175,10 @@ class LayerState:
             else:
                 self.engine.ingest_prefill(k, v, n)
         else:
-            self._ensure_cache(kv_cache).write(key, value, slot_mapping)
+            cache = self._ensure_cache(kv_cache)
+            if cache is None:
+                return
+            cache.write(key, value, slot_mapping)
         self.tokens_written += n
 
     def on_forward(self, impl, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,

@@ -381,3 +381,15 @@ def test_backend_registers_as_custom():
     finally:
         AttentionBackendEnum.CUSTOM.clear_override()
         iv.set_mode(iv.MODE_CAPTURE_ONLY)
+
+
+def test_fp8_cache_is_left_to_vllm(monkeypatch):
+    rec = Recorder(monkeypatch)
+    r = FakeRunner(n_layers=1, num_blocks=32, dtype=torch.float8_e4m3fn)
+    iv.install_hooks(r, mode=iv.MODE_HYBRID, ring_capacity=16, initial_layers_count=0)
+    attn = r.compilation_config.static_forward_context["layer.0"]
+    im, kv = attn.impl, attn.kv_cache[0]
+    bt = Batch([40], n_decode=2, num_blocks=32, seed=6)
+    bt.prefill(im, kv)
+    _, out, _ = bt.decode(im, kv)
+    assert torch.all(out == 7.0) and rec.appends == [] and rec.decodes == []
