@@ -140,6 +140,24 @@ __device__ __forceinline__ uint32_t sw128_chunk(int r, int c) {
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
+// Packed fp32 pairs (one instruction for two independent IEEE operations, same rounding as two
+// scalar ones).
+__device__ __forceinline__ uint64_t f32x2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 f32x2_split(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 // k_unit elements are bf16(fp32 x / den) with x and den bf16.  They are computed as
 // x * (1/den), within 2^-22 relative of the exact quotient.  A quotient of two bf16 values is
 // never exactly a bf16 rounding midpoint (X * 2^p = m * Dn has no solution with X, Dn 8-bit
@@ -178,9 +196,8 @@ __device__ __forceinline__ float fma_sat(float a, float b, float c) {
 // k = 0 and -inf for k = G).  Entry k holds base = #{b <= window start - step/4} and the single
 // boundary t in the window widened by step/4 on each side (+inf if none; the widened window is
 // 2.5 steps < gap_min long), so code(x) = #{b < x} = base + (x > t).  NaN gives k = 0, whose
-// entry is (NB, +inf): NaN sorts after every boundary, as searchsorted places it.  The t values
-// and the bases sit in separate 4-byte tables, so a warp's lookups of up to 32 distinct cells
-// hit distinct banks.
+// entry is (NB, +inf): NaN sorts after every boundary, as searchsorted places it.  An entry is
+// the 8-byte pair (t bits, base), read by one shared load.
 struct SearchGrid {
   float neg_inv_span, c0, g, step, hi;
   int G;
@@ -210,7 +227,7 @@ __device__ __forceinline__ SearchGrid search_grid(const float* __restrict__ bnd,
 }
 template <int NB>
 __device__ __forceinline__ void search_entry(const float* __restrict__ bnd, float sc, const SearchGrid& sg, int k,
-                                             float* lut_t, uint32_t* lut_b) {
+                                             uint2* lut) {
   const float eps = 0.25f * sg.step;
   const float lo_w = sg.hi - float(k + 1) * sg.step - eps, hi_w = sg.hi - float(k - 1) * sg.step + eps;
   uint32_t base = 0;
@@ -221,20 +238,26 @@ __device__ __forceinline__ void search_entry(const float* __restrict__ bnd, floa
     if (b <= lo_w) ++base;
     else if (b <= hi_w || k == 0) t = b;
   }
-  lut_t[k] = t;
-  lut_b[k] = base;
+  lut[k] = make_uint2(__float_as_uint(t), base);
 }
-__device__ __forceinline__ uint32_t search_lut(float x, const SearchGrid& sg, const float* lut_t, const uint32_t* lut_b) {
+// Shared address of entry k is lut + 8k.  f = 2^23 + k exactly (k in [0, G]), whose bits are
+// 0x4B000000 + k, so the address is lut_adj + 8 * bits(f) in 32-bit arithmetic with
+// lut_adj = lut - 8 * 0x4B000000 (mod 2^32): the subtraction of the exponent bits folds into
+// the table base.
+__device__ __forceinline__ uint32_t lut_base_adj(const uint2* lut) { return smem_u32(lut) - (0x4B000000u << 3); }
+__device__ __forceinline__ uint32_t search_lut(float x, const SearchGrid& sg, uint32_t lut_adj) {
   const float f = fmaf(fma_sat(x, sg.neg_inv_span, sg.c0), sg.g, 8388608.0f);
-  const uint32_t k = __float_as_uint(f) - 0x4B000000u;
-  return lut_b[k] - gt_mask(x, lut_t[k]);
+  const uint32_t addr = lut_adj + (__float_as_uint(f) << 3);
+  uint32_t t, b;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(t), "=r"(b) : "r"(addr));
+  return b - gt_mask(x, __uint_as_float(t));
 }
 
 // Codes of 32 consecutive coordinates, packed LSB-first (2-bit: 4 per byte, 3/4-bit: 2 per
 // byte) into 32 * BITS' / 8 bytes, BITS' = 2 or 4.
 template <int BITS, bool LUT>
-__device__ __forceinline__ void encode32(const float (&y)[32], uint32_t* w, const SearchGrid& sg, const float* lut_t,
-                                         const uint32_t* lut_b, const float* __restrict__ bnd, float sc) {
+__device__ __forceinline__ void encode32(const float (&y)[32], uint32_t* w, const SearchGrid& sg, uint32_t lut_adj,
+                                         const float* __restrict__ bnd, float sc) {
   constexpr int NB = (1 << BITS) - 1;
   constexpr int VPB = BITS == 2 ? 4 : 2;
 #pragma unroll
@@ -245,7 +268,7 @@ __device__ __forceinline__ void encode32(const float (&y)[32], uint32_t* w, cons
       const float x = y[4 * VPB * k + u];
       uint32_t c;
       if constexpr (LUT) {
-        c = search_lut(x, sg, lut_t, lut_b);
+        c = search_lut(x, sg, lut_adj);
       } else {  // degenerate boundaries: count them (>u puts NaN after every boundary)
         c = 0;
 #pragma unroll
@@ -271,9 +294,8 @@ __global__ void __launch_bounds__(TR_THREADS, 1) tc_scalar_key_kernel(
   uint8_t* Bs = smem;                                          // [2 splits][2 atoms][128 rows][128 B]
   uint8_t* Rs = smem + TR_B_BYTES;                             // [STAGES][2 atoms][128 rows][128 B]
   float* xch = reinterpret_cast<float*>(Rs + TR_STAGES * TR_TILE);  // [2][128 rows][2 halves][8]
-  float* lut_t = xch + TR_XCH_BYTES / 4;                       // [TR_LUT]
-  uint32_t* lut_b = reinterpret_cast<uint32_t*>(lut_t + TR_LUT);  // [TR_LUT]
-  TrBars* bars = reinterpret_cast<TrBars*>(lut_b + TR_LUT);
+  uint2* lut = reinterpret_cast<uint2*>(xch + TR_XCH_BYTES / 4);  // [TR_LUT] (t bits, base)
+  TrBars* bars = reinterpret_cast<TrBars*>(lut + TR_LUT);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n_rows = n_tokens * n_heads;
   const int tok_per_tile = TR_ROWS / n_heads;
@@ -307,7 +329,7 @@ __global__ void __launch_bounds__(TR_THREADS, 1) tc_scalar_key_kernel(
   }
   const SearchGrid sgrid = search_grid<NB>(bnd, sc);
   if (sgrid.ok)
-    for (int k = threadIdx.x; k <= sgrid.G; k += blockDim.x) search_entry<NB>(bnd, sc, sgrid, k, lut_t, lut_b);
+    for (int k = threadIdx.x; k <= sgrid.G; k += blockDim.x) search_entry<NB>(bnd, sc, sgrid, k, lut);
   fence_async_smem();
   if (threadIdx.x == 0) {
     for (int s = 0; s < TR_STAGES; ++s) {
@@ -409,11 +431,15 @@ __global__ void __launch_bounds__(TR_THREADS, 1) tc_scalar_key_kernel(
       // k_unit in bf16 (the reference's storage type); column j of the A buffer holds elements
       // 2j, 2j+1
       uint32_t cols[2][16];
+      const uint64_t rcp2 = f32x2(rcp, rcp);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const uint32_t w[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) cols[j >> 2][(j & 3) * 4 + e] = pack_bf16x2(bf_lo(w[e]) * rcp, bf_hi(w[e]) * rcp);
+        for (int e = 0; e < 4; ++e) {
+          const float2 u = f32x2_split(mul_f32x2(f32x2(bf_lo(w[e]), bf_hi(w[e])), rcp2));
+          cols[j >> 2][(j & 3) * 4 + e] = pack_bf16x2(u.x, u.y);
+        }
       }
       if (!mbar_wait(&bars->at_free[ab], ((i >> 1) & 1) ^ 1)) { failed = true; break; }
       tc_fence_after();
@@ -479,9 +505,9 @@ __global__ void __launch_bounds__(TR_THREADS, 1) tc_scalar_key_kernel(
           mbar_arrive(&bars->acc_empty[ab]);
         }
         if (sgrid.ok)
-          encode32<BITS, true>(y, w + part * (PD / 16), sgrid, lut_t, lut_b, bnd, sc);
+          encode32<BITS, true>(y, w + part * (PD / 16), sgrid, lut_base_adj(lut), bnd, sc);
         else
-          encode32<BITS, false>(y, w + part * (PD / 16), sgrid, lut_t, lut_b, bnd, sc);
+          encode32<BITS, false>(y, w + part * (PD / 16), sgrid, 0u, bnd, sc);
       }
       const int64_t r = tile * TR_ROWS + t;
       if (r >= n_rows) continue;
