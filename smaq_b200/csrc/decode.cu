@@ -64,7 +64,7 @@ __global__ void decode_plan_kernel(DecodeParams p) {
     p.plan[p.n_seg] = total;
     int64_t per = (total + p.grid - 1) / p.grid;
     per = (per + 15) & ~int64_t(15);
-    if (per < 16) per = 16;
+    if (per < MIN_SLICE) per = MIN_SLICE;
     p.plan[p.n_seg + 1] = per;
     p.plan[p.n_seg + 2] = 0;  // error word (set by a kernel whose bounded wait ran out)
   }

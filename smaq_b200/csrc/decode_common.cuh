@@ -6,13 +6,21 @@ namespace smaq {
 
 constexpr int DEC_WARPS = 8;
 constexpr int DEC_THREADS = DEC_WARPS * 32;
-// Partition weight of one exact-window token in units of one compressed token-head: measured
-// time per window token (an exact bf16 K+V row of 512 B, read at full load latency) against one
-// streamed compressed token-head; 12 balances the single-launch kernels' CTAs best
+// Partition weight of one exact-window token in units of one compressed token-head.  The window
+// of a pair is latency-bound (its K+V rows are read at full load latency), and the CTA holding it
+// is the one that usually arrives last at the pair and runs the pair's final merge, so the weight
+// covers the window's time plus most of a merge: at 40 the window CTAs finish their slices early
+// and a history CTA merges.  Measured best over 12..64 for the single-launch kernels (long-context
+// block-VQ at 1/2/4/8-way head shards, the 32K block-VQ batch and the paged scalar batch).
 #ifndef SMAQ_RECENT_COST
-#define SMAQ_RECENT_COST 12
+#define SMAQ_RECENT_COST 40
 #endif
 constexpr int RECENT_COST = SMAQ_RECENT_COST;
+// Shortest CTA slice (cost units, a multiple of 16).  A slice at least one window token long
+// holds the start of every window token range it meets but the last, so every CTA between the
+// first and the last CTA of a segment attends at least one of its tokens and writes its slot.
+constexpr int64_t MIN_SLICE = (int64_t(RECENT_COST) + 15) & ~int64_t(15);
+static_assert(MIN_SLICE >= RECENT_COST && MIN_SLICE >= 16, "slice floor");
 constexpr int DEC_MAX_CTAS_PER_SM = 8;  // grid cap when the caller lets the library choose
 
 struct DecodeParams {

@@ -744,7 +744,7 @@ __device__ void v3_plan(const DecodeParams& p, int64_t* plan, int64_t* scratch /
     plan[p.n_seg] = total;
     int64_t per = (total + gridDim.x - 1) / gridDim.x;
     per = (per + 15) & ~int64_t(15);
-    if (per < 16) per = 16;
+    if (per < MIN_SLICE) per = MIN_SLICE;
     plan[p.n_seg + 1] = per;
   }
   __syncthreads();
