@@ -76,7 +76,9 @@ enum {
   SMAQ_ERR_UNSUPPORTED = 2,  /* valid request outside the compiled configurations */
   SMAQ_ERR_CUDA = 3,         /* a CUDA runtime call failed */
   SMAQ_ERR_WORKSPACE = 4,    /* workspace too small */
-  SMAQ_ERR_DEVICE = 5        /* the device reported an error word */
+  SMAQ_ERR_DEVICE = 5,       /* the device reported an error word */
+  SMAQ_ERR_TIMEOUT = 6,      /* a collective made no progress before its deadline (a peer is missing) */
+  SMAQ_ERR_PEER = 7          /* a collective failed (remote or NCCL error); the communicator is aborted */
 };
 
 int smaq_abi_version(void);
@@ -323,6 +325,46 @@ typedef struct smaq_attend_args {
 size_t smaq_attend_workspace_size(int64_t n_groups, int n_queries, int64_t n_tokens, int head_dim);
 int smaq_attend_values(const smaq_attend_args* args, void* stream);
 
+
+/* ------------------------------------------------------------------ collectives */
+
+/* All-gather of sequence-split decode partials inside one split group (no counterpart in the
+ * reference, which has no multi-GPU path; the partials are what smaq_merge_partials combines).
+ * One communicator per split group, NCCL underneath, created NON-BLOCKING: every call returns
+ * within its deadline.  A peer that never arrives gives SMAQ_ERR_TIMEOUT, a remote or NCCL
+ * error SMAQ_ERR_PEER; both abort the communicator (ncclCommAbort), after which every call on
+ * it fails and the caller destroys it.  The CUDA device of the communicator is the current
+ * device at smaq_comm_init.  Sequence of a step: smaq_comm_allgather (enqueue on `stream`),
+ * then smaq_comm_wait (host waits for the exchange, polling NCCL's asynchronous error state)
+ * before the merged output is used. */
+#define SMAQ_COMM_ID_BYTES 128
+typedef struct smaq_comm* smaq_comm_t;
+/* Calls the communicator uses, each returning an ncclResult_t value (0 success, 7 in
+ * progress).  Default: NCCL from libnccl.so.2 (dlopen on first use; a process that loaded NCCL
+ * already shares it).  A host with its own NCCL build, or a test, installs its own table;
+ * NULL restores NCCL. */
+typedef struct smaq_comm_backend {
+  int (*unique_id)(uint8_t* id);
+  int (*init_rank)(void** handle, int n_ranks, const uint8_t* id, int rank);  /* non-blocking */
+  int (*async_error)(void* handle);
+  int (*all_gather)(const void* send, void* recv, size_t bytes_per_rank, void* handle, void* stream);
+  int (*abort_comm)(void* handle);
+  int (*finalize)(void* handle);
+  int (*destroy)(void* handle);
+} smaq_comm_backend;
+int smaq_comm_set_backend(const smaq_comm_backend* backend);
+/* Rank 0 of the split group makes the id and hands it to the others (any host channel). */
+int smaq_comm_unique_id(uint8_t* id /* SMAQ_COMM_ID_BYTES */);
+int smaq_comm_init(smaq_comm_t* comm, int n_ranks, int rank, const uint8_t* id, double timeout_s);
+/* recv[r * bytes .. (r+1) * bytes) <- rank r's send buffer, on `stream`. */
+int smaq_comm_allgather(smaq_comm_t comm, const void* send, void* recv, size_t bytes, void* stream,
+                        double timeout_s);
+int smaq_comm_wait(smaq_comm_t comm, void* stream, double timeout_s);
+/* Non-blocking poll of the asynchronous error state (aborts on an error). */
+int smaq_comm_status(smaq_comm_t comm);
+int smaq_comm_abort(smaq_comm_t comm);
+/* Finalize (bounded by timeout_s, abort past it) and free; accepts an aborted communicator. */
+int smaq_comm_destroy(smaq_comm_t comm, double timeout_s);
 
 /* ------------------------------------------------------------------ calibration */
 

@@ -15,7 +15,9 @@ LIB_PATH = os.path.join(_HERE, "libsmaq_b200.so")
 SMAQ_F32, SMAQ_BF16, SMAQ_F16 = 0, 1, 2
 SMAQ_KEYS_NONE, SMAQ_KEYS_SCALAR, SMAQ_KEYS_BVQ = 0, 1, 2
 SMAQ_LAYOUT_REFERENCE, SMAQ_LAYOUT_DECODE = 0, 1
-STATUS = {0: "OK", 1: "INVALID", 2: "UNSUPPORTED", 3: "CUDA", 4: "WORKSPACE", 5: "DEVICE"}
+STATUS = {0: "OK", 1: "INVALID", 2: "UNSUPPORTED", 3: "CUDA", 4: "WORKSPACE", 5: "DEVICE", 6: "TIMEOUT", 7: "PEER"}
+SMAQ_ERR_TIMEOUT, SMAQ_ERR_PEER = 6, 7
+COMM_ID_BYTES = 128
 
 # every symbol include/smaq_b200.h declares (checked by the CPU test suite)
 EXPORTS = (
@@ -25,12 +27,28 @@ EXPORTS = (
     "smaq_merge_partials", "smaq_decode_noalloc", "smaq_decode_noalloc_max_workspace",
     "smaq_decode_status", "smaq_append_status", "smaq_selftest_wait_timeout",
     "smaq_key_scores", "smaq_attend_workspace_size", "smaq_attend_values", "smaq_kmeans_workspace_size",
-    "smaq_kmeans",
+    "smaq_kmeans", "smaq_comm_set_backend", "smaq_comm_unique_id", "smaq_comm_init", "smaq_comm_allgather",
+    "smaq_comm_wait", "smaq_comm_status", "smaq_comm_abort", "smaq_comm_destroy",
 )
 
 vp = C.c_void_p
 i64 = C.c_int64
 i32 = C.c_int
+
+
+CommUniqueId = C.CFUNCTYPE(i32, vp)
+CommInitRank = C.CFUNCTYPE(i32, C.POINTER(vp), i32, vp, i32)
+CommHandleCall = C.CFUNCTYPE(i32, vp)
+CommAllGather = C.CFUNCTYPE(i32, vp, vp, C.c_size_t, vp, vp)
+
+
+class CommBackend(C.Structure):
+    """Mirror of smaq_comm_backend: NCCL calls returning ncclResult_t values."""
+    _fields_ = [
+        ("unique_id", CommUniqueId), ("init_rank", CommInitRank), ("async_error", CommHandleCall),
+        ("all_gather", CommAllGather), ("abort_comm", CommHandleCall), ("finalize", CommHandleCall),
+        ("destroy", CommHandleCall),
+    ]
 
 
 class AppendArgs(C.Structure):
@@ -136,6 +154,22 @@ def load() -> C.CDLL:
     lib.smaq_attend_workspace_size.restype = C.c_size_t
     lib.smaq_attend_values.argtypes = [C.POINTER(AttendArgs), vp]
     lib.smaq_attend_values.restype = i32
+    lib.smaq_comm_set_backend.argtypes = [vp]
+    lib.smaq_comm_set_backend.restype = i32
+    lib.smaq_comm_unique_id.argtypes = [vp]
+    lib.smaq_comm_unique_id.restype = i32
+    lib.smaq_comm_init.argtypes = [C.POINTER(vp), i32, i32, vp, C.c_double]
+    lib.smaq_comm_init.restype = i32
+    lib.smaq_comm_allgather.argtypes = [vp, vp, vp, C.c_size_t, vp, C.c_double]
+    lib.smaq_comm_allgather.restype = i32
+    lib.smaq_comm_wait.argtypes = [vp, vp, C.c_double]
+    lib.smaq_comm_wait.restype = i32
+    lib.smaq_comm_status.argtypes = [vp]
+    lib.smaq_comm_status.restype = i32
+    lib.smaq_comm_abort.argtypes = [vp]
+    lib.smaq_comm_abort.restype = i32
+    lib.smaq_comm_destroy.argtypes = [vp, C.c_double]
+    lib.smaq_comm_destroy.restype = i32
     lib.smaq_kmeans_workspace_size.argtypes = [i32, i64]
     lib.smaq_kmeans_workspace_size.restype = C.c_size_t
     lib.smaq_kmeans.argtypes = [vp, i32, i64, i32, i32, i32, C.c_uint64, vp, vp, C.c_size_t, vp]

@@ -81,7 +81,7 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> str:
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(lambda s: _compile(s, verbose_ptxas), _sources()))
     tmp = OUT + ".tmp"
-    cmd = [nvcc(), *ARCH, "-shared", "-o", tmp, *objs, "-lcudart", "-lcuda"]
+    cmd = [nvcc(), *ARCH, "-shared", "-o", tmp, *objs, "-lcudart", "-lcuda", "-ldl"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -22,10 +22,14 @@ Failure handling: the exchange is the only point where a rank waits on another. 
 ``split_groups`` a ``timeout``; a peer that died or never reaches the exchange then ends the
 all-gather with an error, which ``sharded_decode`` re-raises as ``PeerFailure`` naming the
 split group, between decode steps and with no kernel of this rank in flight.
+``native_split_comms`` gives the same groups on the library's own communicator
+(``SplitComm``, ``smaq_comm_*``): non-blocking NCCL, host-side deadlines on every step, and
+``ncclCommAbort`` when one runs out.
 """
 
 from __future__ import annotations
 
+import ctypes
 import datetime
 import math
 from dataclasses import dataclass
@@ -104,8 +108,85 @@ def split_groups(plan: ShardPlan, backend: Optional[str] = None, timeout: Option
     return groups
 
 
+class SplitComm:
+    """The library's own exchange for one split group (``smaq_comm_*``): an NCCL communicator in
+    non-blocking mode whose every step has a deadline.  A missing or failed peer raises
+    ``PeerFailure`` within ``timeout`` seconds and leaves the communicator aborted, instead of
+    blocking the host inside NCCL.  The current CUDA device at construction is the
+    communicator's device."""
+
+    def __init__(self, n_ranks: int, rank: int, comm_id: bytes, timeout: float = 60.0):
+        from . import _lib
+        self._lib = _lib.load()
+        if len(comm_id) != _lib.COMM_ID_BYTES:
+            raise ValueError(f"comm_id must be {_lib.COMM_ID_BYTES} bytes")
+        self.n_ranks, self.rank, self.timeout = n_ranks, rank, float(timeout)
+        self._h = ctypes.c_void_p()
+        self._check(self._lib.smaq_comm_init(ctypes.byref(self._h), n_ranks, rank, comm_id, self.timeout),
+                    "init")
+
+    @staticmethod
+    def unique_id() -> bytes:
+        """A fresh communicator id; rank 0 of the split group makes it and shares it."""
+        from . import _lib
+        lib = _lib.load()
+        buf = ctypes.create_string_buffer(_lib.COMM_ID_BYTES)
+        st = lib.smaq_comm_unique_id(buf)
+        if st != 0:
+            raise RuntimeError(f"smaq_comm_unique_id: {lib.smaq_last_error().decode()}")
+        return buf.raw
+
+    def _check(self, st: int, what: str) -> None:
+        if st == 0:
+            return
+        from . import _lib
+        msg = self._lib.smaq_last_error().decode()
+        if st in (_lib.SMAQ_ERR_TIMEOUT, _lib.SMAQ_ERR_PEER):
+            raise PeerFailure(f"split-group {what} (rank {self.rank} of {self.n_ranks}): {msg}")
+        raise RuntimeError(f"smaq_comm {what}: {_lib.STATUS.get(st, st)}: {msg}")
+
+    def all_gather(self, partial: torch.Tensor) -> torch.Tensor:
+        """``[...]`` on every rank -> ``[n_ranks, ...]``, on the current stream; returns after the
+        exchange completed (or raises ``PeerFailure``)."""
+        part = partial.contiguous()
+        out = torch.empty((self.n_ranks,) + tuple(part.shape), dtype=part.dtype, device=part.device)
+        stream = torch.cuda.current_stream(part.device).cuda_stream
+        nbytes = part.numel() * part.element_size()
+        self._check(self._lib.smaq_comm_allgather(self._h, part.data_ptr(), out.data_ptr(), nbytes, stream,
+                                                  self.timeout), "all-gather")
+        self._check(self._lib.smaq_comm_wait(self._h, stream, self.timeout), "wait")
+        return out
+
+    def abort(self) -> None:
+        if self._h:
+            self._lib.smaq_comm_abort(self._h)
+
+    def close(self) -> None:
+        if self._h:
+            h, self._h = self._h, ctypes.c_void_p()
+            self._lib.smaq_comm_destroy(h, self.timeout)
+
+
+def native_split_comms(plan: ShardPlan, rank: int, timeout: float = 60.0) -> list:
+    """``split_groups`` built on ``SplitComm``: every rank calls it (same order); the ids travel
+    over the default process group.  Entries are ``None`` without sequence splits, and only this
+    rank's head group gets a communicator."""
+    import torch.distributed as dist
+    if plan.seq_splits == 1:
+        return [None] * plan.head_groups
+    ids = [SplitComm.unique_id() for _ in range(plan.head_groups)] if rank == 0 else [None] * plan.head_groups
+    dist.broadcast_object_list(ids, src=0)
+    hg, sp = plan.coords(rank)
+    groups: list = [None] * plan.head_groups
+    groups[hg] = SplitComm(plan.seq_splits, sp, ids[hg], timeout=timeout)
+    return groups
+
+
 def gather_partials(partial: torch.Tensor, group, world_size: int) -> torch.Tensor:
-    """All-gather ``[B, Hq_local, 2D+2]`` fp32 partials over ``group`` -> ``[R, B, Hq_local, 2D+2]``."""
+    """All-gather ``[B, Hq_local, 2D+2]`` fp32 partials over ``group`` -> ``[R, B, Hq_local, 2D+2]``.
+    ``group`` is a torch process group or a ``SplitComm``."""
+    if isinstance(group, SplitComm):
+        return group.all_gather(partial)
     import torch.distributed as dist
     parts = [torch.empty_like(partial) for _ in range(world_size)]
     dist.all_gather(parts, partial.contiguous(), group=group)
@@ -135,6 +216,8 @@ def sharded_decode(plan: ShardPlan, rank: int, groups: Sequence, decode_fn: Call
     part = decode_fn(partial=True)
     try:
         gathered = gather_partials(part, groups[hg], plan.seq_splits)
+    except PeerFailure:
+        raise
     except Exception as e:  # the backend's timeout / closed-connection error
         raise PeerFailure(f"rank {rank}: partials exchange with ranks {plan.split_peers(rank)} failed: {e}") from e
     return combine(gathered, out_dtype, merge_fn)
