@@ -41,7 +41,8 @@ def __getattr__(name):
         "SMAQFullMetricScalarStrategy": "strategies", "SMAQBlockVQStrategy": "strategies",
         "IdentityMetricStrategy": "strategies", "SMAQFullMetricStrategy": "strategies",
         "SMAQDiagonalMetricState": "strategies", "IdentityScalarStrategy": "strategies",
-        "SMAQDiagonalMetricStrategy": "strategies", "RotationAdapter": "weighted_scalar",
+        "SMAQDiagonalMetricStrategy": "strategies", "ExactShadowStrategy": "strategies",
+        "ExactShadowQuantized": "strategies", "RotationAdapter": "weighted_scalar",
         "SMAQWeightedRotationQuantizer": "weighted_scalar", "IdentityCalibrationProvider": "calibration",
         "StaticCalibrationProvider": "calibration", "TorchHybridAttentionBackend": "backends",
         "AttentionBackend": "core", "CacheBackend": "core", "CacheCapabilities": "core",

@@ -18,7 +18,7 @@ import torch
 from smaq_b200 import ops
 from smaq_b200._lib import SMAQ_KEYS_SCALAR
 from smaq_b200.core import AttentionBackend
-from smaq_b200.store import CompressedKVStore
+from smaq_b200.store import KEYS_SHADOW, CompressedKVStore
 
 MIN_HISTORY_FOR_SMAQ = 16
 
@@ -72,6 +72,8 @@ def compute_hybrid_attention(query: torch.Tensor, store: CompressedKVStore, rece
                              recent_v: Optional[torch.Tensor], num_query_heads: int,
                              scale: Optional[float] = None) -> torch.Tensor:
     """``query [T, Hq, D]`` -> ``[T, Hq, D]`` in the query dtype."""
+    if store.key_format == KEYS_SHADOW:
+        return _shadow_attention(query, store, recent_k, recent_v, num_query_heads, scale)
     call = _decode_call(query, store, recent_k, recent_v, num_query_heads, scale)
     if call is None:
         return torch.zeros(query.shape[0], num_query_heads, store.head_dim, device=query.device, dtype=query.dtype)
@@ -79,11 +81,56 @@ def compute_hybrid_attention(query: torch.Tensor, store: CompressedKVStore, rece
     return ops.decode(q, **kw)
 
 
+def _shadow_attention(query: torch.Tensor, store: CompressedKVStore, recent_k: Optional[torch.Tensor],
+                      recent_v: Optional[torch.Tensor], num_query_heads: int, scale: Optional[float]) -> torch.Tensor:
+    """Hybrid attention with exact history keys (ExactShadowStrategy), smaq/score.py:23-72: the
+    history and window logits are fp32 GEMMs (cuBLAS), one fp32 softmax over both, the 2-bit
+    history values applied by ``smaq_attend_values`` (dequantization fused), each part cast to
+    the query dtype and the parts summed in it."""
+    ops._cuda(query, recent_k, recent_v)
+    D, Hkv = store.head_dim, store.num_kv_heads
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    T = query.shape[0]
+    G = num_query_heads // Hkv
+    flat = store.get_flat_cache()
+    has_hist = flat is not None and flat.num_tokens >= MIN_HISTORY_FOR_SMAQ
+    has_recent = recent_k is not None and recent_k.shape[0] > 0
+    if not has_hist and not has_recent:
+        return torch.zeros(T, num_query_heads, D, device=query.device, dtype=query.dtype)
+    # [Hkv, T*G, D]: query rows grouped by kv head (head h -> kv head h // G)
+    q = query.reshape(T, Hkv, G, D).transpose(0, 1).reshape(Hkv, T * G, D).float()
+    logits = []
+    if has_hist:
+        logits.append(torch.matmul(q, flat.key_q.values.float().transpose(-2, -1)) * scale)
+    if has_recent:
+        logits.append(torch.matmul(q, recent_k.float().permute(1, 2, 0)) * scale)
+    w = torch.softmax(torch.cat(logits, -1), dim=-1)
+
+    def back(x):
+        return x.reshape(Hkv, T, G, D).transpose(0, 1).reshape(T, num_query_heads, D).to(query.dtype)
+
+    out = None
+    n = 0
+    if has_hist:
+        n = flat.num_tokens
+        vq = flat.value_q
+        out = back(ops.attend_values(w[..., :n], vq.data, vq.scales, vq.zeros, bits=store.value_bits,
+                                     group_size=store.value_group_size, head_dim=D, out_dtype=torch.float32))
+    if has_recent:
+        o_r = back(torch.matmul(w[..., n:], recent_v.float().transpose(0, 1)))
+        out = o_r if out is None else out + o_r
+    return out
+
+
 def hybrid_kernel_path(query: torch.Tensor, store: CompressedKVStore, recent_k: Optional[torch.Tensor],
                        recent_v: Optional[torch.Tensor], num_query_heads: int,
                        scale: Optional[float] = None) -> Optional[int]:
     """The decode kernel path compute_hybrid_attention would run for these arguments
-    (``ops.PATH_*``; None when there is nothing to attend).  Launches nothing."""
+    (``ops.PATH_*``; None when there is nothing to attend or the keys are exact shadows, which
+    take no decode kernel).  Launches nothing."""
+    if store.key_format == KEYS_SHADOW:
+        return None
     call = _decode_call(query, store, recent_k, recent_v, num_query_heads, scale)
     if call is None:
         return None

@@ -27,7 +27,11 @@ from smaq_b200.calibration import IdentityCalibrationProvider
 from smaq_b200.core import CacheCapabilities, CalibrationProvider
 from smaq_b200.kv_cache import ValueQuantized
 from smaq_b200.quantizer import SMAQQuantized
-from smaq_b200.strategies import IdentityScalarStrategy, SMAQBlockVQStrategy, SMAQFullMetricScalarStrategy
+from smaq_b200.strategies import (ExactShadowQuantized, ExactShadowStrategy, IdentityScalarStrategy,
+                                  SMAQBlockVQStrategy, SMAQFullMetricScalarStrategy)
+
+# Exact (unquantized) history keys: ExactShadowStrategy.  Host-side tag only; no kernel key format.
+KEYS_SHADOW = -1
 
 
 class FlatCache(NamedTuple):
@@ -43,10 +47,12 @@ def key_format_of(strategy) -> int:
         return SMAQ_KEYS_SCALAR
     if isinstance(strategy, SMAQBlockVQStrategy):
         return SMAQ_KEYS_BVQ
+    if isinstance(strategy, ExactShadowStrategy):
+        return KEYS_SHADOW
     raise NotImplementedError(
         f"key strategy {type(strategy).__name__} has no sm_100a kernel (supported: the scalar strategies "
-        "IdentityScalarStrategy / SMAQFullMetricScalarStrategy / SMAQDiagonalMetricStrategy, and "
-        "SMAQBlockVQStrategy)")
+        "IdentityScalarStrategy / SMAQFullMetricScalarStrategy / SMAQDiagonalMetricStrategy, "
+        "SMAQBlockVQStrategy, and ExactShadowStrategy)")
 
 
 class CompressedKVStore:
@@ -109,8 +115,10 @@ class CompressedKVStore:
     def _alloc(self, cap: int, dtype: torch.dtype) -> dict[str, torch.Tensor]:
         H, D, dev = self.num_kv_heads, self.head_dim, self.device
         ng = D // self.value_group_size
+        keys = (torch.empty((H, cap, D), dtype=dtype, device=dev) if self.key_format == KEYS_SHADOW else
+                torch.empty((H, cap, self._key_row_bytes()), dtype=torch.uint8, device=dev))
         b = {
-            "codes": torch.empty((H, cap, self._key_row_bytes()), dtype=torch.uint8, device=dev),
+            "codes": keys,
             "vdata": torch.empty((H, cap, D * self.value_bits // 8), dtype=torch.uint8, device=dev),
             "vscales": torch.empty((H, cap, ng), dtype=dtype, device=dev),
             "vzeros": torch.empty((H, cap, ng), dtype=dtype, device=dev),
@@ -121,6 +129,8 @@ class CompressedKVStore:
 
     def _decode_layout_ok(self, dtype: torch.dtype) -> bool:
         """True when the rows can use the fast decode kernels' byte order."""
+        if self.key_format == KEYS_SHADOW:
+            return False
         if dtype != torch.bfloat16 or self.head_dim != 128 or self.value_bits != 2 or self.value_group_size != 32:
             return False
         if self.key_format == SMAQ_KEYS_SCALAR:
@@ -156,7 +166,11 @@ class CompressedKVStore:
         if T:
             strat = self.key_strategy
             kw = {}
-            if self.key_format == SMAQ_KEYS_SCALAR:
+            if self.key_format == KEYS_SHADOW:
+                # keys kept as given; the value half of the append kernel quantizes the values
+                self._buf["codes"][:, self._n: self._n + T].copy_(key.transpose(0, 1))
+                key = None
+            elif self.key_format == SMAQ_KEYS_SCALAR:
                 qz = strat.quantizer
                 kw = dict(key_format=SMAQ_KEYS_SCALAR, key_bits=strat.bits, E=qz.E, boundaries=qz.decision_boundaries,
                           key_norms=self._buf["norms"])
@@ -184,7 +198,9 @@ class CompressedKVStore:
         n, b = self._n, self._buf
         dec = self.layout == SMAQ_LAYOUT_DECODE
         codes, vdata = b["codes"][:, :n], b["vdata"][:, :n]
-        if self.key_format == SMAQ_KEYS_SCALAR:
+        if self.key_format == KEYS_SHADOW:
+            kq = ExactShadowQuantized(values=codes)
+        elif self.key_format == SMAQ_KEYS_SCALAR:
             if dec:
                 codes = ops.scalar_codes_to_reference(codes)
             kq = SMAQQuantized(indices=codes, norms=b["norms"][:, :n], bits=self.key_strategy.bits)
@@ -205,7 +221,9 @@ class CompressedKVStore:
             return 0
         n, H = self._n, self.num_kv_heads
         ng = self.head_dim // self.value_group_size
-        if self.key_format == SMAQ_KEYS_SCALAR:
+        if self.key_format == KEYS_SHADOW:
+            keys = H * n * self.head_dim * self._buf["codes"].element_size()
+        elif self.key_format == SMAQ_KEYS_SCALAR:
             keys = H * n * self._key_row_bytes() + 2 * H * n
         else:
             keys = H * n * self._key_row_bytes() * 8

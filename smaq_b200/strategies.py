@@ -4,14 +4,15 @@ Scalar-code strategies (``IdentityScalarStrategy`` and its subclasses
 ``SMAQFullMetricScalarStrategy`` and ``SMAQDiagonalMetricStrategy``) share the
 ``SMAQQuantized`` format.  Their quantizers expose ``E`` / ``E_inv`` / ``centroids`` /
 ``decision_boundaries``, so the scalar-key append and decode kernels serve all three.
-``SMAQBlockVQStrategy`` is served by the block-VQ kernels.  The reference's
-``ExactShadowStrategy`` keeps the history's keys unquantized and scores them with a dense
-matmul: it is a validation mode outside the compressed path and is not provided.
+``SMAQBlockVQStrategy`` is served by the block-VQ kernels.  ``ExactShadowStrategy`` keeps the
+history's keys unquantized (values stay 2-bit): a validation mode that measures what key
+compression costs.  Its scores are a plain GEMM (cuBLAS); the compressed values are applied
+by the fused attend kernel (``smaq_attend_values``).
 """
 
 from __future__ import annotations
 
-from typing import Any
+from typing import Any, NamedTuple
 
 import torch
 
@@ -199,3 +200,51 @@ class SMAQBlockVQStrategy(QuantizationStrategy):
 
     def memory_bytes(self, quantized: BlockVQQuantized) -> int:
         return quantized.indices.nelement() * quantized.indices.element_size()
+
+
+class ExactShadowQuantized(NamedTuple):
+    """Unquantized keys ``[..., N, D]`` standing in for codes (smaq/strategies.py:70-83)."""
+
+    values: torch.Tensor
+
+
+class ExactShadowStrategy(QuantizationStrategy):
+    """Exact history keys (smaq/strategies.py:258-298): the history half of the cache keeps
+    its keys as stored, so attention differs from full precision only by the value codes."""
+
+    name = "exact_shadow"
+    metric_name = "identity"
+    quantization_name = "shadow_exact"
+
+    @property
+    def capabilities(self):
+        from smaq_b200.core import CacheCapabilities
+        return CacheCapabilities(strategy_name=self.name, metric_name=self.metric_name,
+                                 quantization_name=self.quantization_name, compressed_history=False,
+                                 compressed_history_shadow_only=True, values_compressed=False,
+                                 decode_uses_compressed_keys=False, decode_uses_compressed_values=False)
+
+    def quantize(self, keys: Any) -> Any:
+        return ExactShadowQuantized(values=keys.detach().clone())
+
+    def dequantize(self, quantized: Any) -> Any:
+        return quantized.values
+
+    def attention_score(self, query: Any, quantized: Any, scale: float | None = None, **kwargs: Any) -> Any:
+        s = torch.matmul(query.float(), quantized.values.float().transpose(-2, -1))
+        if scale is not None:
+            s = s * scale
+        return s.to(query.dtype)
+
+    def flatten_quantized(self, quantized: ExactShadowQuantized) -> ExactShadowQuantized:
+        v = quantized.values
+        return ExactShadowQuantized(values=v.reshape(-1, v.shape[-2], v.shape[-1]).contiguous())
+
+    def concat_quantized(self, chunks: list[ExactShadowQuantized]) -> ExactShadowQuantized:
+        return ExactShadowQuantized(values=torch.cat([c.values for c in chunks], dim=-2))
+
+    def select_head(self, quantized: ExactShadowQuantized, head_idx: int) -> ExactShadowQuantized:
+        return ExactShadowQuantized(values=quantized.values[head_idx])
+
+    def memory_bytes(self, quantized: ExactShadowQuantized) -> int:
+        return quantized.values.nelement() * quantized.values.element_size()

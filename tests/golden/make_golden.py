@@ -8,7 +8,8 @@ Usage::
 must sit directly under it).  The reference is pure Python on PyTorch; it is
 imported here, fed the seeded synthetic inputs of ``smaq_b200.synthetic``, and
 its outputs are written to ``tests/golden/golden.npz`` and, for the rotation adapter
-(smaq/weighted_scalar.py), ``tests/golden/golden_rotation.npz``.  bf16/fp16 tensors are
+(smaq/weighted_scalar.py), ``tests/golden/golden_rotation.npz``, and for the exact-key
+shadow strategy, ``tests/golden/golden_shadow.npz``.  bf16/fp16 tensors are
 stored as float32 arrays holding exactly representable values.  The GPU box
 never runs this script; the tests only read the ``.npz`` files it wrote.
 """
@@ -112,17 +113,59 @@ def rotation_goldens(out):
     out[p + "meta"] = np.array([Hq, Hkv, nh, nr], np.int64)
 
 
+def shadow_goldens(out):
+    """ExactShadowStrategy (smaq/strategies.py:258-298) through the store and
+    compute_hybrid_attention: exact history keys, 2-bit values, bf16 and fp32."""
+    import torch
+    from smaq.strategies import ExactShadowStrategy
+    from smaq.store import CompressedKVStore
+    from smaq.score import compute_hybrid_attention
+    D = 128
+    cpu = torch.device("cpu")
+    cases = (("bf16", torch.bfloat16, 28, 4, 300, 64, 700), ("bf16_histonly", torch.bfloat16, 8, 2, 120, 0, 710),
+             ("fp32", torch.float32, 8, 2, 150, 10, 720), ("hist15", torch.bfloat16, 8, 2, 15, 20, 730))
+    for tag, dt, Hq, Hkv, nh, nr, seed in cases:
+        hk = torch.from_numpy(syn.keys((nh, Hkv), D, seed=seed)).to(dt)
+        hv = torch.from_numpy(syn.values((nh, Hkv), D, seed=seed + 1)).to(dt)
+        rk = torch.from_numpy(syn.keys((nr, Hkv), D, seed=seed + 2)).to(dt) if nr else None
+        rv = torch.from_numpy(syn.values((nr, Hkv), D, seed=seed + 3)).to(dt) if nr else None
+        q = torch.from_numpy(syn.queries((1, Hq), D, seed=seed + 4)).to(dt)
+        store = CompressedKVStore(D, Hkv, device=cpu, key_strategy=ExactShadowStrategy())
+        h1 = nh // 3
+        store.append_chunk(hk[:h1], hv[:h1])
+        store.append_chunk(hk[h1:], hv[h1:])
+        o = compute_hybrid_attention(q, store, rk, rv, Hq)
+        p = f"sh_{tag}_"
+        flat = store.get_flat_cache()
+        for name, t in (("hist_k", hk), ("hist_v", hv), ("q", q), ("out", o), ("v_data", flat.value_q.data)):
+            out[p + name] = t2n(t)
+        if nr:
+            out[p + "recent_k"], out[p + "recent_v"] = t2n(rk), t2n(rv)
+        out[p + "meta"] = np.array([Hq, Hkv, nh, nr], np.int64)
+        out[p + "memory_bytes"] = np.array([store.memory_bytes()], np.int64)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SMAQ_REFERENCE"),
                     help="checkout of gauravsaini/smaq (or set SMAQ_REFERENCE)")
-    ap.add_argument("--only", choices=["all", "rotation"], default="all",
-                    help="rotation: write only golden_rotation.npz")
+    ap.add_argument("--only", choices=["all", "rotation", "shadow"], default="all",
+                    help="rotation: write only golden_rotation.npz; shadow: only golden_shadow.npz")
     args = ap.parse_args()
     if not args.reference:
         ap.error("--reference PATH (or SMAQ_REFERENCE) is required")
     sys.path.insert(0, args.reference)
     import torch
+    if args.only in ("all", "shadow"):
+        import smaq  # the reference package
+        assert "reference" in smaq.__file__ or args.reference in smaq.__file__, smaq.__file__
+        sh = {}
+        shadow_goldens(sh)
+        path = os.path.join(HERE, "golden_shadow.npz")
+        np.savez_compressed(path, **sh)
+        print("wrote", path, os.path.getsize(path) // 1024, "KiB,", len(sh), "arrays")
+        if args.only == "shadow":
+            return
     if args.only in ("all", "rotation"):
         import smaq  # the reference package
         assert "reference" in smaq.__file__ or args.reference in smaq.__file__, smaq.__file__
