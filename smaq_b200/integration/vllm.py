@@ -19,7 +19,7 @@ registered attention backend (integration/vllm_backend.py) and the monkey-patch 
 
 ``no_alloc`` (vLLM's cache freed) keeps the reference's single-sequence behaviour: one compressed
 store and one exact ring per layer (capture.py), decode through ``compute_hybrid_attention``, and
-prefill attention over the chunk itself.  Without vLLM's cache there is no per-sequence exact
+prefill attention over the chunk itself (this package's decode kernel, ``ops.causal_attention``).  Without vLLM's cache there is no per-sequence exact
 window to read, so that mode serves one sequence at a time.  MLA layers are recognised and
 passed through, as in the reference.  The mode is process-global.
 """
@@ -33,8 +33,7 @@ from dataclasses import dataclass, field
 from typing import Callable, Optional
 
 import torch
-import torch.nn.functional as F
-
+from .. import ops
 from ..capture import KVCaptureEngine
 from ..score import MIN_HISTORY_FOR_SMAQ, compute_hybrid_attention
 from ..store import CompressedKVStore
@@ -92,11 +91,10 @@ def _emit(result: torch.Tensor, query: torch.Tensor, output: Optional[torch.Tens
 
 
 def _causal_chunk_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float) -> torch.Tensor:
-    """Causal attention of a prefill chunk over itself, ``[n, H, D]`` in and out; grouped
-    query heads read their shared KV head directly (no expanded copy of K and V)."""
-    out = F.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None], v.transpose(0, 1)[None],
-                                         is_causal=True, scale=scale, enable_gqa=q.shape[1] != k.shape[1])
-    return out[0].transpose(0, 1)
+    """Causal attention of a prefill chunk over itself, ``[n, H, D]`` in and out, on this
+    package's decode kernel (``ops.causal_attention``): grouped query heads read their shared
+    KV head directly, with no expanded copy of K and V and no library attention kernel."""
+    return ops.causal_attention(q, k, v, scale)
 
 
 class LayerState:

@@ -407,6 +407,57 @@ def decode(q: torch.Tensor, *, n_kv_heads: int, key_format: int, key_codes: torc
     return out
 
 
+_EMPTY_STORES: dict = {}
+
+
+def _empty_store(device: torch.device, n_kv_heads: int, head_dim: int, dtype: torch.dtype) -> dict:
+    """One 16-row page of 4-bit scalar-key store rows (decode layout) that no decode reads: the
+    history streams of a window-only decode must still be valid pointers."""
+    key = (device, n_kv_heads, head_dim, dtype)
+    st = _EMPTY_STORES.get(key)
+    if st is None:
+        H, D = n_kv_heads, head_dim
+        st = dict(codes=torch.zeros((1, H, 16, packed_dim(D, 4)), dtype=torch.uint8, device=device),
+                  norms=torch.zeros((1, H, 16), dtype=dtype, device=device),
+                  vdata=torch.zeros((1, H, 16, D // 4), dtype=torch.uint8, device=device),
+                  vsz=torch.zeros((1, H, 16, max(1, D // 32)), dtype=dtype, device=device),
+                  E_inv=torch.eye(D, dtype=torch.float32, device=device),
+                  centroids=torch.zeros(16, dtype=torch.float32, device=device))
+        _EMPTY_STORES[key] = st
+    return st
+
+
+def causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: Optional[float] = None) -> torch.Tensor:
+    """Causal attention of a chunk over itself: ``q [n, Hq, D]``, ``k / v [n, Hkv, D]`` ->
+    ``[n, Hq, D]`` in the query dtype; query head ``h`` reads KV head ``h // (Hq / Hkv)``.
+
+    Runs as one ``smaq_decode`` over ``n`` window-only rows: row ``i`` is query token ``i`` with
+    an exact window of the chunk's first ``i + 1`` tokens.  The window is the chunk itself for
+    every row (batch stride 0), so K and V are neither expanded per query head nor copied per
+    row; the rows of one KV head are re-read from L2 (``n^2 / 2`` row reads per head).  bf16 /
+    fp16 inputs with head_dim 128 and at most 8 query heads per KV head take the tensor-core
+    window of the fused scalar-key kernel while ``2 n Hkv <= 2048``, other shapes the general
+    kernel."""
+    _cuda(q, k, v)
+    n, Hq, D = q.shape
+    Hkv = k.shape[1]
+    if n == 0:
+        return torch.empty_like(q)
+    k = k if k.stride(-1) == 1 and k.is_contiguous() else k.contiguous()
+    v = v if v.is_contiguous() else v.contiguous()
+    if v.dtype != k.dtype:
+        v = v.to(k.dtype)
+    st = _empty_store(q.device, Hkv, D, k.dtype if k.dtype != torch.float32 else torch.bfloat16)
+    rows = torch.arange(1, n + 1, dtype=torch.int32, device=q.device)
+    zero = torch.zeros(n, dtype=torch.int32, device=q.device)
+    return decode(q, n_kv_heads=Hkv, key_format=SMAQ_KEYS_SCALAR, key_bits=4, E_inv=st["E_inv"],
+                  centroids=st["centroids"], key_norms=st["norms"], key_codes=st["codes"], v_data=st["vdata"],
+                  v_scales=st["vsz"], v_zeros=st["vsz"], hist_len=zero, page_size=16,
+                  block_table=torch.zeros((n, 1), dtype=torch.int32, device=q.device),
+                  recent_k=k.unsqueeze(0).expand(n, n, Hkv, D), recent_v=v.unsqueeze(0).expand(n, n, Hkv, D),
+                  recent_len=rows, scale=scale, layout=SMAQ_LAYOUT_DECODE)
+
+
 def merge_partials(partials: torch.Tensor, out_dtype: torch.dtype) -> torch.Tensor:
     """``[R, B, Hq, 2D+2]`` fp32 partials -> ``[B, Hq, D]`` output."""
     _cuda(partials)

@@ -289,21 +289,17 @@ def test_mixed_prefill_decode_step_runs_vllm_attention(monkeypatch):
     assert int(st.cache.prompt_len[bt.bt[1, 0].long()]) == 33    # the chunk row's new prompt length
 
 
-def test_no_alloc_prefill_is_causal_attention_and_empty_decode_is_zero():
+def test_no_alloc_prefill_needs_the_gpu_and_empty_decode_is_zero():
+    """CPU half: the no-allocation prefill runs on this package's kernel, so CPU tensors raise
+    (no fallback); a decode before anything was compressed is zero; vLLM's cache write is
+    skipped.  The prefill's numbers are checked on the GPU (tests/test_gpu_causal.py)."""
     r = FakeRunner(n_layers=1)
     iv.install_hooks(r, mode=iv.MODE_HYBRID, no_alloc=True)
     im = r.compilation_config.static_forward_context["layer.0"].impl
     n = 7
     q, k, v = torch.randn(n, 4, D), torch.randn(n, 2, D), torch.randn(n, 2, D)
-    out = im.forward(None, q, k, v, None, meta(n, n))
-    kk, vv = k.repeat_interleave(2, 1), v.repeat_interleave(2, 1)
-    s = torch.einsum("thd,shd->hts", q, kk) * im.scale
-    s = s.masked_fill(torch.triu(torch.ones(n, n, dtype=torch.bool), 1), float("-inf"))
-    ref = torch.einsum("hts,shd->thd", s.softmax(-1), vv)
-    assert torch.allclose(out, ref, atol=1e-5)
-    buf = torch.zeros(n, 4 * D)
-    im.forward(None, q.reshape(n, -1), k.reshape(n, -1), v.reshape(n, -1), None, meta(n, n), output=buf)
-    assert torch.allclose(buf.view(n, 4, D), ref, atol=1e-5)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        im.forward(None, q, k, v, None, meta(n, n))
     dq = torch.randn(1, 4 * D)
     out = im.forward(None, dq, dq[:, : 2 * D], dq[:, : 2 * D], None, meta(1, 1))
     assert out.shape == (1, 4 * D) and torch.all(out == 0)     # nothing compressed yet
