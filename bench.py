@@ -70,7 +70,7 @@ def parse(argv=None):
     ap.add_argument("--impl", default="smaq_b200", choices=["smaq_b200", "reference"])
     ap.add_argument("--workload", default="longctx", choices=["longctx", "decode", "append", "append_bvq", "paged", "scores"])
     ap.add_argument("--layers", type=int, default=0, help="build fewer layers (profiling runs only; 0: the config's)")
-    ap.add_argument("--no-cfg1", action="store_true", help="longctx at N=1: skip the configs[1] sub-measurement")
+    ap.add_argument("--no-cfg1", action="store_true", help="longctx at N=1: skip the configs[1], [2] and [3] sub-measurements")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", dest="graph", action="store_false", help="launch every layer from Python")
     ap.add_argument("--no-overlap", dest="overlap", action="store_false",
@@ -406,6 +406,13 @@ def run_decode(a, rank: int, world: int):
         l1 = decode_line(s1, t1, a.steps, a.warmup)
         line["cfg1"] = {k: l1[k] for k in ("value", "unit", "ms_per_step", "config", "hbm_gbs", "roofline", "e2e",
                                            "clocks")}
+        # configs[2] (append) and configs[3] (paged scalar-key decode), same steps, no CPU sample
+        sub = argparse.Namespace(**{**vars(a), "layers": 0, "no_cpu_baseline": True})
+        keep = ("metric", "value", "unit", "ms_per_step", "config", "roofline", "e2e", "gpu_launches", "clocks")
+        l2 = run_append(sub, 0, 1, emit=False)
+        line["cfg2"] = {k: l2[k] for k in keep if k in l2}
+        l3 = run_paged(sub, 0, 1, emit=False)
+        line["cfg3"] = {k: l3[k] for k in keep if k in l3}
     if rank == 0:
         if world == 1 and not a.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(spec)
@@ -631,7 +638,7 @@ def append_step(k, v, quant, o, keys=True, values=True):
                layout=SMAQ_LAYOUT_DECODE)
 
 
-def run_append(a, rank: int, world: int):
+def run_append(a, rank: int, world: int, emit: bool = True):
     import torch
     import torch.distributed as dist
     from smaq_b200 import build
@@ -744,6 +751,8 @@ def run_append(a, rank: int, world: int):
             "gpu_launches": 2 * a.steps,
             "clocks": ck,
         }
+        if not emit:
+            return line
         if world == 1 and not a.no_cpu_baseline:
             line["cpu_baseline"] = append_cpu_sample()
         print(json.dumps(line), flush=True)
@@ -891,7 +900,7 @@ def paged_decode(L, quant, hl, rl, ws, overlap: bool):
                       layout=SMAQ_LAYOUT_DECODE, overlap_prior=overlap)
 
 
-def run_paged(a, rank: int, world: int):
+def run_paged(a, rank: int, world: int, emit: bool = True):
     import torch
     from smaq_b200 import build, ops
     build.build()
@@ -974,6 +983,10 @@ def run_paged(a, rank: int, world: int):
                     "d2h_bytes_per_step": hO.numel() * hO.element_size(),
                     "note": "per layer: query rows host -> device, decode, output rows device -> host"},
             "gpu_launches": n_layers * a.steps, "clocks": ck}
+    del layers
+    torch.cuda.empty_cache()
+    if not emit:
+        return line
     if not a.no_cpu_baseline:
         line["cpu_baseline"] = paged_cpu_sample()
     if rank == 0:
