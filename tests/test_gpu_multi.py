@@ -1,6 +1,7 @@
 """Sequence-split decode across real GPUs over NCCL (smaq_b200.distributed.sharded_decode): each
-rank decodes its token range into partials, the partials are all-gathered and merged, and the
-result must match the single-GPU decode of the whole history.  Needs >= 2 GPUs (skipped
+rank decodes its token range into partials, the partials are all-gathered (torch process group,
+or the library's own communicator, smaq_comm_*) and merged, and the result must match the
+single-GPU decode of the whole history.  Needs >= 2 GPUs (skipped
 otherwise); every rank runs in its own process."""
 
 import os
@@ -14,7 +15,7 @@ pytestmark = pytest.mark.gpu
 D = 128
 
 
-def _worker(rank, world, port, result_path):
+def _worker(rank, world, port, result_path, native=False):
     import torch
     import torch.distributed as dist
     from smaq_b200 import distributed as sd, ops, synthetic as syn
@@ -31,7 +32,7 @@ def _worker(rank, world, port, result_path):
         Eb = torch.from_numpy((np.eye(8)[None] + 0.1 * rng.standard_normal((16, 8, 8))).astype(np.float32)).to(dev)
         dec = torch.from_numpy((rng.standard_normal((16, 256, 8)) * 0.5).astype(np.float16).astype(np.float32)).to(dev)
         plan = sd.make_plan(world, Hkv)
-        groups = sd.split_groups(plan)
+        groups = sd.native_split_comms(plan, rank, timeout=30.0) if native else sd.split_groups(plan)
         # every rank builds the whole store (same seeds) and attends only to its range
         pages = [(n + page - 1) // page for n in hist]
         st = {k: torch.zeros((sum(pages), Hkv, page, w), dtype=torch.uint8, device=dev) for k, w in
@@ -77,11 +78,15 @@ def _worker(rank, world, port, result_path):
         err = O.rel_l2(got.float().cpu().numpy(), full.float().cpu().numpy())
         with open(f"{result_path}.{rank}", "w") as fh:
             fh.write(repr(err))
+        for g in groups:
+            if isinstance(g, sd.SplitComm):
+                g.close()
     finally:
         dist.destroy_process_group()
 
 
-def test_sequence_split_over_nccl(tmp_path):
+@pytest.mark.parametrize("native", [False, True], ids=["torch_group", "smaq_comm"])
+def test_sequence_split_over_nccl(tmp_path, native):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -90,7 +95,8 @@ def test_sequence_split_over_nccl(tmp_path):
     build.build()
     world = 2
     res = str(tmp_path / "err")
-    mp.start_processes(_worker, args=(world, 29700 + os.getpid() % 200, res), nprocs=world, join=True,
+    mp.start_processes(_worker, args=(world, 29700 + os.getpid() % 200 + 300 * native, res, native), nprocs=world,
+                       join=True,
                        start_method="spawn")
     for r in range(world):
         assert float(open(f"{res}.{r}").read()) <= 2e-3
