@@ -175,16 +175,22 @@ __global__ void __launch_bounds__(256) value_bf16_g32_kernel(
   const uint32_t mn_pair = mnb | (mnb << 16);
   // ((v - zero) / scale).round().clamp(0, 3)   (kv_cache.py:85); NaN -> 0
   const uint32_t zero2 = 0u, three2 = 0x40404040u, magic2 = 0x43404340u;  // bf16 pairs 0, 3, 192
-  uint32_t lo = 0, hi = 0;
+  // q = 192 + code in each bf16 half: the code is bits 0-1 (element 2i) and 16-17 (element
+  // 2i + 1), and 192's own low mantissa bits are 0.  Pairs i = 4k .. 4k + 3 collect their two
+  // code fields at bits 4(i - 4k) and 16 + 4(i - 4k) of acc[k]; one shift-and-merge per acc[k]
+  // then interleaves them into the packed order (element 2i at bit 4i, 2i + 1 at bit 4i + 2).
+  uint32_t acc[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const uint32_t d = bf2_sub(x[i], mn_pair);
     uint32_t q = bf2_pack(__uint_as_float(d << 16) * rscale, __uint_as_float(d & 0xFFFF0000u) * rscale);
     q = bf2_add(bf2_min(bf2_max(q, zero2), three2), magic2);
-    const uint32_t c = ((q - magic2) & 0x3u) | (((q - magic2) >> 14) & 0xCu);  // codes 2i, 2i+1
-    if (i < 8) lo |= c << (4 * i);
-    else hi |= c << (4 * (i - 8));
+    acc[i >> 2] |= (q & 0x00030003u) << (4 * (i & 3));
   }
+  uint32_t half16[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) half16[k] = (acc[k] & 0x3333u) | ((acc[k] >> 14) & 0xCCCCu);
+  uint32_t lo = half16[0] | (half16[1] << 16), hi = half16[2] | (half16[3] << 16);
   if (layout == SMAQ_LAYOUT_DECODE) {
     // byte 4 * b + g of the row holds reference byte 8 * g + b (b < 8): transpose the 4 x 8
     // byte matrix held by the row's four threads.  16-bit chunk c of thread g = bytes 2c, 2c+1.
