@@ -16,7 +16,7 @@ import sys
 
 __version__ = "0.1.0"
 
-_MIRRORED = ("ssf", "core", "calibration", "quantizer", "weighted_scalar", "block_vq", "kv_cache", "strategies",
+_MIRRORED = ("ssf", "core", "calibration", "layout", "quantizer", "weighted_scalar", "block_vq", "kv_cache", "strategies",
              "store", "score", "capture", "backends")
 
 
@@ -47,7 +47,9 @@ def __getattr__(name):
         "StaticCalibrationProvider": "calibration", "TorchHybridAttentionBackend": "backends",
         "AttentionBackend": "core", "CacheBackend": "core", "CacheCapabilities": "core",
         "CalibrationProvider": "core", "LayoutInfo": "core", "MetricStrategy": "core",
-        "QuantizationStrategy": "core",
+        "QuantizationStrategy": "core", "ModelLayoutAdapter": "core",
+        "GenericModelLayoutAdapter": "layout", "QwenModelLayoutAdapter": "layout",
+        "GemmaModelLayoutAdapter": "layout", "infer_model_layout_adapter": "layout",
     }
     if name in table:
         return getattr(importlib.import_module(f"{__name__}.{table[name]}"), name)

@@ -124,3 +124,24 @@ class CacheBackend(ABC):
     @abstractmethod
     def capabilities(self) -> CacheCapabilities:
         ...
+
+
+class ModelLayoutAdapter(ABC):
+    """Per-model-family view of the KV tensors a layer hands over (smaq/core.py:152-173):
+    which head dim the cache should use, and whether keys arrive widened or unified."""
+
+    name: str = "generic"
+
+    def resolve_head_dim(self, model: Any, layer_idx: int) -> int:
+        attn = getattr(model.layers[layer_idx], "self_attn", None)
+        if attn is None:
+            return 128
+        if hasattr(attn, "head_dim"):
+            return int(attn.head_dim)
+        if hasattr(attn, "hidden_size") and hasattr(attn, "num_heads"):
+            return int(attn.hidden_size // attn.num_heads)
+        return 128
+
+    @abstractmethod
+    def normalize_kv(self, keys: Any, values: Any, expected_head_dim: int | None = None) -> LayoutInfo:
+        ...
