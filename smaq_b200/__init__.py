@@ -16,8 +16,8 @@ import sys
 
 __version__ = "0.1.0"
 
-_MIRRORED = ("ssf", "core", "calibration", "layout", "quantizer", "weighted_scalar", "block_vq", "kv_cache", "strategies",
-             "store", "score", "capture", "backends")
+_MIRRORED = ("ssf", "core", "calibration", "layout", "quantizer", "triton_kernels", "weighted_scalar", "block_vq",
+             "kv_cache", "strategies", "store", "score", "capture", "backends")
 
 
 def install_as_smaq() -> None:

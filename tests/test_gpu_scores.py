@@ -40,6 +40,25 @@ def test_scalar_key_scores(cuda, bits, D, qdt):
         assert rel(tn(got), ref) <= (2e-6 if qdt == torch.float32 else 4e-3)
 
 
+def test_triton_kernels_entry_point(cuda):
+    """smaq.triton_kernels.smaq_attention_scores (smaq/triton_kernels.py:190-208): the reference's
+    decode-tile shape (query [n_qh, D], packed keys [N, P], norms [N]) -> unscaled fp32 scores,
+    on the CUDA scoring kernel."""
+    from smaq_b200.quantizer import SMAQQuantizer
+    from smaq_b200.triton_kernels import smaq_attention_scores
+    g = torch.Generator().manual_seed(7)
+    D, bits = 128, 4
+    qz = SMAQQuantizer(D, bits=bits, device=cuda)
+    qz.fit(torch.randn(512, D, generator=g).to(cuda))
+    kq = qz.quantize(torch.randn(1000, D, generator=g).to(cuda).to(torch.bfloat16))
+    q = torch.randn(8, D, generator=g).to(cuda).to(torch.bfloat16)
+    got = smaq_attention_scores(qz, q, kq)
+    assert got.shape == (8, 1000) and got.dtype == torch.float32
+    y = tn(qz.centroids)[O.unpack_indices(tn(kq.indices).astype(np.uint8), bits, D)]
+    ref = (tn(q) @ tn(qz.E_inv).T) @ y.T * tn(kq.norms)[None, :]
+    assert rel(tn(got), ref) <= 2e-6
+
+
 @pytest.mark.parametrize("int64", [True, False])
 def test_bvq_key_scores(cuda, int64):
     from smaq_b200.block_vq import SMAQBlockVQ
