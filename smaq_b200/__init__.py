@@ -43,7 +43,9 @@ def __getattr__(name):
         "SMAQDiagonalMetricState": "strategies", "IdentityScalarStrategy": "strategies",
         "SMAQDiagonalMetricStrategy": "strategies", "ExactShadowStrategy": "strategies",
         "ExactShadowQuantized": "strategies", "RotationAdapter": "weighted_scalar",
-        "SMAQWeightedRotationQuantizer": "weighted_scalar", "IdentityCalibrationProvider": "calibration",
+        "SMAQWeightedRotationQuantizer": "weighted_scalar", "build_codebook": "weighted_scalar",
+        "build_rotated_diagonal_metric_scales": "weighted_scalar",
+        "build_block_diagonal_metric_scales": "weighted_scalar", "IdentityCalibrationProvider": "calibration",
         "StaticCalibrationProvider": "calibration", "TorchHybridAttentionBackend": "backends",
         "AttentionBackend": "core", "CacheBackend": "core", "CacheCapabilities": "core",
         "CalibrationProvider": "core", "LayoutInfo": "core", "MetricStrategy": "core",

@@ -82,3 +82,18 @@ def test_layout_module_is_mirrored():
     with pytest.raises(TypeError):
         from smaq_b200.core import ModelLayoutAdapter
         ModelLayoutAdapter()
+
+
+def test_top_level_names_of_the_reference_package():
+    """Every name smaq/__init__.py re-exports resolves on this package."""
+    import smaq_b200
+    names = """TorchHybridAttentionBackend IdentityCalibrationProvider StaticCalibrationProvider BlockVQQuantized
+    SMAQBlockVQ AttentionBackend CacheBackend CacheCapabilities CalibrationProvider LayoutInfo MetricStrategy
+    ModelLayoutAdapter QuantizationStrategy KVCaptureEngine RingBuffer SMAQKVCache GemmaModelLayoutAdapter
+    GenericModelLayoutAdapter QwenModelLayoutAdapter infer_model_layout_adapter SMAQQuantized SMAQQuantizer
+    compute_hybrid_attention ExactShadowStrategy IdentityMetricStrategy IdentityScalarStrategy SMAQBlockVQStrategy
+    SMAQDiagonalMetricState SMAQDiagonalMetricStrategy SMAQFullMetricScalarStrategy SMAQFullMetricStrategy
+    CompressedKVStore RotationAdapter SMAQWeightedRotationQuantizer build_rotated_diagonal_metric_scales
+    build_block_diagonal_metric_scales build_codebook""".split()
+    missing = [n for n in names if not hasattr(smaq_b200, n)]
+    assert not missing, missing
